@@ -1,0 +1,106 @@
+"""ctypes binding of libfgb200.so (declared in include/fgb200.h).
+
+This is the reference-facing C ABI: plain pointers, sizes and a CUDA stream
+handle. There is no fallback: if the library is missing or fails to load,
+`lib()` raises, and every GPU op in this package fails with it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from ctypes import c_float, c_int, c_size_t, c_uint, c_void_p
+from pathlib import Path
+
+from .build import LIB_PATH
+
+_P = c_void_p
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+FG_OK = 0
+FG_ERR_ARG = 1
+FG_ERR_CUDA = 2
+FG_ERR_TIMEOUT = 3
+FG_ERR_PEER = 4
+
+FG_EPI_STORE = 0
+FG_EPI_RESIDUAL = 1
+FG_EPI_SWIGLU = 2
+
+FG_NORM_LLAMA = 0
+FG_NORM_FP32MUL = 1
+
+# name -> (restype, argtypes); every symbol include/fgb200.h declares
+SIGNATURES: dict[str, tuple] = {
+    "fg_last_error": (ctypes.c_char_p, []),
+    "fg_version": (c_int, []),
+    "fg_device_status": (c_int, [ctypes.POINTER(c_uint), c_int, _P]),
+    "fg_embed": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P]),
+    "fg_rmsnorm": (c_int, [_P, _P, _P, c_int, c_int, c_float, c_int, _P]),
+    "fg_gemm_bf16": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, c_size_t, _P]),
+    "fg_gemm_pick_splits": (c_int, [c_int, c_int, c_int]),
+    "fg_gemm_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "fg_rope_kv_append": (
+        c_int,
+        [_P, _P, _P, c_float, _P, c_int, c_int, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P],
+    ),
+    "fg_kv_append": (
+        c_int, [_P, _P, _P, _P, _P, c_int, c_int, _P, _P, c_int, c_int, c_int, c_int, _P],
+    ),
+    "fg_paged_decode_attn": (
+        c_int,
+        [_P, _P, _P, _P, _P, _P, _P, _P, c_size_t, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+         c_int, c_int, c_float, _P],
+    ),
+    "fg_attn_pages_per_split": (c_int, [c_int, c_int, c_int, c_int]),
+    "fg_attn_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "fg_argmax": (c_int, [_P, _P, c_int, c_int, _P]),
+    "fg_advance": (c_int, [_P, _P, c_int, _P]),
+}
+
+
+def lib_path() -> Path:
+    override = os.environ.get("FGB200_LIB")
+    return Path(override) if override else LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the C library with typed entry points."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = lib_path()
+        if not path.exists():
+            raise RuntimeError(
+                f"fgb200 CUDA library not found at {path}; build it with "
+                "`python -m fluidgpu_b200.build` (nvcc, sm_100a)"
+            )
+        handle = ctypes.CDLL(str(path))
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        _lib = handle
+    return _lib
+
+
+class FgError(RuntimeError):
+    """A C entry point returned a nonzero status."""
+
+    def __init__(self, name: str, code: int, text: str) -> None:
+        super().__init__(f"{name} failed with status {code}: {text}")
+        self.code = code
+
+
+def call(name: str, *args) -> int:
+    """Call `name` and raise FgError on a nonzero status."""
+    handle = lib()
+    rc = getattr(handle, name)(*args)
+    if rc != FG_OK:
+        text = handle.fg_last_error()
+        raise FgError(name, rc, text.decode() if text else "")
+    return rc

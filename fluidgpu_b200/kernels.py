@@ -1,0 +1,214 @@
+"""Torch-facing wrappers over the C ABI (include/fgb200.h).
+
+Each wrapper checks its tensors (CUDA, dtype, contiguity), allocates outputs
+through the torch caching allocator, hands raw pointers and the current
+CUDA stream to libfgb200.so and raises on a nonzero status. The C entry
+points never allocate; scratch space comes from `Workspace`, one buffer per
+(device, stream) so calls that may overlap on the GPU never share one.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from ._lib import call
+
+_BF16 = torch.bfloat16
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _check(t: torch.Tensor, name: str, dtype: torch.dtype | None = None) -> None:
+    assert t.is_cuda, f"{name} must be a CUDA tensor, got {t.device}"
+    assert t.is_contiguous(), f"{name} must be contiguous"
+    if dtype is not None:
+        assert t.dtype == dtype, f"{name} must be {dtype}, got {t.dtype}"
+
+
+class Workspace:
+    """Zero-initialised scratch buffers keyed by (device, stream, slot).
+
+    The GEMM split-K tickets must start at zero; the kernels leave them at
+    zero again, so a buffer is zeroed once, when it is (re)allocated.
+    """
+
+    _bufs: dict[tuple[int, int, str], torch.Tensor] = {}
+
+    @classmethod
+    def get(cls, nbytes: int, device: torch.device, slot: str) -> torch.Tensor | None:
+        if nbytes <= 0:
+            return None
+        key = (device.index or 0, _stream(device), slot)
+        buf = cls._bufs.get(key)
+        if buf is None or buf.numel() < nbytes:
+            size = max(nbytes, 1 << 20)
+            buf = torch.zeros(size + 256, dtype=torch.uint8, device=device)
+            off = (-buf.data_ptr()) % 256
+            buf = buf[off : off + size]
+            cls._bufs[key] = buf
+        return buf
+
+    @classmethod
+    def clear(cls) -> None:
+        cls._bufs.clear()
+
+
+def device_status(reset: bool = True) -> int:
+    """Device status word (0 = no device-side failure). Synchronises."""
+    v = _lib.ctypes.c_uint(0)
+    call("fg_device_status", _lib.ctypes.byref(v), int(reset), _stream())
+    return int(v.value)
+
+
+def check_device(what: str = "fgb200") -> None:
+    st = device_status(reset=True)
+    if st:
+        kind = st & 0xFF
+        site = st >> 8
+        names = {1: "pipeline wait timeout", 2: "peer flag timeout", 3: "index out of range"}
+        raise RuntimeError(f"{what}: device-side failure '{names.get(kind, kind)}' at site {site:#x}")
+
+
+# ---------------------------------------------------------------------------
+# ops
+# ---------------------------------------------------------------------------
+def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(ids, "ids", torch.int64)
+    _check(table, "table", _BF16)
+    T = ids.numel()
+    V, H = table.shape
+    if out is None:
+        out = torch.empty((T, H), dtype=_BF16, device=table.device)
+    call("fg_embed", _ptr(ids), _ptr(table), _ptr(out), T, H, V, _stream(table.device))
+    return out
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, mode: int = _lib.FG_NORM_LLAMA,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(x, "x", _BF16)
+    _check(weight, "weight", _BF16)
+    H = x.shape[-1]
+    T = x.numel() // H
+    if out is None:
+        out = torch.empty_like(x)
+    call("fg_rmsnorm", _ptr(x), _ptr(weight), _ptr(out), T, H, float(eps), mode, _stream(x.device))
+    return out
+
+
+def gemm(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = _lib.FG_EPI_STORE,
+         residual: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+         out: torch.Tensor | None = None, splits: int = 0, slot: str = "gemm") -> torch.Tensor:
+    """acc = x @ w.T on tcgen05 with the given epilogue (see fg_gemm_bf16)."""
+    _check(x, "x", _BF16)
+    _check(w, "w", _BF16)
+    K = x.shape[-1]
+    T = x.numel() // K
+    N, Kw = w.shape
+    assert Kw == K, f"gemm: x has K={K}, w has K={Kw}"
+    n_out = N // 2 if epilogue == _lib.FG_EPI_SWIGLU else N
+    if out is None:
+        out = torch.empty((*x.shape[:-1], n_out), dtype=_BF16, device=x.device)
+    if residual is not None:
+        _check(residual, "residual", _BF16)
+        assert residual.numel() == T * n_out, "residual shape mismatch"
+    if bias is not None:
+        _check(bias, "bias", _BF16)
+    lib = _lib.lib()
+    if splits <= 0:
+        splits = lib.fg_gemm_pick_splits(T, N, K)
+    ws_bytes = lib.fg_gemm_workspace_bytes(T, N, K, splits)
+    ws = Workspace.get(ws_bytes, x.device, slot)
+    call("fg_gemm_bf16", _ptr(x), _ptr(w), _ptr(out), _ptr(residual), _ptr(bias), T, N, K,
+         epilogue, splits, _ptr(ws), ws_bytes, _stream(x.device))
+    return out
+
+
+def rope_kv_append(qkv: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor,
+                   attention_scaling: float, block_table: torch.Tensor, k_cache: torch.Tensor,
+                   v_cache: torch.Tensor, nq: int, nkv: int, hd: int,
+                   q_out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(qkv, "qkv", _BF16)
+    _check(positions, "positions", torch.int32)
+    _check(inv_freq, "inv_freq", torch.float32)
+    _check(block_table, "block_table", torch.int32)
+    _check(k_cache, "k_cache", _BF16)
+    _check(v_cache, "v_cache", _BF16)
+    B = positions.numel()
+    assert qkv.numel() == B * (nq + 2 * nkv) * hd, "qkv shape mismatch"
+    num_blocks, _, block_size, _ = k_cache.shape
+    if q_out is None:
+        q_out = torch.empty((B, nq, hd), dtype=_BF16, device=qkv.device)
+    call("fg_rope_kv_append", _ptr(qkv), _ptr(positions), _ptr(inv_freq), float(attention_scaling),
+         _ptr(block_table), block_table.shape[1], num_blocks, _ptr(q_out), _ptr(k_cache),
+         _ptr(v_cache), B, nq, nkv, hd, block_size, _stream(qkv.device))
+    return q_out
+
+
+def kv_append(k: torch.Tensor, v: torch.Tensor, seq_ids: torch.Tensor, positions: torch.Tensor,
+              block_table: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor) -> None:
+    """Write rotated k / raw v [T, nkv, hd] into their paged slots."""
+    _check(k, "k", _BF16)
+    _check(v, "v", _BF16)
+    _check(seq_ids, "seq_ids", torch.int32)
+    _check(positions, "positions", torch.int32)
+    _check(block_table, "block_table", torch.int32)
+    T, nkv, hd = k.shape
+    num_blocks, nkv2, block_size, hd2 = k_cache.shape
+    assert (nkv2, hd2) == (nkv, hd), "cache heads/head_dim mismatch"
+    call("fg_kv_append", _ptr(k), _ptr(v), _ptr(seq_ids), _ptr(positions), _ptr(block_table),
+         block_table.shape[1], num_blocks, _ptr(k_cache), _ptr(v_cache), T, nkv, hd, block_size,
+         _stream(k.device))
+
+
+def paged_decode_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                      block_table: torch.Tensor, seq_lens: torch.Tensor, max_seq_len: int, *,
+                      window: int = 0, sinks: torch.Tensor | None = None,
+                      scale: float | None = None, out: torch.Tensor | None = None,
+                      slot: str = "attn") -> torch.Tensor:
+    _check(q, "q", _BF16)
+    _check(k_cache, "k_cache", _BF16)
+    _check(v_cache, "v_cache", _BF16)
+    _check(block_table, "block_table", torch.int32)
+    _check(seq_lens, "seq_lens", torch.int32)
+    B, nq, hd = q.shape
+    num_blocks, nkv, block_size, hd2 = k_cache.shape
+    assert hd2 == hd, "head_dim mismatch between q and cache"
+    if sinks is not None:
+        _check(sinks, "sinks", torch.float32)
+    if scale is None:
+        scale = 1.0 / math.sqrt(hd)
+    if out is None:
+        out = torch.empty((B, nq * hd), dtype=_BF16, device=q.device)
+    lib = _lib.lib()
+    ws_bytes = lib.fg_attn_workspace_bytes(B, nq, nkv, hd, max_seq_len, window)
+    ws = Workspace.get(ws_bytes, q.device, slot)
+    call("fg_paged_decode_attn", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(block_table),
+         _ptr(seq_lens), _ptr(sinks), _ptr(out), _ptr(ws), ws_bytes, B, nq, nkv, hd, block_size,
+         num_blocks, block_table.shape[1], int(max_seq_len), int(window), float(scale),
+         _stream(q.device))
+    return out
+
+
+def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(logits, "logits", _BF16)
+    V = logits.shape[-1]
+    T = logits.numel() // V
+    if out is None:
+        out = torch.empty((T,), dtype=torch.int64, device=logits.device)
+    call("fg_argmax", _ptr(logits), _ptr(out), T, V, _stream(logits.device))
+    return out
+
+
+def advance(positions: torch.Tensor | None, seq_lens: torch.Tensor | None) -> None:
+    ref = positions if positions is not None else seq_lens
+    if ref is None:
+        return
+    call("fg_advance", _ptr(positions), _ptr(seq_lens), ref.numel(), _stream(ref.device))

@@ -1,0 +1,187 @@
+"""Paged KV cache with the surface of fluidgpu_torch.kv_cache.LayerKVCache
+(fluidgpu_runtime/fluidgpu_torch/kv_cache.py:21-166): owned, static_mode,
+max_seq_len, update, get_seq_length, get_mask_sizes, advance, reset.
+
+Layout in HBM. Every owned layer has K and V page pools
+  [num_blocks, n_kv, 16, head_dim] bf16
+held in one allocation [n_owned, 2, num_blocks, n_kv, 16, head_dim], so a
+page of one KV head is a contiguous 2-4 KB run (what the attention kernel's
+TMA box fetches). All layers share one block table [max_batch, max_blocks]
+int32: sequence b's page p lives in block block_table[b, p] of every layer.
+Device-side per-sequence counters:
+  positions[b] = tokens already cached = position of the next token
+  seq_lens[b]  = positions[b] + 1       = tokens attended during a step
+Both advance on the device (fg_advance), so a decode step needs no host
+round trip; a host mirror tracks the same counts for planning.
+
+Blocks come from a FIFO free list (lowest id first, freed blocks return to
+the tail), and a sequence reserves the pages for its whole expected length
+up front, so the block table is written only when requests join.
+"""
+from __future__ import annotations
+
+import collections
+from typing import Any
+
+import torch
+
+from . import kernels
+
+BLOCK = 16
+
+
+class BlockAllocator:
+    """FIFO free-list of physical block ids (deterministic)."""
+
+    def __init__(self, num_blocks: int) -> None:
+        self.num_blocks = num_blocks
+        self._free = collections.deque(range(num_blocks))
+
+    @property
+    def num_free(self) -> int:
+        return len(self._free)
+
+    def allocate(self, n: int) -> list[int]:
+        assert n <= len(self._free), f"out of KV blocks: need {n}, have {len(self._free)}"
+        return [self._free.popleft() for _ in range(n)]
+
+    def free(self, blocks: list[int]) -> None:
+        self._free.extend(blocks)
+
+
+class PagedKVCache:
+    def __init__(self, num_layers: int, owned_layer_ids: list[int] | tuple[int, ...],
+                 max_seq_len: int, num_kv_heads: int, head_dim: int, dtype: torch.dtype,
+                 device: torch.device | str, *, max_batch: int = 1,
+                 num_blocks: int | None = None) -> None:
+        assert dtype is torch.bfloat16, "the paged cache holds bf16"
+        self.num_layers = num_layers
+        self.owned = set(owned_layer_ids)
+        self.max_seq_len = max_seq_len
+        self.num_kv_heads = num_kv_heads
+        self.head_dim = head_dim
+        self.dtype = dtype
+        self.device = torch.device(device)
+        self.max_batch = max_batch
+        self.max_blocks = (max_seq_len + BLOCK - 1) // BLOCK
+        self.num_blocks = num_blocks if num_blocks is not None else max_batch * self.max_blocks
+        self.static_mode = False
+        self._slot = {lid: i for i, lid in enumerate(sorted(self.owned))}
+        n_owned = len(self._slot)
+        self.pool = torch.zeros((max(n_owned, 1), 2, self.num_blocks, num_kv_heads, BLOCK, head_dim),
+                                dtype=dtype, device=self.device) if n_owned else None
+        self.block_table = torch.full((max_batch, self.max_blocks), -1, dtype=torch.int32,
+                                      device=self.device)
+        self.positions = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
+        self.seq_lens = torch.ones(max_batch, dtype=torch.int32, device=self.device)
+        self.allocator = BlockAllocator(self.num_blocks)
+        self._blocks: list[list[int]] = [[] for _ in range(max_batch)]
+        self._host_pos = [0] * max_batch
+        self.batch = 0
+
+    # -- layout ----------------------------------------------------------------
+    def layer_pages(self, layer_idx: int) -> tuple[torch.Tensor, torch.Tensor]:
+        assert layer_idx in self.owned, f"layer {layer_idx} not owned by this rank"
+        s = self._slot[layer_idx]
+        return self.pool[s, 0], self.pool[s, 1]
+
+    def host_block_table(self) -> list[list[int]]:
+        return [list(b) for b in self._blocks[: self.batch]]
+
+    # -- request admission -----------------------------------------------------
+    def start_batch(self, lengths: list[int], reserve: list[int] | int) -> None:
+        """Begin a batch of len(lengths) sequences with lengths[b] tokens already
+        cached, reserving pages for reserve[b] total tokens each."""
+        self.reset()
+        B = len(lengths)
+        assert 1 <= B <= self.max_batch, f"batch {B} exceeds max_batch {self.max_batch}"
+        res = [reserve] * B if isinstance(reserve, int) else list(reserve)
+        table = torch.full((self.max_batch, self.max_blocks), -1, dtype=torch.int32)
+        for b in range(B):
+            total = max(res[b], lengths[b] + 1)
+            assert total <= self.max_seq_len, f"exceed max_seq_len: {total} > {self.max_seq_len}"
+            nb = (total + BLOCK - 1) // BLOCK
+            self._blocks[b] = self.allocator.allocate(nb)
+            table[b, :nb] = torch.tensor(self._blocks[b], dtype=torch.int32)
+        self.block_table.copy_(table)
+        pos = torch.zeros(self.max_batch, dtype=torch.int32)
+        pos[:B] = torch.tensor(lengths, dtype=torch.int32)
+        self.positions.copy_(pos)
+        self.seq_lens.copy_(pos + 1)
+        self._host_pos = list(lengths) + [0] * (self.max_batch - B)
+        self.batch = B
+
+    # -- LayerKVCache surface --------------------------------------------------
+    def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
+               cache_kwargs: dict[str, Any] | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """Append key/value states [B, n_kv, S, hd] at each sequence's current
+        position (or cache_kwargs['cache_position'] for batch 1); returns the
+        layer's page pools (read through the block table)."""
+        assert layer_idx in self.owned, f"layer {layer_idx} not owned by this rank"
+        assert key_states.shape == value_states.shape, "key/value shapes must match"
+        B, nkv, S, hd = key_states.shape
+        assert nkv == self.num_kv_heads, f"num_kv_heads mismatch: got {nkv}, expected {self.num_kv_heads}"
+        assert hd == self.head_dim, f"head_dim mismatch: got {hd}, expected {self.head_dim}"
+        if B > self.batch:
+            self.start_batch([0] * B, self.max_seq_len)
+        cp = None if cache_kwargs is None else cache_kwargs.get("cache_position")
+        if cp is not None and B == 1:
+            pos = cp.flatten().to(device=self.device, dtype=torch.int32)
+        else:
+            base = self.positions[:B].to(torch.int32)
+            pos = (base[:, None] + torch.arange(S, device=self.device, dtype=torch.int32)[None, :]).reshape(-1)
+        seq = torch.arange(B, device=self.device, dtype=torch.int32).repeat_interleave(S)
+        k = key_states.permute(0, 2, 1, 3).reshape(B * S, nkv, hd).contiguous()
+        v = value_states.permute(0, 2, 1, 3).reshape(B * S, nkv, hd).contiguous()
+        kp, vp = self.layer_pages(layer_idx)
+        kernels.kv_append(k, v, seq, pos, self.block_table, kp, vp)
+        return kp, vp
+
+    def get_seq_length(self, layer_idx: int = 0) -> int:
+        return max(self._host_pos[: max(self.batch, 1)])
+
+    def seq_lengths(self) -> list[int]:
+        return list(self._host_pos[: self.batch])
+
+    def get_max_length(self) -> int:
+        return self.max_seq_len
+
+    def get_max_cache_shape(self) -> int:
+        return self.max_seq_len
+
+    def get_mask_sizes(self, cache_position: torch.Tensor, layer_idx: int | None = None) -> tuple[int, int]:
+        assert cache_position.numel() > 0, "cache_position must not be empty"
+        if self.static_mode:
+            return self.max_seq_len, 0
+        kv_length = int(cache_position.flatten()[-1].item()) + 1
+        assert kv_length <= self.max_seq_len, f"exceed max_seq_len: {kv_length} > {self.max_seq_len}"
+        return kv_length, 0
+
+    def advance(self, seq_len: int) -> None:
+        assert seq_len > 0, f"seq_len must be positive, got {seq_len}"
+        for b in range(self.batch):
+            nxt = self._host_pos[b] + seq_len
+            assert nxt <= self.max_seq_len, f"exceed max_seq_len: {nxt} > {self.max_seq_len}"
+            assert nxt < len(self._blocks[b]) * BLOCK + 1, "sequence ran past its reserved pages"
+            self._host_pos[b] = nxt
+        for _ in range(seq_len):
+            kernels.advance(self.positions, self.seq_lens)
+
+    def max_attended(self) -> int:
+        """Longest attention span of the coming step (host mirror)."""
+        return max(self._host_pos[: max(self.batch, 1)]) + 1
+
+    def reset(self) -> None:
+        for b in range(self.max_batch):
+            if self._blocks[b]:
+                self.allocator.free(self._blocks[b])
+                self._blocks[b] = []
+        self._host_pos = [0] * self.max_batch
+        self.batch = 0
+        if self.positions.is_cuda:
+            self.positions.zero_()
+            self.seq_lens.fill_(1)
+            self.block_table.fill_(-1)
+
+    def reorder_cache(self, beam_idx: torch.LongTensor) -> None:
+        raise NotImplementedError("beam search is not supported")

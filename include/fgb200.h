@@ -1,0 +1,157 @@
+/*
+ * fgb200.h - C ABI of the B200 (sm_100a) decode-step kernels.
+ *
+ * This is the boundary a host binding (ctypes, cgo, JNI, a C++ runtime)
+ * links against. Signatures hold plain pointers, sizes and a CUDA stream:
+ * no torch or C++ types. Every entry point:
+ *   - returns FG_OK (0) or an FG_ERR_* code; fg_last_error() gives the text;
+ *   - only enqueues work on `stream` (asynchronous, no implicit sync);
+ *   - never allocates device memory: scratch space ("workspace") is passed in
+ *     by the caller, sized by the matching *_workspace_bytes() query.
+ * Device buffers hold bf16 as raw 16-bit patterns (fg_bf16).
+ *
+ * Reference interfaces replaced (paths inside the FluidGPU project):
+ *   fluidgpu_runtime/fluidgpu_torch/runner.py        CausalLMRunner (decode step)
+ *   fluidgpu_runtime/fluidgpu_torch/kv_cache.py      LayerKVCache.update
+ *   fluidgpu_runtime/fluidgpu_torch/comm.py          ProcessGroupComm.send/recv
+ *   cpp_runtime/include/comm_backend.cu              pcie/rdma handlers, polling kernels
+ */
+#ifndef FGB200_H_
+#define FGB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint16_t fg_bf16;          /* bfloat16 bit pattern */
+typedef struct CUstream_st* fg_stream_t; /* == cudaStream_t */
+
+/* status codes (ProcessGroupComm raises AssertionError / RuntimeError in the
+ * reference; a host binding maps these codes onto those exceptions) */
+#define FG_OK 0
+#define FG_ERR_ARG 1     /* bad argument: shape, alignment, null pointer */
+#define FG_ERR_CUDA 2    /* CUDA runtime error while enqueueing */
+#define FG_ERR_TIMEOUT 3 /* a bounded device wait gave up */
+#define FG_ERR_PEER 4    /* peer buffer not mapped / peer access unavailable */
+
+/* GEMM epilogues (fg_gemm_bf16) */
+#define FG_EPI_STORE 0     /* out[t,n] = bf16(acc (+ bias)) */
+#define FG_EPI_RESIDUAL 1  /* out[t,n] = bf16(residual[t,n] + bf16(acc (+ bias))) */
+#define FG_EPI_SWIGLU 2    /* out[t,j] = bf16(silu(g) * u), g/u rows interleaved per 64 */
+
+/* RMSNorm weight application (fg_rmsnorm) */
+#define FG_NORM_LLAMA 0    /* w * bf16(x * rstd)    (LlamaRMSNorm)  */
+#define FG_NORM_FP32MUL 1  /* bf16(w * (x * rstd))  (GptOssRMSNorm) */
+
+/* ---- diagnostics ------------------------------------------------------- */
+
+/* Text of the last host-side error on the calling thread. */
+const char* fg_last_error(void);
+/* ABI version; bumped on any signature change. */
+int fg_version(void);
+/* Copy the device status word of the current device into *status (0 = no
+ * device-side failure since the last reset) and optionally reset it. The low
+ * 8 bits hold the failure kind (1 pipeline wait timeout, 2 peer flag timeout,
+ * 3 index out of range), the rest the failing site. Synchronises `stream`. */
+int fg_device_status(unsigned int* status, int reset, fg_stream_t stream);
+
+/* ---- decode-step kernels ------------------------------------------------ */
+
+/* Embedding gather: out[t,:] = table[ids[t],:].
+ * Replaces executor.run_stage("embed", embed_tokens) in
+ * fluidgpu_torch/runner.py:128-134. Out-of-range ids write zeros and set the
+ * device status (index out of range). */
+int fg_embed(const int64_t* ids, const fg_bf16* table, fg_bf16* out, int T, int H, int vocab,
+             fg_stream_t stream);
+
+/* RMSNorm over rows of x[T,H]: layer.input_layernorm / post_attention_layernorm
+ * / model.norm as called at fluidgpu_torch/runner.py:183, :350 and :168.
+ * weight_mode is FG_NORM_LLAMA or FG_NORM_FP32MUL. */
+int fg_rmsnorm(const fg_bf16* x, const fg_bf16* weight, fg_bf16* out, int T, int H, float eps,
+               int weight_mode, fg_stream_t stream);
+
+/* Dense bf16 GEMM on tcgen05 tensor cores, fp32 accumulation in TMEM:
+ *   acc[t,n] = sum_k x[t,k] * w[n,k]      x:[T,K] row-major, w:[N,K] row-major
+ * with the epilogue `epilogue` (FG_EPI_*). For FG_EPI_SWIGLU, w holds the
+ * gate and up projections interleaved in blocks of 64 rows (gate rows
+ * j..j+63, then up rows j..j+63) and out is [T, N/2].
+ * Replaces the nn.Linear calls q/k/v/o_proj, gate/up/down_proj and lm_head
+ * at fluidgpu_torch/runner.py:273-276, :347, :420, :430, :168.
+ * K must be a multiple of 8 (16-byte rows); x, w 16-byte aligned.
+ * splits = number of K slices (0 = pick automatically); when > 1 the partial
+ * sums go through `workspace` (fg_gemm_workspace_bytes bytes, 256-byte
+ * aligned). Its first 64 KiB hold split-K tickets: zero them once before the
+ * first call; every call leaves them zero again, so one workspace serves
+ * calls of any shape in stream order. Calls that overlap on the GPU must not
+ * share a workspace. */
+int fg_gemm_bf16(const fg_bf16* x, const fg_bf16* w, fg_bf16* out, const fg_bf16* residual,
+                 const fg_bf16* bias, int T, int N, int K, int epilogue, int splits,
+                 void* workspace, size_t workspace_bytes, fg_stream_t stream);
+/* Split count fg_gemm_bf16 uses for splits == 0. */
+int fg_gemm_pick_splits(int T, int N, int K);
+/* Workspace bytes fg_gemm_bf16 needs for (T, N, K, splits). 0 if none. */
+size_t fg_gemm_workspace_bytes(int T, int N, int K, int splits);
+
+/* RoPE + paged KV append for one decode token per sequence.
+ * qkv:[B, (nq+2*nkv)*hd] (q heads, then k heads, then v heads; bf16)
+ * positions:[B] int32 = index of the new token in its sequence
+ * cos/sin are computed from inv_freq:[hd/2] fp32 and attention_scaling,
+ * rounded to bf16 as the HF rotary embedding does; rotation uses the
+ * rotate-half convention (apply_rotary_pos_emb).
+ * Writes q_out:[B, nq, hd] and the roped k / raw v of token b into
+ * k_cache/v_cache:[num_blocks, nkv, block_size, hd] at block
+ * block_table[b*max_blocks + pos/block_size], offset pos%block_size.
+ * Replaces q/k/v split + apply_rotary_pos_emb + LayerKVCache.update
+ * (fluidgpu_torch/runner.py:268-293, kv_cache.py:73-113). */
+int fg_rope_kv_append(const fg_bf16* qkv, const int32_t* positions, const float* inv_freq,
+                      float attention_scaling, const int32_t* block_table, int max_blocks,
+                      int num_blocks, fg_bf16* q_out, fg_bf16* k_cache, fg_bf16* v_cache, int B,
+                      int nq, int nkv, int hd, int block_size, fg_stream_t stream);
+
+/* Paged KV append of already-rotated keys: token t (k,v:[T, nkv, hd]) of
+ * sequence seq_ids[t] at position positions[t] goes to its page slot. The
+ * LayerKVCache.update surface (fluidgpu_torch/kv_cache.py:73-113) on the
+ * paged layout; used where RoPE ran elsewhere (prefill, foreign callers). */
+int fg_kv_append(const fg_bf16* k, const fg_bf16* v, const int32_t* seq_ids,
+                 const int32_t* positions, const int32_t* block_table, int max_blocks,
+                 int num_blocks, fg_bf16* k_cache, fg_bf16* v_cache, int T, int nkv, int hd,
+                 int block_size, fg_stream_t stream);
+
+/* Paged GQA decode attention, one query token per sequence.
+ * q:[B, nq, hd]; k_cache/v_cache:[num_blocks, nkv, block_size, hd];
+ * block_table:[B, max_blocks] int32; seq_lens:[B] int32 (tokens to attend,
+ * including the new one). window > 0 keeps only the last `window` tokens
+ * (transformers' sliding-window mask: kv > q - window). sinks:[nq] fp32 or
+ * NULL adds exp(sink) to each head's softmax denominator (gpt-oss s_aux).
+ * out:[B, nq*hd] bf16. Split-K over pages; partials live in `workspace`
+ * (fg_attn_workspace_bytes). Requires hd in {64,128}, block_size == 16.
+ * Replaces eager_attention_forward / SDPA over LayerKVCache
+ * (fluidgpu_torch/runner.py:299-335, masks :713-823, sinks :914-920). */
+int fg_paged_decode_attn(const fg_bf16* q, const fg_bf16* k_cache, const fg_bf16* v_cache,
+                         const int32_t* block_table, const int32_t* seq_lens, const float* sinks,
+                         fg_bf16* out, void* workspace, size_t workspace_bytes, int B, int nq,
+                         int nkv, int hd, int block_size, int num_blocks, int max_blocks,
+                         int max_seq_len, int window, float scale, fg_stream_t stream);
+/* Pages per split fg_paged_decode_attn uses for a batch of B sequences of at
+ * most max_seq_len tokens (window as in fg_paged_decode_attn). */
+int fg_attn_pages_per_split(int B, int nkv, int max_seq_len, int window);
+/* Workspace bytes fg_paged_decode_attn needs for these sizes (0 if none). */
+size_t fg_attn_workspace_bytes(int B, int nq, int nkv, int hd, int max_seq_len, int window);
+
+/* Greedy token: out[t] = argmax_v logits[t, v] (lowest index on ties), the
+ * argmax the reference engine takes after norm_lm_head (engine.py:295-300,
+ * :337-343). */
+int fg_argmax(const fg_bf16* logits, int64_t* out, int T, int V, fg_stream_t stream);
+
+/* positions[b] += 1 and seq_lens[b] += 1 after a decode step
+ * (LayerKVCache.advance, kv_cache.py:140-144). Either pointer may be NULL. */
+int fg_advance(int32_t* positions, int32_t* seq_lens, int B, fg_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FGB200_H_ */

@@ -1,0 +1,251 @@
+"""Per-kernel parity on the GPU: each C-ABI entry point against the CPU oracle
+(oracle/decode_ref.py) or a plain fp32 torch reference, on seeded inputs."""
+import math
+
+import pytest
+import torch
+
+from oracle import decode_ref as ref
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    from fluidgpu_b200 import build
+
+    build.build()
+    yield
+    from fluidgpu_b200 import kernels
+
+    kernels.check_device("kernel tests")
+
+
+def _gen(seed):
+    g = torch.Generator().manual_seed(seed)
+    return g
+
+
+def _randn(shape, g, scale=1.0, dtype=torch.bfloat16):
+    return (torch.randn(shape, generator=g) * scale).to(dtype)
+
+
+# ---------------------------------------------------------------------------
+def test_embed_and_bad_index():
+    from fluidgpu_b200 import kernels
+
+    g = _gen(0)
+    table = _randn((1000, 256), g)
+    ids = torch.randint(0, 1000, (37,), generator=g)
+    out = kernels.embed(ids.to(DEV), table.to(DEV))
+    assert torch.equal(out.cpu(), table[ids])
+    kernels.check_device("embed")
+    bad = torch.tensor([5, 1000, -1], dtype=torch.int64)
+    out = kernels.embed(bad.to(DEV), table.to(DEV)).cpu()
+    assert torch.equal(out[0], table[5]) and out[1:].abs().sum() == 0
+    assert kernels.device_status(reset=True) & 0xFF == 3
+
+
+@pytest.mark.parametrize("H,T", [(1024, 8), (4096, 64), (2880, 5), (64, 1)])
+@pytest.mark.parametrize("fp32mul", [False, True])
+def test_rmsnorm(H, T, fp32mul):
+    from fluidgpu_b200 import kernels
+
+    g = _gen(1)
+    x = _randn((T, H), g)
+    w = _randn((H,), g, 0.5) + 1.0
+    mode = 1 if fp32mul else 0
+    out = kernels.rmsnorm(x.to(DEV), w.to(DEV).to(torch.bfloat16), 1e-5, mode).cpu()
+    exp = ref.rms_norm(x, w.to(torch.bfloat16), 1e-5, fp32mul)
+    diff = (out.float() - exp.float()).abs()
+    # identical up to one bf16 ulp from the fp32 reduction order
+    assert (diff <= exp.float().abs() * 2 ** -7 + 1e-6).all()
+    assert (diff == 0).float().mean() > 0.9
+
+
+def _gemm_ref(x, w, bias=None):
+    y = x.float() @ w.float().T
+    if bias is not None:
+        y = y + bias.float()
+    return y
+
+
+@pytest.mark.parametrize(
+    "T,N,K,splits",
+    [
+        (1, 128, 64, 1),
+        (8, 256, 1024, 0),
+        (13, 384, 640, 2),
+        (64, 6144, 4096, 0),
+        (64, 4096, 4096, 0),
+        (33, 2880, 2880, 0),     # N not a multiple of 128
+        (100, 512, 1024, 3),
+        (256, 1024, 512, 1),
+        (300, 640, 256, 0),      # two token tiles
+        (64, 1000, 200, 0),      # K tail inside one 64-wide stage
+    ],
+)
+def test_gemm_store(T, N, K, splits):
+    from fluidgpu_b200 import kernels
+
+    g = _gen(2)
+    x = _randn((T, K), g)
+    w = _randn((N, K), g, 0.05)
+    out = kernels.gemm(x.to(DEV), w.to(DEV), splits=splits).cpu()
+    exp = _gemm_ref(x, w)
+    err = (out.float() - exp).abs().max().item()
+    assert err <= 1e-2 * exp.abs().max().item() + 1e-3, err
+
+
+def test_gemm_bias_residual():
+    from fluidgpu_b200 import kernels
+
+    g = _gen(3)
+    T, N, K = 64, 4096, 4096
+    x = _randn((T, K), g)
+    w = _randn((N, K), g, 0.02)
+    b = _randn((N,), g, 0.1)
+    r = _randn((T, N), g)
+    for splits in (1, 4):
+        out = kernels.gemm(x.to(DEV), w.to(DEV), epilogue=1, residual=r.to(DEV), bias=b.to(DEV),
+                           splits=splits).cpu()
+        exp = r.float() + _gemm_ref(x, w, b).to(torch.bfloat16).float()
+        err = (out.float() - exp).abs().max().item()
+        assert err <= 2e-2 * exp.abs().max().item(), (splits, err)
+
+
+@pytest.mark.parametrize("T,I,K,splits", [(64, 14336, 4096, 0), (8, 2816, 1024, 0), (5, 128, 64, 1),
+                                           (64, 512, 4096, 4)])
+def test_gemm_swiglu(T, I, K, splits):
+    from fluidgpu_b200 import kernels
+
+    g = _gen(4)
+    x = _randn((T, K), g)
+    wg = _randn((I, K), g, 0.02)
+    wu = _randn((I, K), g, 0.02)
+    # gate/up interleaved in blocks of 64 rows
+    w = torch.stack([wg.view(I // 64, 64, K), wu.view(I // 64, 64, K)], dim=1).reshape(2 * I, K)
+    out = kernels.gemm(x.to(DEV), w.to(DEV), epilogue=2, splits=splits).cpu()
+    gate = _gemm_ref(x, wg).to(torch.bfloat16)
+    up = _gemm_ref(x, wu).to(torch.bfloat16)
+    exp = ref.silu_mul(gate, up).float()
+    err = (out.float() - exp).abs().max().item()
+    assert err <= 2e-2 * exp.abs().max().item() + 1e-4, err
+
+
+# ---------------------------------------------------------------------------
+def _paged_setup(B, nkv, hd, lens, num_blocks, g):
+    max_blocks = max((l + 15) // 16 for l in lens)
+    perm = torch.randperm(num_blocks, generator=g)
+    table = torch.full((B, max_blocks), -1, dtype=torch.int32)
+    used = 0
+    for b, l in enumerate(lens):
+        nb = (l + 15) // 16
+        table[b, :nb] = perm[used : used + nb].to(torch.int32)
+        used += nb
+    assert used <= num_blocks
+    kc = _randn((num_blocks, nkv, 16, hd), g)
+    vc = _randn((num_blocks, nkv, 16, hd), g)
+    return table, kc, vc
+
+
+def _gather(cache, table, b, L):
+    nb = (L + 15) // 16
+    pages = cache[table[b, :nb].long()]  # [nb, nkv, 16, hd]
+    return pages.permute(0, 2, 1, 3).reshape(nb * 16, pages.shape[1], pages.shape[3])[:L]
+
+
+@pytest.mark.parametrize(
+    "B,nq,nkv,hd,lens,window,sinks",
+    [
+        (3, 32, 8, 128, [1, 17, 300], 0, False),
+        (4, 16, 4, 64, [16, 33, 250, 5], 0, False),
+        (2, 64, 8, 64, [300, 129], 128, True),
+        (2, 64, 8, 64, [1000, 7], 0, True),
+        (5, 32, 8, 128, [4096, 4000, 2048, 17, 4097], 0, False),
+        (1, 32, 8, 128, [32768], 0, False),
+        (8, 4, 2, 64, [20, 21, 22, 23, 24, 25, 26, 27], 2, False),
+    ],
+)
+def test_paged_attention(B, nq, nkv, hd, lens, window, sinks):
+    from fluidgpu_b200 import kernels
+
+    g = _gen(5)
+    num_blocks = sum((l + 15) // 16 for l in lens) + 7
+    table, kc, vc = _paged_setup(B, nkv, hd, lens, num_blocks, g)
+    q = _randn((B, nq, hd), g)
+    sk = (torch.randn(nq, generator=g) * 2.0) if sinks else None
+    seq = torch.tensor(lens, dtype=torch.int32)
+    out = kernels.paged_decode_attn(
+        q.to(DEV), kc.to(DEV), vc.to(DEV), table.to(DEV), seq.to(DEV), max(lens), window=window,
+        sinks=None if sk is None else sk.to(DEV),
+    ).cpu()
+    scale = 1.0 / math.sqrt(hd)
+    for b, L in enumerate(lens):
+        k = _gather(kc, table, b, L)
+        v = _gather(vc, table, b, L)
+        exp = ref.attention_one(q[b], k, v, scale, window, sk).reshape(-1)
+        err = (out[b].float() - exp).abs().max().item()
+        assert err <= 2e-2, (b, L, err)
+
+
+def test_rope_kv_append():
+    from fluidgpu_b200 import kernels
+
+    g = _gen(6)
+    B, nq, nkv, hd = 4, 8, 2, 128
+    num_blocks = 16
+    positions = torch.tensor([0, 15, 16, 40], dtype=torch.int32)
+    table = torch.randperm(num_blocks, generator=g)[: B * 4].view(B, 4).to(torch.int32)
+    qkv = _randn((B, (nq + 2 * nkv) * hd), g)
+    inv_freq = ref.default_inv_freq(hd, 500000.0)
+    kc = torch.zeros((num_blocks, nkv, 16, hd), dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    kcd, vcd = kc.to(DEV), vc.to(DEV)
+    q = kernels.rope_kv_append(qkv.to(DEV), positions.to(DEV), inv_freq.to(DEV), 1.0,
+                               table.to(DEV), kcd, vcd, nq, nkv, hd).cpu()
+    cos, sin = ref.rope_cos_sin(positions.long(), inv_freq, 1.0, torch.bfloat16)
+    x = qkv.view(B, nq + 2 * nkv, hd)
+    eq = ref.apply_rope(x[:, :nq], cos, sin)
+    ek = ref.apply_rope(x[:, nq : nq + nkv], cos, sin)
+    ev = x[:, nq + nkv :]
+    assert (q.float() - eq.float()).abs().max() <= 2 ** -6 * eq.float().abs().max()
+    kcd, vcd = kcd.cpu(), vcd.cpu()
+    written = torch.zeros(num_blocks, 16, dtype=torch.bool)
+    for b in range(B):
+        p = int(positions[b])
+        blk = int(table[b, p // 16])
+        written[blk, p % 16] = True
+        assert (kcd[blk, :, p % 16].float() - ek[b].float()).abs().max() <= 2 ** -6 * ek.float().abs().max()
+        assert torch.equal(vcd[blk, :, p % 16], ev[b])
+    # nothing else touched
+    assert kcd.permute(0, 2, 1, 3)[~written].abs().sum() == 0
+    assert vcd.permute(0, 2, 1, 3)[~written].abs().sum() == 0
+
+
+def test_argmax_ties_lowest_index():
+    from fluidgpu_b200 import kernels
+
+    g = _gen(7)
+    T, V = 6, 128256
+    logits = _randn((T, V), g)
+    logits[1, 100] = 50.0
+    logits[1, 7] = 50.0
+    logits[2, V - 1] = 60.0
+    logits[3, :] = 1.0
+    out = kernels.argmax(logits.to(DEV)).cpu()
+    exp = ref.argmax_lowest(logits.float())
+    assert torch.equal(out, exp)
+    assert out[1] == 7 and out[2] == V - 1 and out[3] == 0
+
+
+def test_advance():
+    from fluidgpu_b200 import kernels
+
+    pos = torch.arange(5, dtype=torch.int32, device=DEV)
+    lens = pos + 1
+    kernels.advance(pos, lens)
+    assert pos.cpu().tolist() == [1, 2, 3, 4, 5]
+    assert lens.cpu().tolist() == [2, 3, 4, 5, 6]
