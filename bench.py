@@ -1,0 +1,314 @@
+#!/usr/bin/env python
+"""Decode-step benchmark (Llama-3-8B architecture, batch 64, context 4096,
+paged KV, bf16) on B200.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fgb200|reference]
+
+One "step" = one greedy decode step of the whole model for the batch: every
+sequence appends one token (embed -> 32 x (attention, SwiGLU FFN) -> norm ->
+lm_head -> argmax). Weights are random N(0, 0.02) bf16 from a seed, the KV
+cache is filled with synthetic N(0,1) values for the 4096-token prompts
+(the timed work does not depend on the values), and the KV pool (~35 GB)
+and weights (~16 GB) are far larger than L2, so no flush is needed.
+
+value : tokens/s over all ranks, inputs resident in HBM, device-timed.
+e2e   : tokens/s through DecodeEngine.step (host tokens in pinned memory,
+        H2D copy + step + argmax + D2H read per step), device-timed.
+Under torchrun (N > 1) every rank decodes its own batch of 64 requests
+(attention data-parallel by request, co-located FFN: weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tokens/s"
+CONFIG = {"workload": "llama-3-8b decode step, batch 64, prompt 4096, paged KV block 16 (BASELINE configs[1])",
+          "model": "llama-3-8b (random init)", "batch_per_gpu": 64, "context": 4096,
+          "block_size": 16, "l2": "inputs larger than L2 (KV ~35 GB, weights ~16 GB per GPU)"}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            pass
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi SM clock / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(f"/tmp/fgb200_clocks_{os.getpid()}.csv")
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        try:
+            self.path.unlink()
+        except Exception:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def attn_bytes(meta: dict, lens_sum: int) -> float:
+    """Algorithmic HBM bytes of one paged attention launch: K and V of every
+    attended token + Q + O (bf16)."""
+    B, nq, nkv, hd = meta["B"], meta["nq"], meta["nkv"], meta["hd"]
+    return 2.0 * nkv * hd * 2 * lens_sum + 2.0 * B * nq * hd * 2
+
+
+def cpu_baseline_sample(batch: int, context: int) -> dict:
+    from oracle.cpu_baseline import LayerSample, host_threads, time_sample
+    from fluidgpu_b200.model import LLAMA3_8B as S
+
+    threads = host_threads()
+    torch.set_num_threads(threads)
+    sample = LayerSample(S.hidden, S.n_q, S.n_kv, S.head_dim, S.intermediate, S.vocab, S.rope_theta,
+                         batch, context)
+    sample.layer()  # warm-up
+    r = time_sample(sample, S.num_layers, reps=2)
+    return {"value": r["tokens_per_s"], "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": (f"oracle (CPU restatement, fp32) of 1 Llama-3-8B decoder layer + norm/lm_head/argmax"
+                       f" at batch {batch}, context {context}; step = 32 x {r['t_layer_s']:.3f} s"
+                       f" + {r['t_head_s']:.3f} s")}
+
+
+def run_reference(args) -> None:
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    from oracle.cpu_baseline import LayerSample, host_threads, time_sample
+    from fluidgpu_b200.model import LLAMA3_8B as S
+
+    threads = host_threads()
+    torch.set_num_threads(threads)
+    sample = LayerSample(S.hidden, S.n_q, S.n_kv, S.head_dim, S.intermediate, S.vocab, S.rope_theta,
+                         64, 4096)
+    with torch.inference_mode():
+        for _ in range(max(args.warmup, 0)):
+            sample.layer()
+    steps = []
+    for _ in range(args.steps):
+        r = time_sample(sample, S.num_layers, reps=1)
+        steps.append(r["step_s"])
+    step_s = statistics.mean(steps)
+    value = 64 / step_s
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": CONFIG,
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": "each step: 1 Llama-3-8B decoder layer + norm/lm_head/argmax at "
+                                   "batch 64, context 4096 on the host cores (the reference's CPU "
+                                   "algorithm restated in oracle/), scaled to 32 layers"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_fgb200(args) -> None:
+    world, rank, local = dist_env()
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+
+    from fluidgpu_b200 import build, kernels
+    from fluidgpu_b200.config import EngineConfig
+    from fluidgpu_b200.engine import DecodeEngine
+    from fluidgpu_b200.model import LLAMA3_8B, ModelWeights
+
+    build.build()
+    spec = LLAMA3_8B
+    B, ctx = args.batch, args.context
+    W, K = args.warmup, args.steps
+    total = ctx + W + 2 * K + 8
+    cfg = EngineConfig(model_name=spec.name, max_seq_len=total, world_size=1, device=f"cuda:{local}",
+                       max_batch=B)
+    weights = ModelWeights.random(spec, seed=0, device=dev)
+    eng = DecodeEngine(weights, cfg)
+    eng.start(B, prompt_lens=[ctx] * B, reserve_tokens=total)
+    g = torch.Generator(device=dev).manual_seed(1 + rank)
+    eng.kv_cache.pool.normal_(0.0, 1.0, generator=g)
+    tok = torch.randint(0, spec.vocab, (B,), generator=g, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- warm-up (untimed) ----
+    for _ in range(W):
+        tok = eng.step_device(tok)
+    torch.cuda.synchronize()
+    kernels.check_device("bench warm-up")
+
+    # ---- timed: device-resident inputs ----
+    lens0 = eng.kv_cache.seq_lengths()
+    kernels.KernelTimer.enable("attn")
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    n0 = kernels.launch_count()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        tok = eng.step_device(tok)
+    e1.record()
+    torch.cuda.synchronize()
+    n1 = kernels.launch_count()
+    barrier()
+    clocks = sampler.stop()
+    kernels.KernelTimer.disable()
+    ms = e0.elapsed_time(e1)
+    kernels.check_device("bench timed region")
+
+    # dominant kernel: paged attention, one launch per layer per step
+    attn = kernels.KernelTimer.durations_ms("attn")
+    tot_bytes, tot_ms = 0.0, 0.0
+    for i, (d, meta) in enumerate(attn):
+        step = i // spec.num_layers
+        lens_sum = sum(l + 1 + step for l in lens0[:B])
+        tot_bytes += attn_bytes(meta, lens_sum)
+        tot_ms += d
+    attn_launch_ms = tot_ms / max(len(attn), 1)
+    attn_launch_bytes = tot_bytes / max(len(attn), 1)
+
+    # ---- e2e through the public API: host tokens in, host tokens out ----
+    host_tok = tok.cpu().pin_memory()
+    torch.cuda.synchronize()
+    barrier()
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(K):
+        host_tok = eng.step(host_tok)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = f0.elapsed_time(f1)
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+
+    if rank == 0:
+        peaks = measured_peaks()
+        hbm = peaks.get("hbm_gbs")
+        peak_src = "measured" if hbm else "fallback"
+        hbm = hbm or 6650.0
+        achieved = attn_launch_bytes / (attn_launch_ms * 1e-3) / 1e9
+        traffic = None
+        tp = ROOT / "profiles" / "attn_traffic.json"
+        if tp.exists():
+            try:
+                tj = json.loads(tp.read_text())
+                # ncu dram bytes per token attended, scaled to this launch's tokens
+                traffic = tj["dram_bytes_per_kv_token"] * (attn_launch_bytes / (2 * spec.n_kv * spec.head_dim * 2))
+            except Exception:
+                traffic = None
+        value = world * B * K / (ms * 1e-3)
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {**CONFIG, "parallelism": f"dp{world} (attention data-parallel by request, FFN co-located)"},
+            "e2e": {"value": world * B * K / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8},
+            "roofline": {"bound": "hbm", "kernel": "fg_paged_decode_attn", "achieved": achieved,
+                         "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "peak_source": f"{peak_src} (hbm_gbs)", "traffic": traffic,
+                         "algorithmic_bytes_per_launch": attn_launch_bytes,
+                         "launch_ms": attn_launch_ms, "launches": len(attn)},
+            "gpu_launches": int(n1 - n0),
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_sample(B, ctx)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="fgb200", choices=["fgb200", "reference"])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--context", type=int, default=4096)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    assert args.warmup >= 0 and args.steps > 0
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_fgb200(args)
+
+
+if __name__ == "__main__":
+    main()

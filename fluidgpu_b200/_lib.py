@@ -35,6 +35,7 @@ FG_NORM_FP32MUL = 1
 SIGNATURES: dict[str, tuple] = {
     "fg_last_error": (ctypes.c_char_p, []),
     "fg_version": (c_int, []),
+    "fg_launch_count": (ctypes.c_ulonglong, []),
     "fg_device_status": (c_int, [ctypes.POINTER(c_uint), c_int, _P]),
     "fg_embed": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P]),
     "fg_rmsnorm": (c_int, [_P, _P, _P, c_int, c_int, c_float, c_int, _P]),

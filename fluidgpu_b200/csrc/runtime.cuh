@@ -2,6 +2,7 @@
 // status word, tensor-map encoding and SM count.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -20,7 +21,10 @@ void set_last_error(const char* fmt, ...) {
   va_end(ap);
 }
 
+static std::atomic<unsigned long long> g_launches{0};
+
 int check_launch(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_last_error("%s: %s", what, cudaGetErrorString(e));
@@ -93,6 +97,8 @@ extern "C" {
 const char* fg_last_error(void) { return fg::t_last_error; }
 
 int fg_version(void) { return 1; }
+
+unsigned long long fg_launch_count(void) { return fg::g_launches.load(std::memory_order_relaxed); }
 
 int fg_device_status(unsigned int* status, int reset, fg_stream_t stream) {
   FG_REQUIRE(status != nullptr, "fg_device_status: null status pointer");

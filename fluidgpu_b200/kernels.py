@@ -33,6 +33,44 @@ def _check(t: torch.Tensor, name: str, dtype: torch.dtype | None = None) -> None
         assert t.dtype == dtype, f"{name} must be {dtype}, got {t.dtype}"
 
 
+class KernelTimer:
+    """CUDA-event brackets around selected entry points, on the launching
+    stream. Off unless a name is enabled; bench.py turns on the dominant
+    kernel inside its timed region to measure that kernel's live duration."""
+
+    enabled: set[str] = set()
+    events: dict[str, list[tuple[torch.cuda.Event, torch.cuda.Event, dict]]] = {}
+
+    @classmethod
+    def enable(cls, *names: str) -> None:
+        cls.enabled = set(names)
+        cls.events = {n: [] for n in names}
+
+    @classmethod
+    def disable(cls) -> None:
+        cls.enabled = set()
+
+    @classmethod
+    def start(cls, name: str):
+        if name not in cls.enabled:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        return ev
+
+    @classmethod
+    def stop(cls, name: str, ev0, **meta) -> None:
+        if ev0 is None:
+            return
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev1.record()
+        cls.events[name].append((ev0, ev1, meta))
+
+    @classmethod
+    def durations_ms(cls, name: str) -> list[tuple[float, dict]]:
+        return [(a.elapsed_time(b), m) for a, b, m in cls.events.get(name, [])]
+
+
 class Workspace:
     """Zero-initialised scratch buffers keyed by (device, stream, slot).
 
@@ -59,6 +97,11 @@ class Workspace:
     @classmethod
     def clear(cls) -> None:
         cls._bufs.clear()
+
+
+def launch_count() -> int:
+    """Kernels libfgb200.so has launched in this process."""
+    return int(_lib.lib().fg_launch_count())
 
 
 def device_status(reset: bool = True) -> int:
@@ -126,8 +169,10 @@ def gemm(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = _lib.FG_EPI_STORE,
         splits = lib.fg_gemm_pick_splits(T, N, K)
     ws_bytes = lib.fg_gemm_workspace_bytes(T, N, K, splits)
     ws = Workspace.get(ws_bytes, x.device, slot)
+    ev = KernelTimer.start("gemm")
     call("fg_gemm_bf16", _ptr(x), _ptr(w), _ptr(out), _ptr(residual), _ptr(bias), T, N, K,
          epilogue, splits, _ptr(ws), ws_bytes, _stream(x.device))
+    KernelTimer.stop("gemm", ev, T=T, N=N, K=K)
     return out
 
 
@@ -190,10 +235,13 @@ def paged_decode_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
     lib = _lib.lib()
     ws_bytes = lib.fg_attn_workspace_bytes(B, nq, nkv, hd, max_seq_len, window)
     ws = Workspace.get(ws_bytes, q.device, slot)
+    ev = KernelTimer.start("attn")
     call("fg_paged_decode_attn", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(block_table),
          _ptr(seq_lens), _ptr(sinks), _ptr(out), _ptr(ws), ws_bytes, B, nq, nkv, hd, block_size,
          num_blocks, block_table.shape[1], int(max_seq_len), int(window), float(scale),
          _stream(q.device))
+    KernelTimer.stop("attn", ev, B=B, nq=nq, nkv=nkv, hd=hd, window=int(window),
+                     max_seq_len=int(max_seq_len))
     return out
 
 

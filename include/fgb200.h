@@ -52,6 +52,9 @@ typedef struct CUstream_st* fg_stream_t; /* == cudaStream_t */
 const char* fg_last_error(void);
 /* ABI version; bumped on any signature change. */
 int fg_version(void);
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads): lets a caller count the device work of a region. */
+unsigned long long fg_launch_count(void);
 /* Copy the device status word of the current device into *status (0 = no
  * device-side failure since the last reset) and optionally reset it. The low
  * 8 bits hold the failure kind (1 pipeline wait timeout, 2 peer flag timeout,

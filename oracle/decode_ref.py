@@ -357,3 +357,57 @@ class OracleModel:
             toks.append(nxt)
             logits = self.step(nxt)
         return torch.stack(toks, dim=1), all_logits
+
+
+# ---------------------------------------------------------------------------
+# weights straight from a transformers model (the reference runs HF modules)
+# ---------------------------------------------------------------------------
+def spec_from_hf(cfg) -> OracleSpec:
+    gpt = cfg.model_type == "gpt_oss"
+    hd = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+    params = getattr(cfg, "rope_parameters", None) or {}
+    kind = params.get("rope_type", "default")
+    windows = []
+    if gpt:
+        windows = [int(cfg.sliding_window) if t == "sliding_attention" else 0 for t in cfg.layer_types]
+    return OracleSpec(
+        num_layers=cfg.num_hidden_layers, hidden=cfg.hidden_size, n_q=cfg.num_attention_heads,
+        n_kv=cfg.num_key_value_heads, head_dim=hd, intermediate=cfg.intermediate_size,
+        vocab=cfg.vocab_size, rope_theta=float(params.get("rope_theta", getattr(cfg, "rope_theta", 10000.0))),
+        eps=float(cfg.rms_norm_eps), moe=gpt, num_experts=int(getattr(cfg, "num_local_experts", 0) or 0),
+        top_k=int(getattr(cfg, "num_experts_per_tok", 0) or 0) if gpt else 0,
+        attn_bias=bool(getattr(cfg, "attention_bias", False)), sinks=gpt, layer_windows=windows,
+        rope_yarn=dict(params) if kind == "yarn" else None, fp32_weight_mul=gpt)
+
+
+def weights_from_hf(model) -> dict[str, torch.Tensor]:
+    m = model.model
+    w: dict[str, torch.Tensor] = {"embed": m.embed_tokens.weight.detach(),
+                                  "final_norm": m.norm.weight.detach(),
+                                  "lm_head": model.lm_head.weight.detach()}
+    for i, layer in enumerate(m.layers):
+        a = layer.self_attn
+        w[f"{i}.ln1"] = layer.input_layernorm.weight.detach()
+        w[f"{i}.ln2"] = layer.post_attention_layernorm.weight.detach()
+        for n in ("q", "k", "v", "o"):
+            w[f"{i}.w{n}"] = getattr(a, f"{n}_proj").weight.detach()
+            b = getattr(a, f"{n}_proj").bias
+            if b is not None:
+                w[f"{i}.b{n}"] = b.detach()
+        if hasattr(a, "sinks"):
+            w[f"{i}.sinks"] = a.sinks.detach()
+        mlp = layer.mlp
+        if hasattr(mlp, "router"):
+            w[f"{i}.router_w"] = mlp.router.weight.detach()
+            w[f"{i}.router_b"] = mlp.router.bias.detach()
+            ex = mlp.experts
+            # HF keeps [E, H, 2I] / [E, I, H] (x @ W); the oracle uses [out, in]
+            w[f"{i}.w_gate_up"] = ex.gate_up_proj.detach().transpose(1, 2).contiguous()
+            w[f"{i}.b_gate_up"] = ex.gate_up_proj_bias.detach()
+            w[f"{i}.w_down"] = ex.down_proj.detach().transpose(1, 2).contiguous()
+            w[f"{i}.b_down"] = ex.down_proj_bias.detach()
+        else:
+            w[f"{i}.wg"] = mlp.gate_proj.weight.detach()
+            w[f"{i}.wu"] = mlp.up_proj.weight.detach()
+            w[f"{i}.wd"] = mlp.down_proj.weight.detach()
+    return w
