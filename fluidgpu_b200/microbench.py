@@ -1,0 +1,139 @@
+"""Kernel microbenchmarks (benchmark config 5 and per-kernel roofline checks).
+
+  python -m fluidgpu_b200.microbench attn  [--batch B] [--context L] [--window W]
+  python -m fluidgpu_b200.microbench gemm  [--T T] [--N N] [--K K] [--epilogue store|residual|swiglu]
+  python -m fluidgpu_b200.microbench sweep-attn      # B in {1,32,256} x ctx in {512,4096,32768}
+
+Each prints one JSON line per case: device time per launch (CUDA events,
+median of --iters after --warmup), algorithmic bytes and GB/s, and the
+fraction of the measured HBM peak (MEASURED_PEAKS.json when present).
+Inputs are seeded N(0,1) (attention) / N(0,0.02) (weights); the KV pool of
+each case is sized to the case, so small cases stay small under a profiler.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import statistics
+from pathlib import Path
+
+import torch
+
+from . import _lib, build, kernels
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _peak_hbm() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def _time(fn, iters: int, warmup: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    return statistics.median(ts)
+
+
+def bench_attn(B: int, ctx: int, nq: int = 32, nkv: int = 8, hd: int = 128, window: int = 0,
+               iters: int = 20, warmup: int = 5, seed: int = 1) -> dict:
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    pages = (ctx + 15) // 16
+    num_blocks = B * pages
+    kc = torch.empty((num_blocks, nkv, 16, hd), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
+    vc = torch.empty_like(kc).normal_(generator=g)
+    perm = torch.randperm(num_blocks, generator=g, device="cuda").to(torch.int32)
+    table = perm.view(B, pages).contiguous()
+    q = torch.empty((B, nq, hd), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
+    lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+    out = torch.empty((B, nq * hd), dtype=torch.bfloat16, device="cuda")
+    fn = lambda: kernels.paged_decode_attn(q, kc, vc, table, lens, ctx, window=window, out=out)  # noqa: E731
+    ms = _time(fn, iters, warmup)
+    eff = min(ctx, window) if window else ctx
+    nbytes = 2.0 * B * nkv * hd * 2 * eff + 2.0 * B * nq * hd * 2
+    peak, src = _peak_hbm()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    kernels.check_device("attn microbench")
+    return {"kernel": "fg_paged_decode_attn", "B": B, "context": ctx, "nq": nq, "nkv": nkv, "hd": hd,
+            "window": window, "ms": ms, "bytes": nbytes, "GBps": gbs, "frac_hbm": gbs / peak,
+            "peak": f"{src} {peak} GB/s"}
+
+
+def bench_gemm(T: int, N: int, K: int, epilogue: str = "store", iters: int = 20, warmup: int = 5,
+               seed: int = 2, splits: int = 0) -> dict:
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.empty((T, K), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
+    w = torch.empty((N, K), dtype=torch.bfloat16, device="cuda").normal_(0, 0.02, generator=g)
+    epi = {"store": _lib.FG_EPI_STORE, "residual": _lib.FG_EPI_RESIDUAL, "swiglu": _lib.FG_EPI_SWIGLU}[epilogue]
+    n_out = N // 2 if epi == _lib.FG_EPI_SWIGLU else N
+    res = torch.empty((T, n_out), dtype=torch.bfloat16, device="cuda").normal_(generator=g) \
+        if epi == _lib.FG_EPI_RESIDUAL else None
+    out = torch.empty((T, n_out), dtype=torch.bfloat16, device="cuda")
+    fn = lambda: kernels.gemm(x, w, epilogue=epi, residual=res, out=out, splits=splits)  # noqa: E731
+    ms = _time(fn, iters, warmup)
+    nbytes = 2.0 * (N * K + T * K + T * n_out * (2 if res is not None else 1))
+    flops = 2.0 * T * N * K
+    peak, src = _peak_hbm()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    kernels.check_device("gemm microbench")
+    used = splits if splits > 0 else _lib.lib().fg_gemm_pick_splits(T, N, K)
+    return {"kernel": "fg_gemm_bf16", "T": T, "N": N, "K": K, "epilogue": epilogue, "splits": used,
+            "ms": ms, "bytes": nbytes, "GBps": gbs, "TFLOPs": flops / (ms * 1e-3) / 1e12,
+            "frac_hbm": gbs / peak, "peak": f"{src} {peak} GB/s"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["attn", "gemm", "sweep-attn", "llama-gemms"])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--context", type=int, default=4096)
+    ap.add_argument("--window", type=int, default=0)
+    ap.add_argument("--nq", type=int, default=32)
+    ap.add_argument("--nkv", type=int, default=8)
+    ap.add_argument("--hd", type=int, default=128)
+    ap.add_argument("--T", type=int, default=64)
+    ap.add_argument("--N", type=int, default=28672)
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--splits", type=int, default=0)
+    ap.add_argument("--epilogue", default="store")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    a = ap.parse_args()
+    build.build()
+    torch.cuda.set_device(0)
+    if a.what == "attn":
+        print(json.dumps(bench_attn(a.batch, a.context, a.nq, a.nkv, a.hd, a.window, a.iters, a.warmup)))
+    elif a.what == "gemm":
+        print(json.dumps(bench_gemm(a.T, a.N, a.K, a.epilogue, a.iters, a.warmup, splits=a.splits)))
+    elif a.what == "sweep-attn":
+        for B in (1, 32, 256):
+            for ctx in (512, 4096, 32768):
+                if B * ctx * 8 * 128 * 4 > 40e9:  # keep each case's pool under ~40 GB
+                    continue
+                print(json.dumps(bench_attn(B, ctx, iters=a.iters, warmup=a.warmup)), flush=True)
+                torch.cuda.empty_cache()
+    elif a.what == "llama-gemms":
+        T = a.T
+        for N, K, epi in ((6144, 4096, "store"), (4096, 4096, "residual"), (28672, 4096, "swiglu"),
+                          (4096, 14336, "residual"), (128256, 4096, "store")):
+            print(json.dumps(bench_gemm(T, N, K, epi, a.iters, a.warmup)), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -338,6 +338,53 @@ class OracleModel:
         x = rms_norm(h, self.w["final_norm"], s.eps, s.fp32_weight_mul)
         return F.linear(x, self.w["lm_head"])
 
+    def prefill(self, prompts: torch.Tensor) -> torch.Tensor:
+        """Full-prompt prefill of prompts [B, S] with a causal (and, per layer,
+        sliding-window) mask, as the reference's prefill does
+        (runner.py:66-116); fills the caches and returns the last logits."""
+        s = self.spec
+        B, S = prompts.shape
+        self.reset(B)
+        pos = torch.arange(S)
+        cos, sin = rope_cos_sin(pos, self.inv_freq, self.rope_scaling, self.dtype)
+        h = self.w["embed"][prompts.reshape(-1)].view(B, S, s.hidden)
+        scale = 1.0 / math.sqrt(s.head_dim)
+        G = s.n_q // s.n_kv
+        for i in range(s.num_layers):
+            x = rms_norm(h, self.w[f"{i}.ln1"], s.eps, s.fp32_weight_mul)
+            bias = s.attn_bias
+            q = self._linear(x, f"{i}.wq", f"{i}.bq" if bias else None).view(B * S, s.n_q, s.head_dim)
+            k = self._linear(x, f"{i}.wk", f"{i}.bk" if bias else None).view(B * S, s.n_kv, s.head_dim)
+            v = self._linear(x, f"{i}.wv", f"{i}.bv" if bias else None).view(B, S, s.n_kv, s.head_dim)
+            q = apply_rope(q, cos.repeat(B, 1), sin.repeat(B, 1)).view(B, S, s.n_q, s.head_dim)
+            k = apply_rope(k, cos.repeat(B, 1), sin.repeat(B, 1)).view(B, S, s.n_kv, s.head_dim)
+            for b in range(B):
+                self.k_cache[b][i] = k[b].clone()
+                self.v_cache[b][i] = v[b].clone()
+            kk = k.float().repeat_interleave(G, dim=2)
+            vv = v.float().repeat_interleave(G, dim=2)
+            sc = torch.einsum("bqhd,bkhd->bhqk", q.float(), kk) * scale
+            mask = pos[None, :] > pos[:, None]
+            window = s.layer_windows[i] if s.layer_windows else 0
+            if window > 0:
+                mask = mask | (pos[None, :] <= pos[:, None] - window)
+            sc = sc.masked_fill(mask, float("-inf"))
+            if s.sinks:
+                sk = self.w[f"{i}.sinks"].float()[None, :, None, None].expand(B, -1, S, 1)
+                lg = torch.cat([sc, sk], dim=-1)
+                lg = lg - lg.max(dim=-1, keepdim=True).values
+                probs = torch.softmax(lg, dim=-1)[..., :-1]
+            else:
+                probs = torch.softmax(sc, dim=-1)
+            o = torch.einsum("bhqk,bkhd->bqhd", probs, vv).reshape(B, S, -1).to(self.dtype)
+            h = h + self._linear(o, f"{i}.wo", f"{i}.bo" if bias else None)
+            flat = h.reshape(B * S, s.hidden)
+            flat = self._moe_ffn(i, flat) if s.moe else self._dense_ffn(i, flat)
+            h = flat.view(B, S, s.hidden)
+        self.lengths = [S] * B
+        x = rms_norm(h[:, -1], self.w["final_norm"], s.eps, s.fp32_weight_mul)
+        return F.linear(x, self.w["lm_head"])
+
     def prefill_stepwise(self, prompts: torch.Tensor) -> torch.Tensor:
         """Feed prompts [B, S] one position at a time (causal attention makes
         this equal to a full prefill); returns the last logits [B, V]."""
@@ -349,7 +396,7 @@ class OracleModel:
 
     def generate(self, prompts: torch.Tensor, steps: int) -> tuple[torch.Tensor, list[torch.Tensor]]:
         """Greedy decode: returns tokens [B, steps] and the logits of every step."""
-        logits = self.prefill_stepwise(prompts)
+        logits = self.prefill(prompts)
         toks, all_logits = [], []
         for _ in range(steps):
             all_logits.append(logits)

@@ -1,0 +1,70 @@
+"""The C ABI: libfgb200.so builds for sm_100a here (nvcc cross-compiles), loads
+without a GPU, and exports exactly what include/fgb200.h declares."""
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _declared() -> set[str]:
+    text = (ROOT / "include" / "fgb200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"^\s*(?:const\s+)?[\w ]+?\**\s*\b(fg_\w+)\s*\(", text, flags=re.M))
+
+
+@pytest.fixture(scope="module")
+def lib_path():
+    from fluidgpu_b200 import build
+
+    return build.build()
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    for must in ("fg_gemm_bf16", "fg_paged_decode_attn", "fg_rope_kv_append", "fg_last_error",
+                 "fg_device_status", "fg_kv_append", "fg_argmax", "fg_embed", "fg_rmsnorm"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol(lib_path):
+    out = subprocess.run(["nm", "-D", "--defined-only", str(lib_path)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    missing = _declared() - exported
+    assert not missing, f"declared but not exported: {sorted(missing)}"
+
+
+def test_binding_covers_header(lib_path):
+    from fluidgpu_b200 import _lib
+
+    assert set(_lib.SIGNATURES) == _declared()
+    handle = _lib.lib()
+    for name in _lib.SIGNATURES:
+        assert getattr(handle, name) is not None
+    assert handle.fg_version() >= 1
+
+
+def test_argument_errors_need_no_gpu(lib_path):
+    """Shape/pointer validation happens on the host before any CUDA call."""
+    from fluidgpu_b200 import _lib
+
+    h = _lib.lib()
+    rc = h.fg_gemm_bf16(None, None, None, None, None, 4, 128, 64, 0, 1, None, 0, None)
+    assert rc == _lib.FG_ERR_ARG
+    assert b"null pointer" in h.fg_last_error()
+    rc = h.fg_paged_decode_attn(1, 1, 1, 1, 1, None, 1, None, 0, 1, 32, 8, 96, 16, 1, 1, 16, 0,
+                                1.0, None)
+    assert rc == _lib.FG_ERR_ARG and b"hd must be 64 or 128" in h.fg_last_error()
+    assert h.fg_gemm_workspace_bytes(64, 4096, 4096, 4) > 0
+    assert h.fg_gemm_workspace_bytes(64, 4096, 4096, 1) == 0
+
+
+def test_no_cluster_multicast_anywhere():
+    """Multi-GPU safety rule: no bulk/TMA load with cluster multicast in any source."""
+    pat = "multi" + "cast::cluster"
+    for p in list((ROOT / "fluidgpu_b200" / "csrc").rglob("*")) + [ROOT / "include" / "fgb200.h"]:
+        if p.is_file():
+            assert pat not in p.read_text(), p
