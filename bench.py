@@ -11,9 +11,14 @@ cache is filled with synthetic N(0,1) values for the 4096-token prompts
 (the timed work does not depend on the values), and the KV pool (~35 GB)
 and weights (~16 GB) are far larger than L2, so no flush is needed.
 
-value : tokens/s over all ranks, inputs resident in HBM, device-timed.
+value : tokens/s over all ranks, inputs resident in HBM, device-timed; each
+        step is one replay of the CUDA graph holding the whole decode step.
 e2e   : tokens/s through DecodeEngine.step (host tokens in pinned memory,
         H2D copy + step + argmax + D2H read per step), device-timed.
+roofline: paged attention (the dominant kernel, ~60% of the step), its
+        duration from CUDA event pairs around each of its launches during R
+        steps run right after the timed region from the host (the same
+        kernels and split plans the graph replays).
 Under torchrun (N > 1) every rank decodes its own batch of 64 requests
 (attention data-parallel by request, co-located FFN: weak scaling).
 """
@@ -182,50 +187,64 @@ def run_fgb200(args) -> None:
     spec = LLAMA3_8B
     B, ctx = args.batch, args.context
     W, K = args.warmup, args.steps
-    total = ctx + W + 2 * K + 8
+    R = 3  # replays of the attention-timed graph
+    total = ctx + W + 2 * K + R + 8
     cfg = EngineConfig(model_name=spec.name, max_seq_len=total, world_size=1, device=f"cuda:{local}",
-                       max_batch=B)
+                       max_batch=B, cuda_graph_decode=not args.eager)
     weights = ModelWeights.random(spec, seed=0, device=dev)
     eng = DecodeEngine(weights, cfg)
     eng.start(B, prompt_lens=[ctx] * B, reserve_tokens=total)
     g = torch.Generator(device=dev).manual_seed(1 + rank)
     eng.kv_cache.pool.normal_(0.0, 1.0, generator=g)
-    tok = torch.randint(0, spec.vocab, (B,), generator=g, device=dev)
+    eng._tok_dev.copy_(torch.randint(0, spec.vocab, (B,), generator=g, device=dev))
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    # ---- warm-up (untimed) ----
-    for _ in range(W):
-        tok = eng.step_device(tok)
+    def one_step():
+        if args.eager:
+            eng._tok_dev.copy_(eng.step_device(eng._tok_dev))
+        else:
+            eng.replay()
+
+    # launches one step issues (graph capture counts them; eager counts directly)
+    n0 = kernels.launch_count()
+    one_step()  # first warm-up step (captures the graph)
+    launches_per_step = kernels.launch_count() - n0
+    for _ in range(W - 1):
+        one_step()
     torch.cuda.synchronize()
     kernels.check_device("bench warm-up")
 
     # ---- timed: device-resident inputs ----
-    lens0 = eng.kv_cache.seq_lengths()
-    kernels.KernelTimer.enable("attn")
     sampler = ClockSampler(local)
     barrier()
     torch.cuda.synchronize()
     sampler.start()
-    n0 = kernels.launch_count()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
+    h0 = time.perf_counter()
     for _ in range(K):
-        tok = eng.step_device(tok)
+        one_step()
+    host_ms = (time.perf_counter() - h0) * 1e3 / K  # enqueue cost per step (diagnostic)
     e1.record()
     torch.cuda.synchronize()
-    n1 = kernels.launch_count()
     barrier()
     clocks = sampler.stop()
-    kernels.KernelTimer.disable()
     ms = e0.elapsed_time(e1)
     kernels.check_device("bench timed region")
 
-    # dominant kernel: paged attention, one launch per layer per step
+    # ---- dominant kernel: paged attention durations from event pairs captured
+    # around each of its launches (same kernels, same stream, R replays) ----
+    lens0 = eng.kv_cache.seq_lengths()
+    kernels.KernelTimer.enable("attn")
+    for _ in range(R):  # eager steps: the same kernels and split plans the graph replays
+        eng._tok_dev.copy_(eng.step_device(eng._tok_dev))
+    torch.cuda.synchronize()
     attn = kernels.KernelTimer.durations_ms("attn")
+    kernels.KernelTimer.disable()
     tot_bytes, tot_ms = 0.0, 0.0
     for i, (d, meta) in enumerate(attn):
         step = i // spec.num_layers
@@ -234,9 +253,10 @@ def run_fgb200(args) -> None:
         tot_ms += d
     attn_launch_ms = tot_ms / max(len(attn), 1)
     attn_launch_bytes = tot_bytes / max(len(attn), 1)
+    kernels.check_device("bench roofline region")
 
     # ---- e2e through the public API: host tokens in, host tokens out ----
-    host_tok = tok.cpu().pin_memory()
+    host_tok = eng._tok_dev.cpu().pin_memory()
     torch.cuda.synchronize()
     barrier()
     f0 = torch.cuda.Event(enable_timing=True)
@@ -282,7 +302,10 @@ def run_fgb200(args) -> None:
                          "peak_source": f"{peak_src} (hbm_gbs)", "traffic": traffic,
                          "algorithmic_bytes_per_launch": attn_launch_bytes,
                          "launch_ms": attn_launch_ms, "launches": len(attn)},
-            "gpu_launches": int(n1 - n0),
+            "gpu_launches": int(launches_per_step * K),
+            "launches_per_step": int(launches_per_step),
+            "cuda_graph": not args.eager,
+            "host_enqueue_ms_per_step": host_ms,
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -302,6 +325,7 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="launch every kernel from the host (no CUDA graph)")
     args = ap.parse_args()
     assert args.warmup >= 0 and args.steps > 0
     if args.impl == "reference":

@@ -40,7 +40,10 @@ SIGNATURES: dict[str, tuple] = {
     "fg_embed": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P]),
     "fg_rmsnorm": (c_int, [_P, _P, _P, c_int, c_int, c_float, c_int, _P]),
     "fg_gemm_bf16": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, c_size_t, _P]),
-    "fg_gemm_pick_splits": (c_int, [c_int, c_int, c_int]),
+    "fg_gemm_bf16_packed": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, c_size_t, _P]),
+    "fg_pack_weight_bf16": (c_int, [_P, _P, c_int, c_int, _P]),
+    "fg_packed_weight_bytes": (c_size_t, [c_int, c_int]),
+    "fg_gemm_grid": (c_int, [c_int, c_int, c_int, c_int]),
     "fg_gemm_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "fg_rope_kv_append": (
         c_int,

@@ -102,6 +102,8 @@ __global__ void __launch_bounds__(kThreads) paged_attn_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int G = p.G;
+  griddep_wait();  // q, the new token's KV and seq_lens come from earlier kernels
+  if (threadIdx.x == 0) griddep_launch_dependents();
 
   const int Lq = p.seq_lens[b];
   const int lo = p.window > 0 ? max(0, Lq - p.window) : 0;
@@ -339,6 +341,8 @@ __global__ void __launch_bounds__(kThreads) paged_attn_kernel(
 
 // merge split partials: grid (nq, B), block = hd threads
 __global__ void attn_combine_kernel(const Params p, int hd) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int64_t base = ((int64_t)b * p.nq + h) * p.splits;
   float M = kNegBig;
@@ -393,12 +397,11 @@ int launch(const Params& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaSt
     }
     attr_done[dev & 63] = true;
   }
-  dim3 grid(p.splits, p.nkv, p.B);
-  kern<<<grid, kThreads, L::DYN_SMEM, st>>>(tk, tv, p);
-  int rc = check_launch("fg_paged_decode_attn");
+  int rc = launch_k("fg_paged_decode_attn", kern, dim3(p.splits, p.nkv, p.B), dim3(kThreads),
+                    L::DYN_SMEM, st, tk, tv, p);
   if (rc || p.splits == 1) return rc;
-  attn_combine_kernel<<<dim3(p.nq, p.B), HD, 0, st>>>(p, HD);
-  return check_launch("fg_paged_decode_attn(combine)");
+  return launch_k("fg_paged_decode_attn(combine)", attn_combine_kernel, dim3(p.nq, p.B), dim3(HD), 0,
+                  st, p, HD);
 }
 
 }  // namespace attn

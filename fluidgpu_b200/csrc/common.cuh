@@ -150,6 +150,29 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
 }
 
 // ---------------------------------------------------------------------------
+// bulk (non-tensor) copy global -> own shared memory, completion on an mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                          uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start while its predecessor drains; everything that
+// reads the predecessor's results (or writes what it reads) must come after
+// griddep_wait(). Both are no-ops for a normal launch.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // warp helpers
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float warp_max(float v) {
@@ -176,6 +199,64 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64
                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                       CUtensorMapSwizzle swizzle);
 int num_sms();
+bool pdl_enabled();
+
+// Launch with programmatic stream serialisation (PDL) unless disabled by
+// FGB200_PDL=0; the kernel must call griddep_wait() before dependent work.
+template <typename... KArgs, typename... Args>
+int launch_k(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+             cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) {
+    set_last_error("%s: launch failed: %s", what, cudaGetErrorString(e));
+    (void)cudaGetLastError();
+    return FG_ERR_CUDA;
+  }
+  return check_launch(what);
+}
+// Launch as a thread-block cluster of `cluster` CTAs (plus PDL as launch_k).
+template <typename... KArgs, typename... Args>
+int launch_kc(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 cluster, dim3 block,
+              size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cluster.x;
+    attr[na].val.clusterDim.y = cluster.y;
+    attr[na].val.clusterDim.z = cluster.z;
+    ++na;
+  }
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) {
+    set_last_error("%s: launch failed: %s", what, cudaGetErrorString(e));
+    (void)cudaGetLastError();
+    return FG_ERR_CUDA;
+  }
+  return check_launch(what);
+}
 }  // namespace fg
 
 #define FG_REQUIRE(cond, ...)              \

@@ -13,6 +13,8 @@ namespace fg {
 // ---------------------------------------------------------------------------
 __global__ void embed_kernel(const int64_t* __restrict__ ids, const uint4* __restrict__ table,
                              uint4* __restrict__ out, int H8, int vocab) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int t = blockIdx.x;
   const int64_t id = ids[t];
   const bool ok = id >= 0 && id < vocab;
@@ -42,6 +44,8 @@ __global__ void __launch_bounds__(THREADS) rmsnorm_kernel(const uint4* __restric
                                                           const uint4* __restrict__ w,
                                                           uint4* __restrict__ out, int H,
                                                           float eps, int mode) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float red[THREADS / 32];
   const int H8 = H >> 3;
   const uint4* xr = x + (int64_t)blockIdx.x * H8;
@@ -100,6 +104,8 @@ __global__ void rope_kv_append_kernel(const __nv_bfloat16* __restrict__ qkv,
                                       __nv_bfloat16* __restrict__ k_cache,
                                       __nv_bfloat16* __restrict__ v_cache, int nq, int nkv, int hd,
                                       int block_size) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int b = blockIdx.x;
   const int head = blockIdx.y;
   const int i = threadIdx.x;
@@ -153,6 +159,8 @@ __device__ __forceinline__ void argmax_merge(float& v, int& i, float ov, int oi)
 template <int THREADS>
 __global__ void __launch_bounds__(THREADS) argmax_kernel(const __nv_bfloat16* __restrict__ logits,
                                                          int64_t* __restrict__ out, int V) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float sv[THREADS / 32];
   __shared__ int si[THREADS / 32];
   const __nv_bfloat16* row = logits + (int64_t)blockIdx.x * V;
@@ -203,6 +211,8 @@ __global__ void kv_append_kernel(const uint4* __restrict__ k, const uint4* __res
                                  const int32_t* __restrict__ block_table, int max_blocks,
                                  int num_blocks, uint4* __restrict__ k_cache,
                                  uint4* __restrict__ v_cache, int nkv, int hd8, int block_size) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int t = blockIdx.x;
   const int head = blockIdx.y;
   const bool is_k = head < nkv;
@@ -222,6 +232,8 @@ __global__ void kv_append_kernel(const uint4* __restrict__ k, const uint4* __res
 }
 
 __global__ void advance_kernel(int32_t* positions, int32_t* seq_lens, int B) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < B) {
     if (positions) positions[b] += 1;
@@ -240,9 +252,9 @@ int fg_embed(const int64_t* ids, const fg_bf16* table, fg_bf16* out, int T, int 
   FG_REQUIRE(((uintptr_t)table & 15) == 0 && ((uintptr_t)out & 15) == 0,
              "fg_embed: table/out must be 16-byte aligned");
   if (T == 0) return FG_OK;
-  fg::embed_kernel<<<T, 128, 0, (cudaStream_t)stream>>>(
-      ids, reinterpret_cast<const uint4*>(table), reinterpret_cast<uint4*>(out), H / 8, vocab);
-  return fg::check_launch("fg_embed");
+  return fg::launch_k("fg_embed", fg::embed_kernel, dim3(T), dim3(128), 0, (cudaStream_t)stream,
+                      ids, reinterpret_cast<const uint4*>(table), reinterpret_cast<uint4*>(out),
+                      H / 8, vocab);
 }
 
 int fg_rmsnorm(const fg_bf16* x, const fg_bf16* weight, fg_bf16* out, int T, int H, float eps,
@@ -255,10 +267,10 @@ int fg_rmsnorm(const fg_bf16* x, const fg_bf16* weight, fg_bf16* out, int T, int
   FG_REQUIRE((((uintptr_t)x | (uintptr_t)weight | (uintptr_t)out) & 15) == 0,
              "fg_rmsnorm: pointers must be 16-byte aligned");
   if (T == 0) return FG_OK;
-  fg::rmsnorm_kernel<256><<<T, 256, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const uint4*>(x), reinterpret_cast<const uint4*>(weight),
-      reinterpret_cast<uint4*>(out), H, eps, weight_mode);
-  return fg::check_launch("fg_rmsnorm");
+  return fg::launch_k("fg_rmsnorm", fg::rmsnorm_kernel<256>, dim3(T), dim3(256), 0,
+                      (cudaStream_t)stream, reinterpret_cast<const uint4*>(x),
+                      reinterpret_cast<const uint4*>(weight), reinterpret_cast<uint4*>(out), H, eps,
+                      weight_mode);
 }
 
 int fg_rope_kv_append(const fg_bf16* qkv, const int32_t* positions, const float* inv_freq,
@@ -271,13 +283,13 @@ int fg_rope_kv_append(const fg_bf16* qkv, const int32_t* positions, const float*
   FG_REQUIRE(hd % 2 == 0 && hd <= 256 && block_size > 0 && max_blocks > 0 && num_blocks > 0,
              "fg_rope_kv_append: bad hd=%d / block_size=%d", hd, block_size);
   if (B == 0) return FG_OK;
-  dim3 grid(B, nq + 2 * nkv);
-  fg::rope_kv_append_kernel<<<grid, hd / 2, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(qkv), positions, inv_freq, attention_scaling,
-      block_table, max_blocks, num_blocks, reinterpret_cast<__nv_bfloat16*>(q_out),
-      reinterpret_cast<__nv_bfloat16*>(k_cache), reinterpret_cast<__nv_bfloat16*>(v_cache), nq,
-      nkv, hd, block_size);
-  return fg::check_launch("fg_rope_kv_append");
+  return fg::launch_k("fg_rope_kv_append", fg::rope_kv_append_kernel, dim3(B, nq + 2 * nkv),
+                      dim3(hd / 2), 0, (cudaStream_t)stream,
+                      reinterpret_cast<const __nv_bfloat16*>(qkv), positions, inv_freq,
+                      attention_scaling, block_table, max_blocks, num_blocks,
+                      reinterpret_cast<__nv_bfloat16*>(q_out),
+                      reinterpret_cast<__nv_bfloat16*>(k_cache),
+                      reinterpret_cast<__nv_bfloat16*>(v_cache), nq, nkv, hd, block_size);
 }
 
 int fg_kv_append(const fg_bf16* k, const fg_bf16* v, const int32_t* seq_ids,
@@ -292,28 +304,27 @@ int fg_kv_append(const fg_bf16* k, const fg_bf16* v, const int32_t* seq_ids,
   FG_REQUIRE((((uintptr_t)k | (uintptr_t)v | (uintptr_t)k_cache | (uintptr_t)v_cache) & 15) == 0,
              "fg_kv_append: pointers must be 16-byte aligned");
   if (T == 0) return FG_OK;
-  dim3 grid(T, 2 * nkv);
-  fg::kv_append_kernel<<<grid, hd / 8 < 32 ? 32 : hd / 8, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const uint4*>(k), reinterpret_cast<const uint4*>(v), seq_ids, positions,
-      block_table, max_blocks, num_blocks, reinterpret_cast<uint4*>(k_cache),
-      reinterpret_cast<uint4*>(v_cache), nkv, hd / 8, block_size);
-  return fg::check_launch("fg_kv_append");
+  return fg::launch_k("fg_kv_append", fg::kv_append_kernel, dim3(T, 2 * nkv),
+                      dim3(hd / 8 < 32 ? 32 : hd / 8), 0, (cudaStream_t)stream,
+                      reinterpret_cast<const uint4*>(k), reinterpret_cast<const uint4*>(v), seq_ids,
+                      positions, block_table, max_blocks, num_blocks,
+                      reinterpret_cast<uint4*>(k_cache), reinterpret_cast<uint4*>(v_cache), nkv,
+                      hd / 8, block_size);
 }
 
 int fg_argmax(const fg_bf16* logits, int64_t* out, int T, int V, fg_stream_t stream) {
   FG_REQUIRE(logits && out, "fg_argmax: null pointer");
   FG_REQUIRE(T >= 0 && V > 0, "fg_argmax: bad sizes");
   if (T == 0) return FG_OK;
-  fg::argmax_kernel<1024><<<T, 1024, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(logits), out, V);
-  return fg::check_launch("fg_argmax");
+  return fg::launch_k("fg_argmax", fg::argmax_kernel<1024>, dim3(T), dim3(1024), 0,
+                      (cudaStream_t)stream, reinterpret_cast<const __nv_bfloat16*>(logits), out, V);
 }
 
 int fg_advance(int32_t* positions, int32_t* seq_lens, int B, fg_stream_t stream) {
   FG_REQUIRE(B >= 0, "fg_advance: bad B");
   if (B == 0 || (!positions && !seq_lens)) return FG_OK;
-  fg::advance_kernel<<<(B + 255) / 256, 256, 0, (cudaStream_t)stream>>>(positions, seq_lens, B);
-  return fg::check_launch("fg_advance");
+  return fg::launch_k("fg_advance", fg::advance_kernel, dim3((B + 255) / 256), dim3(256), 0,
+                      (cudaStream_t)stream, positions, seq_lens, B);
 }
 
 }  // extern "C"

@@ -7,6 +7,14 @@ Two entry points per step:
       greedy argmax (fg_argmax, on the device like the reference's sync-free
       loop, engine.py:328-348) and copies the next tokens back.
   step_device(tokens) -> next tokens on the device, no host round trip.
+
+With EngineConfig.cuda_graph_decode the whole step (embed .. argmax, KV
+append and position advance included) is captured once per attention length
+bucket (powers of two from 256 up to max_seq_len) and replayed: the device
+counters advance inside the graph, the host mirror advances after each
+replay, and the next-token buffer feeds the following replay directly. This
+is the B200 form of the reference's graphed decode segments
+(graph_decode.py:57-153), without the per-segment host send/recv.
 """
 from __future__ import annotations
 
@@ -40,6 +48,9 @@ class DecodeEngine:
         self.device = cfg.torch_device
         self._tok_dev: torch.Tensor | None = None
         self._tok_host: torch.Tensor | None = None
+        self._next_dev: torch.Tensor | None = None
+        self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.use_graph = bool(cfg.cuda_graph_decode)
 
     @property
     def kv_cache(self):
@@ -49,7 +60,9 @@ class DecodeEngine:
               reserve_tokens: int | list[int] | None = None) -> None:
         self.runner.start(batch, prompt_lens, reserve_tokens)
         self._tok_dev = torch.zeros(batch, dtype=torch.int64, device=self.device)
+        self._next_dev = torch.zeros(batch, dtype=torch.int64, device=self.device)
         self._tok_host = torch.zeros(batch, dtype=torch.int64).pin_memory()
+        self._graphs.clear()
 
     @torch.inference_mode()
     def step_device(self, tokens: torch.Tensor) -> torch.Tensor | None:
@@ -58,12 +71,53 @@ class DecodeEngine:
             return None
         return kernels.argmax(logits.reshape(logits.shape[0], -1))
 
+    # -- CUDA graph decode ------------------------------------------------------
+    def bucket(self, n: int) -> int:
+        return self.kv_cache.bucket(n)
+
+    def capture(self, bucket: int) -> torch.cuda.CUDAGraph:
+        """Capture one decode step planned for `bucket` tokens. The graph reads
+        its tokens from, and writes the next tokens back to, a static buffer."""
+        if bucket in self._graphs:
+            return self._graphs[bucket]
+        kv = self.kv_cache
+        B = kv.batch
+        self.runner.reserve_workspaces(B, bucket)
+        snap = kv.snapshot_host()
+        kv.plan_len_override = bucket
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        try:
+            with torch.cuda.stream(s), torch.inference_mode():
+                with torch.cuda.graph(g, stream=s):
+                    logits = self.runner.decode_step(self._tok_dev)
+                    kernels.argmax(logits.reshape(B, -1), out=self._next_dev)
+                    self._tok_dev.copy_(self._next_dev)
+        finally:
+            kv.plan_len_override = None
+            kv.restore_host(snap)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self._graphs[bucket] = g
+        return g
+
+    def replay(self) -> torch.Tensor:
+        """One graphed decode step from the static token buffer; returns the
+        static next-token buffer (also the next replay's input)."""
+        g = self.capture(self.bucket(self.kv_cache.max_attended()))
+        g.replay()
+        self.kv_cache.host_advance(1)
+        return self._next_dev
+
     @torch.inference_mode()
     def step(self, tokens_host: torch.Tensor) -> torch.Tensor | None:
         """One greedy step from host tokens [B] to host tokens [B]."""
         assert self._tok_dev is not None, "call start() first"
         self._tok_dev.copy_(tokens_host, non_blocking=True)
-        nxt = self.step_device(self._tok_dev)
+        if self.use_graph and self.rank == 0 and self.comm.get_world_size() == 1:
+            nxt = self.replay()
+        else:
+            nxt = self.step_device(self._tok_dev)
         if nxt is None:
             return None
         self._tok_host.copy_(nxt, non_blocking=True)

@@ -72,19 +72,22 @@ class KernelTimer:
 
 
 class Workspace:
-    """Zero-initialised scratch buffers keyed by (device, stream, slot).
+    """Zero-initialised scratch buffers keyed by (device, slot).
 
-    The GEMM split-K tickets must start at zero; the kernels leave them at
+    Kernels that share a slot run in stream order; callers that may overlap
+    on the GPU (several runners, several streams) use distinct slot names.
+    The GEMM stream-K tickets must start at zero and the kernels leave them at
     zero again, so a buffer is zeroed once, when it is (re)allocated.
+    Buffers persist (and may be captured into CUDA graphs).
     """
 
-    _bufs: dict[tuple[int, int, str], torch.Tensor] = {}
+    _bufs: dict[tuple[int, str], torch.Tensor] = {}
 
     @classmethod
     def get(cls, nbytes: int, device: torch.device, slot: str) -> torch.Tensor | None:
         if nbytes <= 0:
             return None
-        key = (device.index or 0, _stream(device), slot)
+        key = (device.index if device.index is not None else torch.cuda.current_device(), slot)
         buf = cls._bufs.get(key)
         if buf is None or buf.numel() < nbytes:
             size = max(nbytes, 1 << 20)
@@ -146,12 +149,35 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, mode: int = _lib.
     return out
 
 
-def gemm(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = _lib.FG_EPI_STORE,
+class PackedWeight:
+    """A [N, K] bf16 weight in the tile layout of fg_pack_weight_bf16
+    (contiguous 16 KB swizzled 128x64 tiles), ready for fg_gemm_bf16_packed."""
+
+    def __init__(self, w: torch.Tensor) -> None:
+        _check(w, "w", _BF16)
+        assert w.ndim == 2, "weight must be [N, K]"
+        self.N, self.K = int(w.shape[0]), int(w.shape[1])
+        self.device = w.device
+        nbytes = _lib.lib().fg_packed_weight_bytes(self.N, self.K)
+        self.data = torch.empty(nbytes, dtype=torch.uint8, device=w.device)
+        call("fg_pack_weight_bf16", _ptr(w), _ptr(self.data), self.N, self.K, _stream(w.device))
+
+    @property
+    def shape(self) -> tuple[int, int]:
+        return (self.N, self.K)
+
+    def nbytes(self) -> int:
+        return self.data.numel()
+
+
+def gemm(x: torch.Tensor, w: "torch.Tensor | PackedWeight", *, epilogue: int = _lib.FG_EPI_STORE,
          residual: torch.Tensor | None = None, bias: torch.Tensor | None = None,
          out: torch.Tensor | None = None, splits: int = 0, slot: str = "gemm") -> torch.Tensor:
     """acc = x @ w.T on tcgen05 with the given epilogue (see fg_gemm_bf16)."""
     _check(x, "x", _BF16)
-    _check(w, "w", _BF16)
+    packed = isinstance(w, PackedWeight)
+    if not packed:
+        _check(w, "w", _BF16)
     K = x.shape[-1]
     T = x.numel() // K
     N, Kw = w.shape
@@ -165,12 +191,11 @@ def gemm(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = _lib.FG_EPI_STORE,
     if bias is not None:
         _check(bias, "bias", _BF16)
     lib = _lib.lib()
-    if splits <= 0:
-        splits = lib.fg_gemm_pick_splits(T, N, K)
     ws_bytes = lib.fg_gemm_workspace_bytes(T, N, K, splits)
     ws = Workspace.get(ws_bytes, x.device, slot)
     ev = KernelTimer.start("gemm")
-    call("fg_gemm_bf16", _ptr(x), _ptr(w), _ptr(out), _ptr(residual), _ptr(bias), T, N, K,
+    call("fg_gemm_bf16_packed" if packed else "fg_gemm_bf16", _ptr(x),
+         _ptr(w.data) if packed else _ptr(w), _ptr(out), _ptr(residual), _ptr(bias), T, N, K,
          epilogue, splits, _ptr(ws), ws_bytes, _stream(x.device))
     KernelTimer.stop("gemm", ev, T=T, N=N, K=K)
     return out

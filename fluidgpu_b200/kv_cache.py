@@ -78,6 +78,9 @@ class PagedKVCache:
         self._blocks: list[list[int]] = [[] for _ in range(max_batch)]
         self._host_pos = [0] * max_batch
         self.batch = 0
+        # attention split plan length used while capturing a CUDA graph (the
+        # captured launch must stay valid as sequences grow within a bucket)
+        self.plan_len_override: int | None = None
 
     # -- layout ----------------------------------------------------------------
     def layer_pages(self, layer_idx: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -170,6 +173,34 @@ class PagedKVCache:
     def max_attended(self) -> int:
         """Longest attention span of the coming step (host mirror)."""
         return max(self._host_pos[: max(self.batch, 1)]) + 1
+
+    def bucket(self, n: int) -> int:
+        """Power-of-two length bucket (>= 256, <= max_seq_len) holding n tokens."""
+        b = 256
+        while b < n:
+            b *= 2
+        return min(b, self.max_seq_len)
+
+    def plan_len(self) -> int:
+        """Length the attention kernels plan their page splits for: the bucket
+        of the coming step's longest sequence, so eager steps and CUDA graphs
+        captured for that bucket launch identical plans (identical results)."""
+        if self.plan_len_override is not None:
+            return self.plan_len_override
+        return self.bucket(self.max_attended())
+
+    def host_advance(self, seq_len: int) -> None:
+        """Advance only the host mirror (after a replayed CUDA graph advanced
+        the device counters)."""
+        for b in range(self.batch):
+            self._host_pos[b] += seq_len
+            assert self._host_pos[b] < len(self._blocks[b]) * BLOCK + 1, "sequence ran past its reserved pages"
+
+    def snapshot_host(self) -> list[int]:
+        return list(self._host_pos)
+
+    def restore_host(self, snap: list[int]) -> None:
+        self._host_pos = list(snap)
 
     def reset(self) -> None:
         for b in range(self.max_batch):

@@ -35,10 +35,40 @@ def _peak_hbm() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
+GRAPH = True  # time launches replayed from a CUDA graph (no host overhead inside the window)
+
+
 def _time(fn, iters: int, warmup: int) -> float:
+    """Device milliseconds per call. With GRAPH, `iters` calls are captured in
+    one CUDA graph and replayed back to back between two events (the kernels'
+    own time plus the inter-kernel gaps a captured decode step also has);
+    otherwise each call is bracketed by events (host launch cost included)."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    if GRAPH:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            fn()  # workspace allocation happens outside the capture
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(iters):
+                    fn()
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(3):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b) / iters)
+        return statistics.median(ts)
     ts = []
     for _ in range(iters):
         a = torch.cuda.Event(enable_timing=True)
@@ -72,11 +102,11 @@ def bench_attn(B: int, ctx: int, nq: int = 32, nkv: int = 8, hd: int = 128, wind
     kernels.check_device("attn microbench")
     return {"kernel": "fg_paged_decode_attn", "B": B, "context": ctx, "nq": nq, "nkv": nkv, "hd": hd,
             "window": window, "ms": ms, "bytes": nbytes, "GBps": gbs, "frac_hbm": gbs / peak,
-            "peak": f"{src} {peak} GB/s"}
+            "peak": f"{src} {peak} GB/s", "timing": "graph" if GRAPH else "eager"}
 
 
 def bench_gemm(T: int, N: int, K: int, epilogue: str = "store", iters: int = 20, warmup: int = 5,
-               seed: int = 2, splits: int = 0) -> dict:
+               seed: int = 2, splits: int = 0, packed: bool = True) -> dict:
     g = torch.Generator(device="cuda").manual_seed(seed)
     x = torch.empty((T, K), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
     w = torch.empty((N, K), dtype=torch.bfloat16, device="cuda").normal_(0, 0.02, generator=g)
@@ -85,17 +115,18 @@ def bench_gemm(T: int, N: int, K: int, epilogue: str = "store", iters: int = 20,
     res = torch.empty((T, n_out), dtype=torch.bfloat16, device="cuda").normal_(generator=g) \
         if epi == _lib.FG_EPI_RESIDUAL else None
     out = torch.empty((T, n_out), dtype=torch.bfloat16, device="cuda")
-    fn = lambda: kernels.gemm(x, w, epilogue=epi, residual=res, out=out, splits=splits)  # noqa: E731
+    wk = kernels.PackedWeight(w) if packed else w
+    fn = lambda: kernels.gemm(x, wk, epilogue=epi, residual=res, out=out, splits=splits)  # noqa: E731
     ms = _time(fn, iters, warmup)
     nbytes = 2.0 * (N * K + T * K + T * n_out * (2 if res is not None else 1))
     flops = 2.0 * T * N * K
     peak, src = _peak_hbm()
     gbs = nbytes / (ms * 1e-3) / 1e9
     kernels.check_device("gemm microbench")
-    used = splits if splits > 0 else _lib.lib().fg_gemm_pick_splits(T, N, K)
-    return {"kernel": "fg_gemm_bf16", "T": T, "N": N, "K": K, "epilogue": epilogue, "splits": used,
+    used = _lib.lib().fg_gemm_grid(T, N, K, splits)
+    return {"kernel": "fg_gemm_bf16", "T": T, "N": N, "K": K, "epilogue": epilogue, "grid": used, "packed": packed,
             "ms": ms, "bytes": nbytes, "GBps": gbs, "TFLOPs": flops / (ms * 1e-3) / 1e12,
-            "frac_hbm": gbs / peak, "peak": f"{src} {peak} GB/s"}
+            "frac_hbm": gbs / peak, "peak": f"{src} {peak} GB/s", "timing": "graph" if GRAPH else "eager"}
 
 
 def main() -> None:
@@ -112,15 +143,20 @@ def main() -> None:
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--epilogue", default="store")
+    ap.add_argument("--rowmajor", action="store_true", help="row-major weights (2-D TMA) instead of packed")
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--eager", action="store_true", help="event-bracket each call instead of graph replay")
     ap.add_argument("--warmup", type=int, default=5)
     a = ap.parse_args()
+    global GRAPH
+    GRAPH = not a.eager
     build.build()
     torch.cuda.set_device(0)
     if a.what == "attn":
         print(json.dumps(bench_attn(a.batch, a.context, a.nq, a.nkv, a.hd, a.window, a.iters, a.warmup)))
     elif a.what == "gemm":
-        print(json.dumps(bench_gemm(a.T, a.N, a.K, a.epilogue, a.iters, a.warmup, splits=a.splits)))
+        print(json.dumps(bench_gemm(a.T, a.N, a.K, a.epilogue, a.iters, a.warmup, splits=a.splits,
+                                    packed=not a.rowmajor)))
     elif a.what == "sweep-attn":
         for B in (1, 32, 256):
             for ctx in (512, 4096, 32768):
@@ -132,7 +168,9 @@ def main() -> None:
         T = a.T
         for N, K, epi in ((6144, 4096, "store"), (4096, 4096, "residual"), (28672, 4096, "swiglu"),
                           (4096, 14336, "residual"), (128256, 4096, "store")):
-            print(json.dumps(bench_gemm(T, N, K, epi, a.iters, a.warmup)), flush=True)
+            for splits in ([a.splits] if a.splits else [0, 1, 2, 4, 8]):
+                print(json.dumps(bench_gemm(T, N, K, epi, a.iters, a.warmup, splits=splits,
+                                            packed=not a.rowmajor)), flush=True)
 
 
 if __name__ == "__main__":

@@ -135,10 +135,25 @@ class ModelWeights:
     def device(self) -> torch.device:
         return self.embed.device
 
-    def finalize(self) -> "ModelWeights":
+    GEMM_WEIGHTS = ("wqkv", "wo", "w_gate_up", "w_down")
+
+    def finalize(self, pack: bool = True) -> "ModelWeights":
+        """RoPE tables, and (pack=True) every GEMM weight converted to the
+        packed 16 KB tile layout the weight-streaming GEMM reads; the
+        row-major copies are released (the embedding table stays row-major
+        for the gather; a tied lm_head gets its own packed copy)."""
         inv, sc = self.spec.rope_tables()
         self.inv_freq = inv.to(device=self.device, dtype=torch.float32).contiguous()
         self.rope_scaling = float(sc)
+        if pack and self.device.type == "cuda":
+            from .kernels import PackedWeight
+
+            for L in self.layers:
+                for k in self.GEMM_WEIGHTS:
+                    if k in L and isinstance(L[k], torch.Tensor):
+                        L[k] = PackedWeight(L[k])
+            if isinstance(self.lm_head, torch.Tensor):
+                self.lm_head = PackedWeight(self.lm_head)
         return self
 
     # -- constructors --------------------------------------------------------

@@ -52,6 +52,8 @@ class FluidRunner:
             max_seq_len=cfg.max_seq_len, num_kv_heads=self.spec.n_kv, head_dim=self.spec.head_dim,
             dtype=cfg.dtype, device=self.device, max_batch=cfg.max_batch, num_blocks=num_blocks)
         self._moe_states: dict[int, dict[str, torch.Tensor]] = {}
+        # scratch slots of this runner (runners on other streams use their own)
+        self.slot = f"runner{id(self):x}"
 
     # -- sequence admission ---------------------------------------------------
     def start(self, batch: int, prompt_lens: list[int] | None = None,
@@ -135,14 +137,16 @@ class FluidRunner:
         B = hidden.shape[0]
         h = hidden.reshape(B, s.hidden)
         x = kernels.rmsnorm(h, W["ln1"], s.eps, s.norm_mode)
-        qkv = kernels.gemm(x, W["wqkv"], bias=W.get("bqkv"))
+        qkv = kernels.gemm(x, W["wqkv"], bias=W.get("bqkv"), slot=self.slot + ".gemm")
         kp, vp = kv.layer_pages(layer)
         bt = kv.block_table[:B]
         q = kernels.rope_kv_append(qkv, kv.positions[:B], self.weights.inv_freq,
                                    self.weights.rope_scaling, bt, kp, vp, s.n_q, s.n_kv, s.head_dim)
-        a = kernels.paged_decode_attn(q, kp, vp, bt, kv.seq_lens[:B], kv.max_attended(),
-                                      window=s.window(layer), sinks=W.get("sinks"))
-        out = kernels.gemm(a, W["wo"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h, bias=W.get("bo"))
+        a = kernels.paged_decode_attn(q, kp, vp, bt, kv.seq_lens[:B], kv.plan_len(),
+                                      window=s.window(layer), sinks=W.get("sinks"),
+                                      slot=self.slot + ".attn")
+        out = kernels.gemm(a, W["wo"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h, bias=W.get("bo"),
+                           slot=self.slot + ".gemm")
         return out.view(B, 1, s.hidden)
 
     def _run_mlp(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
@@ -151,8 +155,9 @@ class FluidRunner:
         B = hidden.shape[0]
         h = hidden.reshape(B, s.hidden)
         x = kernels.rmsnorm(h, W["ln2"], s.eps, s.norm_mode)
-        act = kernels.gemm(x, W["w_gate_up"], epilogue=_lib.FG_EPI_SWIGLU)
-        out = kernels.gemm(act, W["w_down"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h)
+        act = kernels.gemm(x, W["w_gate_up"], epilogue=_lib.FG_EPI_SWIGLU, slot=self.slot + ".gemm")
+        out = kernels.gemm(act, W["w_down"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h,
+                           slot=self.slot + ".gemm")
         return out.view(B, 1, s.hidden)
 
     def _run_moe_router(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
@@ -188,7 +193,22 @@ class FluidRunner:
         s = self.spec
         B = hidden.shape[0]
         x = kernels.rmsnorm(hidden.reshape(B, s.hidden), self.weights.final_norm, s.eps, s.norm_mode)
-        return kernels.gemm(x, self.weights.lm_head).view(B, 1, s.vocab)
+        return kernels.gemm(x, self.weights.lm_head, slot=self.slot + ".gemm").view(B, 1, s.vocab)
 
     def _skip_head(self, hidden: torch.Tensor) -> torch.Tensor:
         return hidden
+
+    def reserve_workspaces(self, batch: int, plan_len: int) -> None:
+        """Allocate this runner's scratch at the size a step of `batch`
+        sequences planned for `plan_len` tokens needs (before graph capture)."""
+        s = self.spec
+        lib = _lib.lib()
+        windows = {s.window(i) for i in self.layers}
+        attn = max(lib.fg_attn_workspace_bytes(batch, s.n_q, s.n_kv, s.head_dim, plan_len, w)
+                   for w in windows)
+        kernels.Workspace.get(attn, self.device, self.slot + ".attn")
+        shapes = [(s.qkv_width, s.hidden), (s.hidden, s.n_q * s.head_dim), (s.vocab, s.hidden)]
+        if not s.moe:
+            shapes += [(2 * s.intermediate, s.hidden), (s.hidden, s.intermediate)]
+        gemm = max(lib.fg_gemm_workspace_bytes(batch, n, k, 0) for n, k in shapes)
+        kernels.Workspace.get(gemm, self.device, self.slot + ".gemm")

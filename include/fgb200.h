@@ -84,17 +84,32 @@ int fg_rmsnorm(const fg_bf16* x, const fg_bf16* weight, fg_bf16* out, int T, int
  * Replaces the nn.Linear calls q/k/v/o_proj, gate/up/down_proj and lm_head
  * at fluidgpu_torch/runner.py:273-276, :347, :420, :430, :168.
  * K must be a multiple of 8 (16-byte rows); x, w 16-byte aligned.
- * splits = number of K slices (0 = pick automatically); when > 1 the partial
- * sums go through `workspace` (fg_gemm_workspace_bytes bytes, 256-byte
- * aligned). Its first 64 KiB hold split-K tickets: zero them once before the
- * first call; every call leaves them zero again, so one workspace serves
- * calls of any shape in stream order. Calls that overlap on the GPU must not
- * share a workspace. */
+ * The work (output tiles x 64-wide K steps) is spread evenly over a
+ * persistent grid (stream-K); splits = 0 sizes that grid to the SMs,
+ * splits > 0 cuts every tile into about `splits` K slices instead. Tiles
+ * shared by several CTAs are reduced through `workspace`
+ * (fg_gemm_workspace_bytes bytes, 256-byte aligned; 0 means none needed).
+ * The first 64 KiB of the workspace hold reduction tickets: zero them once
+ * before the first call; every call leaves them zero again, so one workspace
+ * serves calls of any shape in stream order. Calls that overlap on the GPU
+ * must not share a workspace. */
 int fg_gemm_bf16(const fg_bf16* x, const fg_bf16* w, fg_bf16* out, const fg_bf16* residual,
                  const fg_bf16* bias, int T, int N, int K, int epilogue, int splits,
                  void* workspace, size_t workspace_bytes, fg_stream_t stream);
-/* Split count fg_gemm_bf16 uses for splits == 0. */
-int fg_gemm_pick_splits(int T, int N, int K);
+/* Same GEMM with the weight in the packed tile layout of fg_pack_weight_bf16:
+ * each CTA then streams whole 16 KB tiles with 1-D bulk copies. */
+int fg_gemm_bf16_packed(const fg_bf16* x, const void* w_packed, fg_bf16* out,
+                        const fg_bf16* residual, const fg_bf16* bias, int T, int N, int K,
+                        int epilogue, int splits, void* workspace, size_t workspace_bytes,
+                        fg_stream_t stream);
+/* Pack a row-major weight w:[N,K] into [ceil(N/128)][ceil(K/64)] tiles of
+ * 128 x 64 bf16 (16 KB), each stored as the 128-byte-swizzled K-major image
+ * the tensor cores read (16-byte chunk c of row r at chunk c ^ (r % 8));
+ * padding is zero. `packed` holds fg_packed_weight_bytes(N, K) bytes. */
+int fg_pack_weight_bf16(const fg_bf16* w, void* packed, int N, int K, fg_stream_t stream);
+size_t fg_packed_weight_bytes(int N, int K);
+/* CTAs fg_gemm_bf16 launches for (T, N, K, splits). */
+int fg_gemm_grid(int T, int N, int K, int splits);
 /* Workspace bytes fg_gemm_bf16 needs for (T, N, K, splits). 0 if none. */
 size_t fg_gemm_workspace_bytes(int T, int N, int K, int splits);
 

@@ -58,7 +58,8 @@ def test_argument_errors_need_no_gpu(lib_path):
     rc = h.fg_paged_decode_attn(1, 1, 1, 1, 1, None, 1, None, 0, 1, 32, 8, 96, 16, 1, 1, 16, 0,
                                 1.0, None)
     assert rc == _lib.FG_ERR_ARG and b"hd must be 64 or 128" in h.fg_last_error()
-    assert h.fg_gemm_workspace_bytes(64, 4096, 4096, 4) > 0
+    assert h.fg_gemm_workspace_bytes(64, 4096, 4096, -7) > 0   # stream-K reduces through it
+    assert h.fg_gemm_workspace_bytes(64, 4096, 4096, 4) == 0   # cluster split-K: on chip
     assert h.fg_gemm_workspace_bytes(64, 4096, 4096, 1) == 0
 
 

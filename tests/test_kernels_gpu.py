@@ -85,15 +85,21 @@ def _gemm_ref(x, w, bias=None):
         (256, 1024, 512, 1),
         (300, 640, 256, 0),      # two token tiles
         (64, 1000, 200, 0),      # K tail inside one 64-wide stage
+        (64, 4096, 4096, 8),     # cluster of 8 CTAs per tile, DSMEM reduction
+        (40, 896, 1024, -7),     # persistent stream-K, 7 CTAs: uneven tile splits
+        (64, 128256 // 8, 4096, 0),  # many tiles: automatic stream-K
+        (200, 640, 512, -5),     # stream-K with two token tiles
     ],
 )
-def test_gemm_store(T, N, K, splits):
+@pytest.mark.parametrize("packed", [True, False])
+def test_gemm_store(T, N, K, splits, packed):
     from fluidgpu_b200 import kernels
 
     g = _gen(2)
     x = _randn((T, K), g)
     w = _randn((N, K), g, 0.05)
-    out = kernels.gemm(x.to(DEV), w.to(DEV), splits=splits).cpu()
+    wd = kernels.PackedWeight(w.to(DEV)) if packed else w.to(DEV)
+    out = kernels.gemm(x.to(DEV), wd, splits=splits).cpu()
     exp = _gemm_ref(x, w)
     err = (out.float() - exp).abs().max().item()
     assert err <= 1e-2 * exp.abs().max().item() + 1e-3, err
@@ -108,8 +114,9 @@ def test_gemm_bias_residual():
     w = _randn((N, K), g, 0.02)
     b = _randn((N,), g, 0.1)
     r = _randn((T, N), g)
-    for splits in (1, 4):
-        out = kernels.gemm(x.to(DEV), w.to(DEV), epilogue=1, residual=r.to(DEV), bias=b.to(DEV),
+    for splits, wd in ((1, w.to(DEV)), (4, w.to(DEV)), (0, kernels.PackedWeight(w.to(DEV))),
+                       (3, kernels.PackedWeight(w.to(DEV))), (-11, kernels.PackedWeight(w.to(DEV)))):
+        out = kernels.gemm(x.to(DEV), wd, epilogue=1, residual=r.to(DEV), bias=b.to(DEV),
                            splits=splits).cpu()
         exp = r.float() + _gemm_ref(x, w, b).to(torch.bfloat16).float()
         err = (out.float() - exp).abs().max().item()
@@ -117,7 +124,7 @@ def test_gemm_bias_residual():
 
 
 @pytest.mark.parametrize("T,I,K,splits", [(64, 14336, 4096, 0), (8, 2816, 1024, 0), (5, 128, 64, 1),
-                                           (64, 512, 4096, 4)])
+                                           (64, 512, 4096, 4), (64, 512, 4096, -9), (64, 2816, 1024, 6)])
 def test_gemm_swiglu(T, I, K, splits):
     from fluidgpu_b200 import kernels
 
@@ -127,12 +134,54 @@ def test_gemm_swiglu(T, I, K, splits):
     wu = _randn((I, K), g, 0.02)
     # gate/up interleaved in blocks of 64 rows
     w = torch.stack([wg.view(I // 64, 64, K), wu.view(I // 64, 64, K)], dim=1).reshape(2 * I, K)
-    out = kernels.gemm(x.to(DEV), w.to(DEV), epilogue=2, splits=splits).cpu()
+    out = kernels.gemm(x.to(DEV), kernels.PackedWeight(w.to(DEV)), epilogue=2, splits=splits).cpu()
+    out2 = kernels.gemm(x.to(DEV), w.to(DEV), epilogue=2, splits=splits).cpu()
+    assert torch.equal(out, out2)  # same tiles, same order: packed == row-major bit for bit
     gate = _gemm_ref(x, wg).to(torch.bfloat16)
     up = _gemm_ref(x, wu).to(torch.bfloat16)
     exp = ref.silu_mul(gate, up).float()
     err = (out.float() - exp).abs().max().item()
     assert err <= 2e-2 * exp.abs().max().item() + 1e-4, err
+
+
+def test_pack_weight_layout():
+    """Packed tile (nt, kb): 16-byte chunk c of row r sits at chunk c ^ (r % 8)."""
+    from fluidgpu_b200 import kernels
+
+    g = _gen(9)
+    N, K = 200, 136  # ragged in both dimensions
+    w = _randn((N, K), g)
+    pw = kernels.PackedWeight(w.to(DEV))
+    data = pw.data.cpu().view(torch.bfloat16).view(2, 3, 128, 8, 8)  # [nt][kb][row][slot][8]
+    for nt in range(2):
+        for kb in range(3):
+            for r in (0, 5, 71, 127):
+                for c in range(8):
+                    n, k = nt * 128 + r, kb * 64 + c * 8
+                    got = data[nt, kb, r, c ^ (r % 8)]
+                    exp = w[n, k:k + 8] if (n < N and k < K) else torch.zeros(8, dtype=torch.bfloat16)
+                    assert torch.equal(got, exp), (nt, kb, r, c)
+
+
+def test_gemm_chain_with_pdl():
+    """Back-to-back dependent GEMMs and norms (programmatic dependent launch):
+    each result feeds the next call; compare the whole chain to torch."""
+    from fluidgpu_b200 import kernels
+
+    g = _gen(10)
+    T, H, I = 64, 1024, 2048
+    x = _randn((T, H), g)
+    ws = [_randn((I, H), g, 0.03), _randn((H, I), g, 0.03), _randn((I, H), g, 0.03)]
+    pw = [kernels.PackedWeight(w.to(DEV)) for w in ws]
+    h = x.to(DEV)
+    ref_h = x.float()
+    for it in range(3):
+        a = kernels.gemm(h, pw[0])
+        h = kernels.gemm(a, pw[1], epilogue=1, residual=h)
+        ref_a = (ref_h.to(torch.bfloat16).float() @ ws[0].float().T).to(torch.bfloat16).float()
+        ref_h = (ref_h + (ref_a @ ws[1].float().T).to(torch.bfloat16).float()).to(torch.bfloat16).float()
+    err = (h.cpu().float() - ref_h).abs().max().item()
+    assert err <= 3e-2 * ref_h.abs().max().item(), err
 
 
 # ---------------------------------------------------------------------------

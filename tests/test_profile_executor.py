@@ -116,7 +116,7 @@ def test_reference_layer_plan_format_loads(tmp_path):
     (lambda r: r["tasks"].__setitem__(0, {**r["tasks"][0], "rank": 1}), "embed must be assigned to rank 0"),
     (lambda r: r.__setitem__("dtype", "float32"), "bfloat16"),
     (lambda r: r["tasks"].pop(1), "supported attention/feed-forward task sequence"),
-    (lambda r: r["tasks"][2].__setitem__("decode_rank", 1), "decode_rank is only supported"),
+    (lambda r: r["tasks"][1].__setitem__("decode_rank", 1), "decode_rank is only supported"),
 ])
 def test_plan_validation_errors(mutate, msg):
     raw = attn_ffn_profile("m", 1, 4, 2, 2, 8)
