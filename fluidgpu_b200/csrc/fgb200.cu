@@ -5,3 +5,4 @@
 #include "elementwise.cuh"
 #include "gemm.cuh"
 #include "attention.cuh"
+#include "attention_noalloc.cuh"

@@ -159,6 +159,22 @@ int fg_attn_pages_per_split(int B, int nkv, int max_seq_len, int window);
 /* Workspace bytes fg_paged_decode_attn needs for these sizes (0 if none). */
 size_t fg_attn_workspace_bytes(int B, int nq, int nkv, int hd, int max_seq_len, int window);
 
+/* Paged decode attention for callers that cannot allocate device memory (a
+ * runtime that owns all device memory through its own pool and refuses
+ * cudaMalloc while serving, or an FFI binding without a device allocator).
+ * No counterpart in the reference: it exists for such hosts. Same arguments
+ * and results as fg_paged_decode_attn, minus the workspace: the split
+ * scratch is a built-in 8 MiB device array that every GPU loading this
+ * library holds until exit. The first call on a device resolves that
+ * array's address (make it before any stream capture); calls needing more
+ * than 8 MiB (fg_attn_workspace_bytes) fail with FG_ERR_ARG; calls share
+ * the array, so calls that overlap on the GPU race. Allocates nothing. */
+int fg_paged_decode_attn_noalloc(const fg_bf16* q, const fg_bf16* k_cache, const fg_bf16* v_cache,
+                                 const int32_t* block_table, const int32_t* seq_lens,
+                                 const float* sinks, fg_bf16* out, int B, int nq, int nkv, int hd,
+                                 int block_size, int num_blocks, int max_blocks, int max_seq_len,
+                                 int window, float scale, fg_stream_t stream);
+
 /* Greedy token: out[t] = argmax_v logits[t, v] (lowest index on ties), the
  * argmax the reference engine takes after norm_lm_head (engine.py:295-300,
  * :337-343). */
