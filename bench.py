@@ -43,6 +43,11 @@ METRIC = "decode tokens/s"
 CONFIG = {"workload": "llama-3-8b decode step, batch 64, prompt 4096, paged KV block 16 (BASELINE configs[1])",
           "model": "llama-3-8b (random init)", "batch_per_gpu": 64, "context": 4096,
           "block_size": 16, "l2": "inputs larger than L2 (KV ~35 GB, weights ~16 GB per GPU)"}
+CONFIG_GPTOSS = {"workload": "gpt-oss-20b decode step, batch 128, prompt 4096, paged KV block 16, "
+                             "MXFP4 experts (BASELINE configs[2] on one GPU)",
+                 "model": "gpt-oss-20b (random init, MXFP4 experts)", "batch_per_gpu": 128,
+                 "context": 4096, "block_size": 16,
+                 "l2": "inputs larger than L2 (KV ~26 GB, experts ~10 GB per GPU)"}
 
 
 def dist_env():
@@ -181,11 +186,12 @@ def run_fgb200(args) -> None:
     from fluidgpu_b200 import build, kernels
     from fluidgpu_b200.config import EngineConfig
     from fluidgpu_b200.engine import DecodeEngine
-    from fluidgpu_b200.model import LLAMA3_8B, ModelWeights
+    from fluidgpu_b200.model import GPT_OSS_20B, LLAMA3_8B, ModelWeights
 
     build.build()
-    spec = LLAMA3_8B
-    B, ctx = args.batch, args.context
+    spec = GPT_OSS_20B if args.model == "gpt-oss-20b" else LLAMA3_8B
+    config = CONFIG_GPTOSS if args.model == "gpt-oss-20b" else CONFIG
+    B, ctx = (args.batch or config["batch_per_gpu"]), args.context
     W, K = args.warmup, args.steps
     R = 3  # replays of the attention-timed graph
     total = ctx + W + 2 * K + R + 8
@@ -248,7 +254,8 @@ def run_fgb200(args) -> None:
     tot_bytes, tot_ms = 0.0, 0.0
     for i, (d, meta) in enumerate(attn):
         step = i // spec.num_layers
-        lens_sum = sum(l + 1 + step for l in lens0[:B])
+        win = meta["window"]
+        lens_sum = sum(min(l + 1 + step, win) if win else l + 1 + step for l in lens0[:B])
         tot_bytes += attn_bytes(meta, lens_sum)
         tot_ms += d
     attn_launch_ms = tot_ms / max(len(attn), 1)
@@ -294,7 +301,8 @@ def run_fgb200(args) -> None:
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {**CONFIG, "parallelism": f"dp{world} (attention data-parallel by request, FFN co-located)"},
+            "config": {**config, "batch_per_gpu": B,
+                       "parallelism": f"dp{world} (attention data-parallel by request, FFN co-located)"},
             "e2e": {"value": world * B * K / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8},
             "roofline": {"bound": "hbm", "kernel": "fg_paged_decode_attn", "achieved": achieved,
@@ -308,7 +316,7 @@ def run_fgb200(args) -> None:
             "host_enqueue_ms_per_step": host_ms,
             "clocks": clocks,
         }
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and spec is LLAMA3_8B:
             line["cpu_baseline"] = cpu_baseline_sample(B, ctx)
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -322,7 +330,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="fgb200", choices=["fgb200", "reference"])
-    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--batch", type=int, default=0, help="sequences per GPU (default: the model's config)")
+    ap.add_argument("--model", default="llama-3-8b", choices=["llama-3-8b", "gpt-oss-20b"])
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch every kernel from the host (no CUDA graph)")

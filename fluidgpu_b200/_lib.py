@@ -27,6 +27,7 @@ FG_ERR_PEER = 4
 FG_EPI_STORE = 0
 FG_EPI_RESIDUAL = 1
 FG_EPI_SWIGLU = 2
+FG_EPI_SWIGLU_OAI = 3
 
 FG_NORM_LLAMA = 0
 FG_NORM_FP32MUL = 1
@@ -65,7 +66,19 @@ SIGNATURES: dict[str, tuple] = {
     "fg_attn_pages_per_split": (c_int, [c_int, c_int, c_int, c_int]),
     "fg_attn_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
     "fg_argmax": (c_int, [_P, _P, c_int, c_int, _P]),
+    "fg_moe_router_topk": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P, _P, _P]),
+    "fg_moe_tile_tokens": (c_int, [c_int, c_int, c_int]),
+    "fg_moe_max_items": (c_int, [c_int, c_int, c_int, c_int]),
+    "fg_moe_permute": (c_int, [_P, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P, _P]),
+    "fg_moe_gather": (c_int, [_P, _P, c_int, c_int, c_int, _P, _P]),
+    "fg_pack_mxfp4": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P]),
+    "fg_mxfp4_packed_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "fg_moe_gemm_mxfp4": (
+        c_int, [_P, _P, _P, _P, _P, _P, c_int, _P, c_int, c_int, c_int, c_int, c_int, _P],
+    ),
+    "fg_moe_unpermute": (c_int, [_P, _P, _P, _P, _P, _P, c_int, c_int, c_int, _P]),
     "fg_advance": (c_int, [_P, _P, c_int, _P]),
+    "fg_add_bf16": (c_int, [_P, _P, _P, ctypes.c_longlong, _P]),
 }
 
 

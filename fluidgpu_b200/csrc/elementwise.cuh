@@ -231,6 +231,26 @@ __global__ void kv_append_kernel(const uint4* __restrict__ k, const uint4* __res
   for (int i = threadIdx.x; i < hd8; i += blockDim.x) dst[i] = src[i];
 }
 
+// out = bf16(a + b), 8 elements per thread
+__global__ void add_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
+                           uint4* __restrict__ out, long long n8) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  const uint4 x = a[i], y = b[i];
+  const uint32_t* px = reinterpret_cast<const uint32_t*>(&x);
+  const uint32_t* py = reinterpret_cast<const uint32_t*>(&y);
+  uint4 o;
+  uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float2 fx = unpack_bf16x2(px[q]), fy = unpack_bf16x2(py[q]);
+    po[q] = pack_bf16x2(fx.x + fy.x, fx.y + fy.y);
+  }
+  out[i] = o;
+}
+
 __global__ void advance_kernel(int32_t* positions, int32_t* seq_lens, int B) {
   griddep_wait();
   griddep_launch_dependents();
@@ -318,6 +338,18 @@ int fg_argmax(const fg_bf16* logits, int64_t* out, int T, int V, fg_stream_t str
   if (T == 0) return FG_OK;
   return fg::launch_k("fg_argmax", fg::argmax_kernel<1024>, dim3(T), dim3(1024), 0,
                       (cudaStream_t)stream, reinterpret_cast<const __nv_bfloat16*>(logits), out, V);
+}
+
+int fg_add_bf16(const fg_bf16* a, const fg_bf16* b, fg_bf16* out, long long n, fg_stream_t stream) {
+  FG_REQUIRE(a && b && out, "fg_add_bf16: null pointer");
+  FG_REQUIRE(n >= 0 && n % 8 == 0, "fg_add_bf16: n=%lld must be a multiple of 8", n);
+  FG_REQUIRE((((uintptr_t)a | (uintptr_t)b | (uintptr_t)out) & 15) == 0,
+             "fg_add_bf16: pointers must be 16-byte aligned");
+  if (n == 0) return FG_OK;
+  const long long n8 = n / 8;
+  return fg::launch_k("fg_add_bf16", fg::add_kernel, dim3((unsigned)((n8 + 255) / 256)), dim3(256), 0,
+                      (cudaStream_t)stream, reinterpret_cast<const uint4*>(a),
+                      reinterpret_cast<const uint4*>(b), reinterpret_cast<uint4*>(out), n8);
 }
 
 int fg_advance(int32_t* positions, int32_t* seq_lens, int B, fg_stream_t stream) {

@@ -6,3 +6,4 @@
 #include "gemm.cuh"
 #include "attention.cuh"
 #include "attention_noalloc.cuh"
+#include "moe.cuh"

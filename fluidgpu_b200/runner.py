@@ -54,6 +54,9 @@ class FluidRunner:
         self._moe_states: dict[int, dict[str, torch.Tensor]] = {}
         # scratch slots of this runner (runners on other streams use their own)
         self.slot = f"runner{id(self):x}"
+        # MoE routing of the last step per layer (tests compare it with the oracle)
+        self.record_routing = False
+        self.last_routing: dict[int, torch.Tensor] = {}
 
     # -- sequence admission ---------------------------------------------------
     def start(self, batch: int, prompt_lens: list[int] | None = None,
@@ -115,8 +118,6 @@ class FluidRunner:
             out = self.executor.run_kernel_group(f"layer_{i}_mlp", self._run_mlp, hidden,
                                                  mode="decode", seq_len=1, batch=B, layer=i)
             return out if out is not None else hidden
-        from . import moe
-
         for suffix, fn in (("moe_router", self._run_moe_router), ("moe_experts", self._run_moe_experts),
                            ("moe_combine", self._run_moe_combine)):
             out = self.executor.run_kernel_group(f"layer_{i}_{suffix}", fn, hidden, mode="decode",
@@ -168,24 +169,35 @@ class FluidRunner:
         B = hidden.shape[0]
         h = hidden.reshape(B, s.hidden)
         x = kernels.rmsnorm(h, W["ln2"], s.eps, s.norm_mode)
-        weights, idx = moe.router_topk(x, W["router_w"], W["router_b"], s.top_k)
+        weights, idx = moe.router_topk(x, W["router_w"], W.get("router_b"), s.top_k)
         self._moe_states[layer] = {"residual": h, "weights": weights, "indices": idx}
+        if self.record_routing:
+            self.last_routing[layer] = idx
         return x.view(B, 1, s.hidden)
 
     def _run_moe_experts(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
         from . import moe
 
         s = self.spec
-        st = self._moe_states[layer]
+        st = self._moe_states.get(layer)
+        assert st is not None, (
+            f"layer {layer}: moe_experts needs the router state on this rank "
+            "(router and experts groups must share a rank)")
         B = hidden.shape[0]
+        # the combine group's residual add is fused when it runs here too
+        fuse = self.executor.task_rank(f"layer_{layer}_moe_combine", "decode") == self.executor.my_rank
         y = moe.experts_forward(hidden.reshape(B, s.hidden), st["indices"], st["weights"],
-                                self.weights.layers[layer], s)
+                                self.weights.layers[layer], s,
+                                residual=st["residual"] if fuse else None)
+        st["fused"] = fuse
         return y.view(B, 1, s.hidden)
 
     def _run_moe_combine(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
         from . import moe
 
         st = self._moe_states.pop(layer)
+        if st.get("fused"):
+            return hidden
         B = hidden.shape[0]
         return moe.residual_add(st["residual"], hidden.reshape(B, -1)).view(B, 1, -1)
 

@@ -41,6 +41,7 @@ typedef struct CUstream_st* fg_stream_t; /* == cudaStream_t */
 #define FG_EPI_STORE 0     /* out[t,n] = bf16(acc (+ bias)) */
 #define FG_EPI_RESIDUAL 1  /* out[t,n] = bf16(residual[t,n] + bf16(acc (+ bias))) */
 #define FG_EPI_SWIGLU 2    /* out[t,j] = bf16(silu(g) * u), g/u rows interleaved per 64 */
+#define FG_EPI_SWIGLU_OAI 3 /* gpt-oss: (clamp(u,-7,7)+1) * g' * sigmoid(1.702 g'), g' = min(g,7) */
 
 /* RMSNorm weight application (fg_rmsnorm) */
 #define FG_NORM_LLAMA 0    /* w * bf16(x * rstd)    (LlamaRMSNorm)  */
@@ -179,6 +180,57 @@ int fg_paged_decode_attn_noalloc(const fg_bf16* q, const fg_bf16* k_cache, const
  * argmax the reference engine takes after norm_lm_head (engine.py:295-300,
  * :337-343). */
 int fg_argmax(const fg_bf16* logits, int64_t* out, int T, int V, fg_stream_t stream);
+
+/* ---- gpt-oss MoE feed-forward (runner.py:432-457 moe_router / moe_experts /
+ * moe_combine; GptOssMLP semantics; vllm_integration.py:452-485) -------- */
+
+/* Router: logits[t,e] = bf16(x[t] . w[e] + bias[e]) (w:[E,H]), top-k by value
+ * (ties: lower expert id), weights = bf16(softmax over the k selected logits).
+ * weights,indices:[T,k]; logits:[T,E] or NULL. E <= 64, k <= 8. */
+int fg_moe_router_topk(const fg_bf16* x, const fg_bf16* w, const fg_bf16* bias, int T, int H, int E,
+                       int k, fg_bf16* weights, int32_t* indices, fg_bf16* logits,
+                       fg_stream_t stream);
+/* Token tile (16/32/64) the expert GEMMs use for T tokens, and the bound on
+ * (expert, token tile) work items fg_moe_permute emits. */
+int fg_moe_tile_tokens(int T, int k, int E);
+int fg_moe_max_items(int T, int k, int E, int BN);
+/* Deterministic counting sort of the T*k (token, slot) pairs by expert:
+ * offsets:[E+1] rows of each expert; perm_pair:[T*k] pair id (t*k+j) of each
+ * permuted row (pairs of one expert stay in (t, j) order); inv:[T*k] row of
+ * each pair; items:[fg_moe_max_items][2] (expert, token tile), item_count:[1]. */
+int fg_moe_permute(const int32_t* indices, int T, int k, int E, int BN, int32_t* offsets,
+                   int32_t* perm_pair, int32_t* inv, int32_t* items, int32_t* item_count,
+                   fg_stream_t stream);
+/* out[i,:] = x[perm_pair[i] / k, :] for the T*k permuted rows. */
+int fg_moe_gather(const fg_bf16* x, const int32_t* perm_pair, int T, int k, int H, fg_bf16* out,
+                  fg_stream_t stream);
+/* Pack MXFP4 expert weights: values:[E][N][K/2] (e2m1 pairs, low nibble =
+ * even k), scales:[E][N][K/32] (e8m0) -> records of 128 rows x 64 K
+ * (4096 B values + 256 B scales), fg_mxfp4_packed_bytes(E,N,K) bytes. */
+int fg_pack_mxfp4(const uint8_t* values, const uint8_t* scales, void* packed, int E, int N, int K,
+                  fg_stream_t stream);
+size_t fg_mxfp4_packed_bytes(int E, int N, int K);
+/* Grouped expert GEMM on tcgen05: for every work item (expert e, token tile),
+ * acc = x[rows of e] . dequant(W_e)^T with W_e packed MXFP4 [N,K], dequantised
+ * to bf16 in shared memory (exactly as transformers dequantises MXFP4), fp32
+ * accumulation; epilogue FG_EPI_STORE (+ bias[e]) -> out:[rows,N], or
+ * FG_EPI_SWIGLU_OAI (+ bias, gate/up rows interleaved per 64) -> out:[rows,N/2].
+ * Only experts that received tokens read their weights. */
+int fg_moe_gemm_mxfp4(const fg_bf16* x, const void* w_packed, const fg_bf16* bias,
+                      const int32_t* offsets, const int32_t* items, const int32_t* item_count,
+                      int max_items, fg_bf16* out, int rows, int N, int K, int BN, int epilogue,
+                      fg_stream_t stream);
+/* out[t] = residual[t] + sum over the k slots in ascending expert id of
+ * bf16(y[inv[t*k+j]] * weights[t,j]), each addition rounded to bf16 (the
+ * index_add_ order of GptOssExperts.forward); residual may be NULL. */
+int fg_moe_unpermute(const fg_bf16* y, const int32_t* inv, const int32_t* indices,
+                     const fg_bf16* weights, const fg_bf16* residual, fg_bf16* out, int T, int k,
+                     int H, fg_stream_t stream);
+
+/* out = bf16(a + b) over n bf16 elements (n % 8 == 0): the residual add of
+ * the moe_combine group (runner.py:454-457) when it runs apart from the
+ * experts group (otherwise fg_moe_unpermute fuses it). */
+int fg_add_bf16(const fg_bf16* a, const fg_bf16* b, fg_bf16* out, long long n, fg_stream_t stream);
 
 /* positions[b] += 1 and seq_lens[b] += 1 after a decode step
  * (LayerKVCache.advance, kv_cache.py:140-144). Either pointer may be NULL. */

@@ -1,0 +1,214 @@
+"""gpt-oss MoE on the B200: router top-k, permute, MXFP4 grouped GEMMs and
+un-permute against the CPU oracle / plain torch, then a whole gpt-oss-style
+decode (sinks, sliding window, YaRN, MXFP4 experts) against the oracle.
+
+Router indices are integer results and must match exactly; the only allowed
+difference is a near tie at the k-th place (two bf16 logits within one
+bf16 ulp, where fp32 summation order can round either way)."""
+import pytest
+import torch
+
+from oracle import decode_ref as ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    from fluidgpu_b200 import build
+
+    build.build()
+    yield
+    from fluidgpu_b200 import kernels
+
+    kernels.check_device("moe tests")
+
+
+def _g(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+@pytest.mark.parametrize("T,H,E,k", [(128, 2880, 32, 4), (7, 256, 8, 2), (64, 512, 64, 8), (1, 64, 4, 1)])
+def test_router_topk(T, H, E, k):
+    from fluidgpu_b200 import moe
+
+    g = _g(1)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w = (torch.randn(E, H, generator=g) * 0.05).to(torch.bfloat16)
+    b = (torch.randn(E, generator=g) * 0.1).to(torch.bfloat16)
+    wts, idx, lg = moe.router_topk(x.to(DEV), w.to(DEV), b.to(DEV), k, logits=True)
+    exp_logits = torch.nn.functional.linear(x, w, b)  # bf16 linear, as the reference's router
+    assert (lg.cpu().float() - exp_logits.float()).abs().max() <= 2 * 2 ** -8 * exp_logits.float().abs().max()
+    top_v, top_i = ref.topk_lowest(lg.cpu().float(), k)  # selection on the kernel's own logits: exact
+    assert torch.equal(idx.cpu().long(), top_i)
+    exp_w = torch.softmax(top_v, dim=-1).to(torch.bfloat16)
+    assert torch.equal(wts.cpu(), exp_w)
+    # against the oracle's logits: equal unless a one-ulp near tie at the boundary
+    ov, oi = ref.topk_lowest(exp_logits.float(), k)
+    for t in range(T):
+        if not torch.equal(oi[t], idx[t].cpu().long()):
+            srt = exp_logits[t].float().sort(descending=True).values
+            gap = (srt[k - 1] - srt[k]).abs().item() if k < E else 1.0
+            assert gap <= 2 ** -7 * srt[0].abs().item(), f"token {t}: router indices differ without a tie"
+
+
+@pytest.mark.parametrize("T,k,E", [(128, 4, 32), (5, 2, 8), (300, 4, 32), (64, 8, 64)])
+def test_permute_exact(T, k, E):
+    from fluidgpu_b200 import moe
+
+    g = _g(2)
+    idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    if T > 100:
+        idx[: T // 2, 0] = 3  # a hot expert: several token tiles
+    r = moe.Routing(idx.to(DEV), E)
+    flat = idx.reshape(-1).long()
+    counts = torch.bincount(flat, minlength=E)
+    offsets = torch.cat([torch.zeros(1, dtype=torch.long), counts.cumsum(0)])
+    assert torch.equal(r.offsets.cpu().long(), offsets)
+    exp_perm = torch.argsort(flat * (T * k) + torch.arange(T * k), stable=True)
+    assert torch.equal(r.perm_pair.cpu().long(), exp_perm)
+    inv = torch.empty_like(exp_perm)
+    inv[exp_perm] = torch.arange(T * k)
+    assert torch.equal(r.inv.cpu().long(), inv)
+    items = [(e, t) for e in range(E) for t in range((int(counts[e]) + r.BN - 1) // r.BN)]
+    n = int(r.item_count.item())
+    assert n == len(items)
+    assert r.items.cpu().view(-1, 2)[:n].tolist() == [list(x) for x in items]
+
+
+def _ref_expert_gemm(x_perm, deq_w, bias, offsets, epilogue):
+    """fp32 reference of the grouped GEMM on the dequantised (exact bf16) weights."""
+    out = []
+    for e in range(deq_w.shape[0]):
+        xs = x_perm[offsets[e]:offsets[e + 1]].float()
+        y = xs @ deq_w[e].float().T + bias[e].float()
+        if epilogue == "swiglu_oai":
+            y = y.to(torch.bfloat16).float()
+            I = y.shape[1] // 2
+            g, u = y.view(-1, I // 64, 2, 64)[:, :, 0].reshape(-1, I), y.view(-1, I // 64, 2, 64)[:, :, 1].reshape(-1, I)
+            y = ref.swiglu_oai(g.to(torch.bfloat16), u.to(torch.bfloat16)).float()
+        out.append(y)
+    return torch.cat(out)
+
+
+@pytest.mark.parametrize("T,k,E,H,I", [(128, 4, 32, 2880, 2880), (9, 2, 8, 256, 512), (40, 4, 16, 512, 256)])
+def test_grouped_mxfp4_gemms(T, k, E, H, I):
+    from fluidgpu_b200 import _lib, moe
+
+    g = _g(3)
+    w1 = torch.randn(E, 2 * I, H, generator=g) * 0.02      # already 64-interleaved order here
+    w2 = torch.randn(E, H, I, generator=g) * 0.02
+    b1 = (torch.randn(E, 2 * I, generator=g) * 0.1).to(torch.bfloat16)
+    b2 = (torch.randn(E, H, generator=g) * 0.1).to(torch.bfloat16)
+    v1, s1 = moe.quantize_mxfp4(w1.to(DEV))
+    v2, s2 = moe.quantize_mxfp4(w2.to(DEV))
+    d1 = moe.dequantize_mxfp4(v1, s1).cpu()
+    d2 = moe.dequantize_mxfp4(v2, s2).cpu()
+    # the product quantiser agrees with the oracle's restatement
+    ov, os_ = ref.mxfp4_quantize(w1[:2, :128])
+    assert torch.equal(ref.mxfp4_dequantize(ov, os_), d1[:2, :128])
+    p1, p2 = moe.pack_mxfp4(v1, s1), moe.pack_mxfp4(v2, s2)
+    idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    r = moe.Routing(idx.to(DEV), E)
+    x_perm = x[r.perm_pair.cpu().long() // k]
+    offsets = r.offsets.cpu().tolist()
+    act = moe.grouped_gemm(x_perm.to(DEV).contiguous(), p1, b1.to(DEV), r, 2 * I, H, _lib.FG_EPI_SWIGLU_OAI)
+    exp_act = _ref_expert_gemm(x_perm, d1, b1, offsets, "swiglu_oai")
+    err = (act.cpu().float() - exp_act).abs().max().item()
+    assert err <= 2e-2 * exp_act.abs().max().item() + 1e-3, err
+    y = moe.grouped_gemm(act, p2, b2.to(DEV), r, H, I, _lib.FG_EPI_STORE)
+    exp_y = _ref_expert_gemm(act.cpu(), d2, b2, offsets, "store")
+    err = (y.cpu().float() - exp_y).abs().max().item()
+    assert err <= 1e-2 * exp_y.abs().max().item() + 1e-3, err
+
+
+def test_unpermute_order_and_residual():
+    from fluidgpu_b200 import _lib, moe
+
+    g = _g(4)
+    T, k, E, H = 33, 4, 16, 256
+    idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    wts = torch.softmax(torch.randn(T, k, generator=g), -1).to(torch.bfloat16)
+    r = moe.Routing(idx.to(DEV), E)
+    y = torch.randn(T * k, H, generator=g).to(torch.bfloat16)
+    res = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=DEV)
+    yd, idxd, wd, rd = y.to(DEV), idx.to(DEV), wts.to(DEV), res.to(DEV)  # keep the device copies alive
+    _lib.call("fg_moe_unpermute", yd.data_ptr(), r.inv.data_ptr(), idxd.data_ptr(), wd.data_ptr(),
+              rd.data_ptr(), out.data_ptr(), T, k, H, torch.cuda.current_stream().cuda_stream)
+    inv = r.inv.cpu().long()
+    exp = torch.zeros(T, H, dtype=torch.bfloat16)
+    for t in range(T):
+        for j in sorted(range(k), key=lambda j: int(idx[t, j])):  # index_add_ order: ascending expert
+            exp[t] += y[inv[t * k + j]] * wts[t, j]
+    exp = res + exp
+    assert torch.equal(out.cpu(), exp)
+
+
+def _tiny_gptoss(seed=0):
+    from transformers.models.gpt_oss import GptOssConfig, GptOssForCausalLM
+
+    from fluidgpu_b200 import moe
+
+    torch.manual_seed(seed)
+    cfg = GptOssConfig(num_hidden_layers=2, num_local_experts=8, vocab_size=1024, hidden_size=512,
+                       intermediate_size=256, head_dim=64, num_attention_heads=8, num_key_value_heads=2,
+                       sliding_window=16, num_experts_per_tok=2,
+                       layer_types=["sliding_attention", "full_attention"], max_position_embeddings=4096)
+    cfg._attn_implementation = "eager"
+    model = GptOssForCausalLM(cfg).to(torch.bfloat16).eval()
+    with torch.no_grad():
+        for layer in model.model.layers:
+            ex = layer.mlp.experts
+            # make the experts MXFP4-exact (a real gpt-oss checkpoint is MXFP4)
+            for name in ("gate_up_proj", "down_proj"):
+                p = getattr(ex, name)
+                wt = p.data.transpose(1, 2).float()
+                v, s = moe.quantize_mxfp4(wt)
+                p.data.copy_(moe.dequantize_mxfp4(v, s).transpose(1, 2).to(p.dtype))
+            layer.mlp.router.weight.data.normal_(0, 0.2)  # spread router logits
+            layer.self_attn.sinks.data.normal_(0, 1.0)
+    return model
+
+
+def test_gpt_oss_decode_matches_oracle():
+    from fluidgpu_b200 import kernels
+    from fluidgpu_b200.config import EngineConfig
+    from fluidgpu_b200.engine import DecodeEngine
+    from fluidgpu_b200.model import ModelWeights
+
+    model = _tiny_gptoss()
+    w = ModelWeights.from_hf(model, DEV)
+    batch, prompt, steps = 4, 20, 12
+    eng = DecodeEngine(w, EngineConfig(model_name="tiny-gpt-oss", max_seq_len=64, world_size=1,
+                                       device="cuda:0", max_batch=batch))
+    eng.runner.record_routing = True
+    spec = ref.spec_from_hf(model.config)
+    wo = ref.weights_from_hf(model)
+    truth = ref.OracleModel(spec, {k: v.float() for k, v in wo.items()}, torch.float32)
+    bf16 = ref.OracleModel(spec, wo, torch.bfloat16)
+    g = _g(5)
+    prompts = torch.randint(0, 1024, (batch, prompt), generator=g)
+    eng.start(batch, reserve_tokens=prompt + steps + 2)
+    truth.reset(batch)
+    bf16.reset(batch)
+    tie_flips = 0
+    for t in range(prompt + steps):
+        tok = prompts[:, t] if t < prompt else ref.argmax_lowest(lt.float())
+        got = eng.runner.decode_step(tok.to(DEV)).reshape(batch, -1).float().cpu()
+        lt = truth.step(tok)
+        lb = bf16.step(tok)
+        err = (got - lt).abs()
+        ref_err = (lb.float() - lt).abs().max().item()
+        excess = (err - (2e-2 + 1e-2 * lt.abs())).max().item()
+        assert excess <= 0 or err.max().item() <= 1.25 * ref_err + 1e-3, (t, err.max().item(), ref_err)
+        # router indices: identical to the bf16 oracle's, barring one-ulp near ties
+        for layer in range(spec.num_layers):
+            gi = eng.runner.last_routing[layer].cpu().long()
+            oi = bf16.router_indices[layer]
+            if not torch.equal(torch.sort(gi, -1).values, torch.sort(oi, -1).values):
+                tie_flips += 1
+    assert tie_flips <= 2, f"{tie_flips} router decisions differ"
+    kernels.check_device("gpt-oss decode")
