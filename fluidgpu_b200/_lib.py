@@ -79,6 +79,12 @@ SIGNATURES: dict[str, tuple] = {
     "fg_moe_unpermute": (c_int, [_P, _P, _P, _P, _P, _P, c_int, c_int, c_int, _P]),
     "fg_advance": (c_int, [_P, _P, c_int, _P]),
     "fg_add_bf16": (c_int, [_P, _P, _P, ctypes.c_longlong, _P]),
+    "fg_mailbox_bytes": (c_size_t, [c_int, c_int, c_size_t]),
+    "fg_ipc_export": (c_int, [_P, _P, ctypes.POINTER(c_size_t)]),
+    "fg_ipc_import": (c_int, [_P, c_size_t, ctypes.POINTER(c_void_p)]),
+    "fg_ipc_close": (c_int, [_P, c_size_t]),
+    "fg_handoff_put": (c_int, [_P, c_size_t, _P, _P, c_int, c_int, c_int, c_int, c_size_t, c_int, _P]),
+    "fg_handoff_recv": (c_int, [_P, c_size_t, _P, _P, c_int, c_int, c_int, c_int, c_size_t, c_int, _P]),
 }
 
 

@@ -7,3 +7,4 @@
 #include "attention.cuh"
 #include "attention_noalloc.cuh"
 #include "moe.cuh"
+#include "handoff.cuh"

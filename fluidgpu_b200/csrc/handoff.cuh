@@ -1,0 +1,296 @@
+// Hidden-state hand-off between the ranks of one NVLink node: the B200
+// replacement of the reference's NCCL send/recv at task boundaries
+// (executor.py:104-123, comm.py:24-46) and of the native runtime's
+// IPC-buffer + flag and RDMA-write + flag handlers (comm_backend.cu:92-381,
+// :1078-1187), whose device polling kernels spin without bound
+// (comm_backend.cu:31-57).
+//
+// Mailbox (one allocation per rank, in that rank's HBM, mapped by every peer
+// through CUDA IPC; all words 128-byte aligned):
+//   data  [world][nslot][slot_bytes]   written by the sender (peer stores)
+//   flags [world][nslot] u32           slot sequence number, sender-released
+//   acks  [world][nslot] u32           acks of what THIS rank sent to each
+//                                      peer, written remotely by the receiver
+//   send_seq [world] u32, recv_seq [world] u32, tickets [2*world] u32 (local)
+// Channel src -> dst uses dst's data[src][*] / flags[src][*] and src's
+// acks[dst][*]. Message n of a channel goes to slot n % nslot.
+//
+// fg_handoff_put (on src): wait until acks[dst][slot] >= n - nslot (the
+// receiver has drained the slot's previous message), store the payload into
+// the peer slot with 16-byte stores, fence at system scope, and the last CTA
+// (ticket) release-stores n into the peer flag.
+// fg_handoff_recv (on dst): acquire-spin until flags[src][slot] >= n, copy
+// the slot out, and the last CTA release-stores n into the sender's ack.
+// Sequence numbers live on the device, so a captured CUDA graph can replay a
+// put / recv any number of times. Every wait gives up after `timeout_ms`,
+// records FG status 2 (peer flag timeout) and lets the kernel finish.
+#pragma once
+#include <cstring>
+
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace fg {
+namespace handoff {
+
+constexpr size_t kWordStride = 32;  // u32 words per flag / ack (128 bytes apart)
+
+inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// byte offsets of the regions for (world, nslot, slot_bytes)
+struct Geometry {
+  size_t data, flags, acks, send_seq, recv_seq, tickets, total;
+  Geometry(int world, int nslot, size_t slot_bytes) {
+    const size_t words = (size_t)world * nslot * kWordStride * 4;
+    data = 0;
+    flags = round_up((size_t)world * nslot * slot_bytes, 256);
+    acks = flags + words;
+    send_seq = acks + words;
+    recv_seq = send_seq + (size_t)world * kWordStride * 4;
+    tickets = recv_seq + (size_t)world * kWordStride * 4;
+    total = tickets + (size_t)2 * world * kWordStride * 4;
+  }
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// spin (bounded) until *p reaches seq (wrap-safe); false on timeout
+__device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t seq, uint64_t timeout_ns,
+                                              unsigned int site) {
+  if ((int32_t)(ld_acquire_sys(p) - seq) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if ((int32_t)(ld_acquire_sys(p) - seq) >= 0) return true;
+    if ((it & 63u) == 0) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        record_device_error(DEV_FLAG_TIMEOUT, site);
+        return false;
+      }
+      __nanosleep(256);
+    }
+  }
+}
+
+struct PutArgs {
+  const uint4* src;
+  uint4* peer_slot0;        // peer data[me][0]
+  uint32_t* peer_flags;     // peer flags[me][*]
+  uint32_t* my_acks;        // my acks[dst][*]
+  uint32_t* my_send_seq;    // my send_seq[dst]
+  uint32_t* ticket;         // my tickets[dst]
+  long long n16;            // payload in 16-byte units
+  size_t slot_bytes;
+  int nslot;
+  uint64_t timeout_ns;
+};
+
+__global__ void __launch_bounds__(256) put_kernel(const PutArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
+  __shared__ uint32_t s_seq;
+  __shared__ int s_last;
+  if (threadIdx.x == 0) {
+    const uint32_t seq = *((volatile uint32_t*)a.my_send_seq) + 1u;
+    const int slot = (int)(seq % (uint32_t)a.nslot);
+    // the receiver must have drained this slot's previous message
+    if (seq > (uint32_t)a.nslot) wait_at_least(a.my_acks + slot * kWordStride, seq - a.nslot, a.timeout_ns, 0x401);
+    s_seq = seq;
+  }
+  __syncthreads();
+  const uint32_t seq = s_seq;
+  const int slot = (int)(seq % (uint32_t)a.nslot);
+  uint4* dst = a.peer_slot0 + (size_t)slot * (a.slot_bytes / 16);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < a.n16;
+       i += (long long)gridDim.x * blockDim.x)
+    dst[i] = a.src[i];
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    __threadfence_system();
+    st_release_sys(a.peer_flags + slot * kWordStride, seq);
+    *a.ticket = 0u;
+    *((volatile uint32_t*)a.my_send_seq) = seq;
+  }
+}
+
+struct RecvArgs {
+  uint4* out;
+  const uint4* my_slot0;    // my data[src][0]
+  const uint32_t* my_flags; // my flags[src][*]
+  uint32_t* peer_acks;      // src's acks[me][*]
+  uint32_t* my_recv_seq;    // my recv_seq[src]
+  uint32_t* ticket;         // my tickets[world + src]
+  long long n16;
+  size_t slot_bytes;
+  int nslot;
+  uint64_t timeout_ns;
+};
+
+__global__ void __launch_bounds__(256) recv_kernel(const RecvArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
+  __shared__ uint32_t s_seq;
+  __shared__ int s_last;
+  if (threadIdx.x == 0) {
+    const uint32_t seq = *((volatile uint32_t*)a.my_recv_seq) + 1u;
+    wait_at_least(a.my_flags + (seq % (uint32_t)a.nslot) * kWordStride, seq, a.timeout_ns, 0x402);
+    s_seq = seq;
+  }
+  __syncthreads();
+  const uint32_t seq = s_seq;
+  const int slot = (int)(seq % (uint32_t)a.nslot);
+  const uint4* src = a.my_slot0 + (size_t)slot * (a.slot_bytes / 16);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < a.n16;
+       i += (long long)gridDim.x * blockDim.x)
+    a.out[i] = src[i];
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    __threadfence_system();
+    st_release_sys(a.peer_acks + slot * kWordStride, seq);  // slot may be reused
+    *a.ticket = 0u;
+    *((volatile uint32_t*)a.my_recv_seq) = seq;
+  }
+}
+
+// A few CTAs saturate a peer link (NVLink ~770 GB/s per direction) and keep
+// the waiting side from parking spinning CTAs on most SMs.
+inline int copy_grid(long long n16) {
+  long long g = (n16 + 1023) / 1024;
+  if (g > 32) g = 32;
+  return (int)(g < 1 ? 1 : g);
+}
+
+}  // namespace handoff
+}  // namespace fg
+
+extern "C" {
+
+size_t fg_mailbox_bytes(int world, int nslot, size_t slot_bytes) {
+  if (world <= 0 || nslot <= 0 || slot_bytes == 0 || slot_bytes % 16) return 0;
+  return fg::handoff::Geometry(world, nslot, slot_bytes).total;
+}
+
+int fg_ipc_export(const void* ptr, void* handle_out, size_t* offset_out) {
+  FG_REQUIRE(ptr && handle_out && offset_out, "fg_ipc_export: null pointer");
+  // IPC handles name whole allocations: find the one holding ptr
+  static PFN_cuMemGetAddressRange_v3020 get_range = nullptr;
+  if (!get_range) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      fg::set_last_error("fg_ipc_export: cuMemGetAddressRange unavailable");
+      return FG_ERR_CUDA;
+    }
+    get_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (get_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) {
+    fg::set_last_error("fg_ipc_export: pointer %p is not device memory", ptr);
+    return FG_ERR_ARG;
+  }
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) {
+    fg::set_last_error("fg_ipc_export: cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+    return FG_ERR_CUDA;
+  }
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base);
+  return FG_OK;
+}
+
+int fg_ipc_import(const void* handle, size_t offset, void** ptr_out) {
+  FG_REQUIRE(handle && ptr_out, "fg_ipc_import: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    fg::set_last_error("fg_ipc_import: cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+    (void)cudaGetLastError();
+    return FG_ERR_PEER;
+  }
+  *ptr_out = static_cast<uint8_t*>(base) + offset;
+  return FG_OK;
+}
+
+int fg_ipc_close(void* base_plus_offset, size_t offset) {
+  FG_REQUIRE(base_plus_offset, "fg_ipc_close: null pointer");
+  cudaError_t e = cudaIpcCloseMemHandle(static_cast<uint8_t*>(base_plus_offset) - offset);
+  if (e != cudaSuccess) {
+    fg::set_last_error("fg_ipc_close: %s", cudaGetErrorString(e));
+    return FG_ERR_CUDA;
+  }
+  return FG_OK;
+}
+
+int fg_handoff_put(const void* src, size_t nbytes, void* my_mailbox, void* peer_mailbox, int world,
+                   int me, int dst, int nslot, size_t slot_bytes, int timeout_ms, fg_stream_t stream) {
+  using namespace fg::handoff;
+  FG_REQUIRE(src && my_mailbox && peer_mailbox, "fg_handoff_put: null pointer");
+  FG_REQUIRE(world > 0 && me >= 0 && me < world && dst >= 0 && dst < world && dst != me && nslot > 0,
+             "fg_handoff_put: bad ranks me=%d dst=%d world=%d", me, dst, world);
+  FG_REQUIRE(nbytes % 16 == 0 && nbytes <= slot_bytes && slot_bytes % 16 == 0,
+             "fg_handoff_put: %zu bytes do not fit a %zu-byte slot (multiples of 16)", nbytes, slot_bytes);
+  FG_REQUIRE(((uintptr_t)src & 15) == 0, "fg_handoff_put: src must be 16-byte aligned");
+  const Geometry g(world, nslot, slot_bytes);
+  uint8_t* mine = static_cast<uint8_t*>(my_mailbox);
+  uint8_t* peer = static_cast<uint8_t*>(peer_mailbox);
+  PutArgs a;
+  a.src = static_cast<const uint4*>(src);
+  a.peer_slot0 = reinterpret_cast<uint4*>(peer + g.data + (size_t)me * nslot * slot_bytes);
+  a.peer_flags = reinterpret_cast<uint32_t*>(peer + g.flags) + (size_t)me * nslot * kWordStride;
+  a.my_acks = reinterpret_cast<uint32_t*>(mine + g.acks) + (size_t)dst * nslot * kWordStride;
+  a.my_send_seq = reinterpret_cast<uint32_t*>(mine + g.send_seq) + (size_t)dst * kWordStride;
+  a.ticket = reinterpret_cast<uint32_t*>(mine + g.tickets) + (size_t)dst * kWordStride;
+  a.n16 = (long long)(nbytes / 16);
+  a.slot_bytes = slot_bytes;
+  a.nslot = nslot;
+  a.timeout_ns = (uint64_t)(timeout_ms > 0 ? timeout_ms : 2000) * 1000000ull;
+  return fg::launch_k("fg_handoff_put", put_kernel, dim3(copy_grid(a.n16)), dim3(256), 0,
+                      (cudaStream_t)stream, a);
+}
+
+int fg_handoff_recv(void* out, size_t nbytes, void* my_mailbox, void* peer_mailbox, int world,
+                    int me, int src, int nslot, size_t slot_bytes, int timeout_ms, fg_stream_t stream) {
+  using namespace fg::handoff;
+  FG_REQUIRE(out && my_mailbox && peer_mailbox, "fg_handoff_recv: null pointer");
+  FG_REQUIRE(world > 0 && me >= 0 && me < world && src >= 0 && src < world && src != me && nslot > 0,
+             "fg_handoff_recv: bad ranks me=%d src=%d world=%d", me, src, world);
+  FG_REQUIRE(nbytes % 16 == 0 && nbytes <= slot_bytes && slot_bytes % 16 == 0,
+             "fg_handoff_recv: %zu bytes do not fit a %zu-byte slot (multiples of 16)", nbytes, slot_bytes);
+  FG_REQUIRE(((uintptr_t)out & 15) == 0, "fg_handoff_recv: out must be 16-byte aligned");
+  const Geometry g(world, nslot, slot_bytes);
+  uint8_t* mine = static_cast<uint8_t*>(my_mailbox);
+  uint8_t* peer = static_cast<uint8_t*>(peer_mailbox);
+  RecvArgs a;
+  a.out = static_cast<uint4*>(out);
+  a.my_slot0 = reinterpret_cast<const uint4*>(mine + g.data + (size_t)src * nslot * slot_bytes);
+  a.my_flags = reinterpret_cast<const uint32_t*>(mine + g.flags) + (size_t)src * nslot * kWordStride;
+  a.peer_acks = reinterpret_cast<uint32_t*>(peer + g.acks) + (size_t)me * nslot * kWordStride;
+  a.my_recv_seq = reinterpret_cast<uint32_t*>(mine + g.recv_seq) + (size_t)src * kWordStride;
+  a.ticket = reinterpret_cast<uint32_t*>(mine + g.tickets) + (size_t)(world + src) * kWordStride;
+  a.n16 = (long long)(nbytes / 16);
+  a.slot_bytes = slot_bytes;
+  a.nslot = nslot;
+  a.timeout_ns = (uint64_t)(timeout_ms > 0 ? timeout_ms : 2000) * 1000000ull;
+  return fg::launch_k("fg_handoff_recv", recv_kernel, dim3(copy_grid(a.n16)), dim3(256), 0,
+                      (cudaStream_t)stream, a);
+}
+
+}  // extern "C"

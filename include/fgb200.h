@@ -232,6 +232,33 @@ int fg_moe_unpermute(const fg_bf16* y, const int32_t* inv, const int32_t* indice
  * experts group (otherwise fg_moe_unpermute fuses it). */
 int fg_add_bf16(const fg_bf16* a, const fg_bf16* b, fg_bf16* out, long long n, fg_stream_t stream);
 
+/* ---- NVLink hand-off between ranks (replaces the NCCL send/recv of
+ * ProcessGroupComm.send_tensor / recv_tensor, comm.py:24-46, at the task
+ * boundaries of executor.py:104-123; design ancestor: the IPC-buffer + flag
+ * and RDMA-write + flag handlers of cpp_runtime comm_backend.cu:92-381,
+ * :1078-1187) ------------------------------------------------------------ */
+
+/* Bytes of one rank's mailbox: data [world][nslot][slot_bytes], sequence
+ * flags, acks, device-side counters. Zero it before first use. */
+size_t fg_mailbox_bytes(int world, int nslot, size_t slot_bytes);
+/* CUDA IPC export of the allocation holding `ptr`: 64-byte handle + offset of
+ * ptr inside it (comm_backend.cu:118-152 exchanges the same handles). */
+int fg_ipc_export(const void* ptr, void* handle_out, size_t* offset_out);
+/* Map a peer allocation (peer access enabled lazily): *ptr_out = base + offset. */
+int fg_ipc_import(const void* handle, size_t offset, void** ptr_out);
+int fg_ipc_close(void* base_plus_offset, size_t offset);
+/* Store nbytes of src (16-byte aligned, nbytes % 16 == 0, <= slot_bytes)
+ * into rank dst's mailbox slot for messages from `me`, then release the
+ * slot's sequence flag. Waits (bounded, timeout_ms) until dst drained the
+ * slot's previous message. Graph-capturable: sequence numbers live on the
+ * device. */
+int fg_handoff_put(const void* src, size_t nbytes, void* my_mailbox, void* peer_mailbox, int world,
+                   int me, int dst, int nslot, size_t slot_bytes, int timeout_ms, fg_stream_t stream);
+/* Wait (bounded, timeout_ms; on expiry the device status records a peer flag
+ * timeout) for the next message from src, copy it to out, ack the slot. */
+int fg_handoff_recv(void* out, size_t nbytes, void* my_mailbox, void* peer_mailbox, int world,
+                    int me, int src, int nslot, size_t slot_bytes, int timeout_ms, fg_stream_t stream);
+
 /* positions[b] += 1 and seq_lens[b] += 1 after a decode step
  * (LayerKVCache.advance, kv_cache.py:140-144). Either pointer may be NULL. */
 int fg_advance(int32_t* positions, int32_t* seq_lens, int B, fg_stream_t stream);
