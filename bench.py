@@ -324,6 +324,79 @@ def run_fgb200(args) -> None:
         dist.destroy_process_group()
 
 
+def run_disagg(args) -> None:
+    """Config 2 form: attention (+ embed, head) on rank 0, FFN on rank 1, hidden
+    states handed off over NVLink (P2PComm), M ping-pong micro-batches of
+    `batch` sequences each; every rank replays captured graphs."""
+    world, rank, local = dist_env()
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    assert world == 2, "--mode disagg runs on two GPUs (attention rank 0, FFN rank 1)"
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    from fluidgpu_b200 import build, kernels
+    from fluidgpu_b200.comm import P2PComm
+    from fluidgpu_b200.config import EngineConfig
+    from fluidgpu_b200.model import LLAMA3_8B, ModelWeights
+    from fluidgpu_b200.pingpong import PingPongEngine
+    from fluidgpu_b200.profile import attn_ffn_profile, profile_from_dict
+
+    build.build()
+    spec = LLAMA3_8B
+    B, ctx, W, K, M = (args.batch or 64), args.context, args.warmup, args.steps, args.micro_batches
+    total = ctx + W + K + 8
+    prof = profile_from_dict(attn_ffn_profile(spec.name, spec.num_layers, spec.hidden, spec.n_kv,
+                                              spec.head_dim, total))
+    cfg = EngineConfig(model_name=spec.name, max_seq_len=total, world_size=2, device=f"cuda:{local}",
+                       max_batch=B, cuda_graph_decode=True)
+    weights = ModelWeights.random(spec, seed=0, device=dev)
+    pp = PingPongEngine(weights, cfg, prof,
+                        lambda m: P2PComm(slot_bytes=B * spec.hidden * 2, nslot=2, tag=m),
+                        micro_batches=M)
+    pp.start(B, prompt_lens=[ctx] * B, reserve_tokens=total)
+    g = torch.Generator(device=dev).manual_seed(1)
+    for eng in pp.engines:
+        if eng.kv_cache.pool is not None:
+            eng.kv_cache.pool.normal_(0.0, 1.0, generator=g)
+        eng._tok_dev.copy_(torch.randint(0, spec.vocab, (B,), generator=g, device=dev))
+    for _ in range(W):
+        pp.step()
+    torch.cuda.synchronize()
+    kernels.check_device("disagg warm-up")
+    dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        pp.step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    kernels.check_device("disagg timed region")
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": M * B * K / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 2,
+            "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {**CONFIG, "batch_per_micro_batch": B, "micro_batches": M,
+                       "parallelism": "attention GPU0 / FFN GPU1, NVLink hand-off, ping-pong"},
+            "mode": "disagg",
+        }
+        print(json.dumps(line), flush=True)
+    for eng in pp.engines:
+        eng._graphs.clear()
+    torch.cuda.synchronize()
+    dist.barrier()
+    for eng in pp.engines:
+        eng.comm.close()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -335,10 +408,15 @@ def main() -> None:
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch every kernel from the host (no CUDA graph)")
+    ap.add_argument("--mode", default="replicas", choices=["replicas", "disagg"],
+                    help="N>1: independent co-located replicas (default) or attention/FFN disaggregation")
+    ap.add_argument("--micro-batches", type=int, default=2, help="ping-pong micro-batches (disagg)")
     args = ap.parse_args()
     assert args.warmup >= 0 and args.steps > 0
     if args.impl == "reference":
         run_reference(args)
+    elif args.mode == "disagg":
+        run_disagg(args)
     else:
         run_fgb200(args)
 

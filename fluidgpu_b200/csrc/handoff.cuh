@@ -79,6 +79,22 @@ __device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t seq, u
   }
 }
 
+// grid-stride 16-byte copy, four loads in flight per thread before their
+// stores (a remote store stream needs many outstanding requests)
+__device__ __forceinline__ void copy16(uint4* __restrict__ dst, const uint4* __restrict__ src,
+                                       long long n16) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n16; i += 4 * stride) {
+    const uint4 v0 = src[i], v1 = src[i + stride], v2 = src[i + 2 * stride], v3 = src[i + 3 * stride];
+    dst[i] = v0;
+    dst[i + stride] = v1;
+    dst[i + 2 * stride] = v2;
+    dst[i + 3 * stride] = v3;
+  }
+  for (; i < n16; i += stride) dst[i] = src[i];
+}
+
 struct PutArgs {
   const uint4* src;
   uint4* peer_slot0;        // peer data[me][0]
@@ -107,10 +123,7 @@ __global__ void __launch_bounds__(256) put_kernel(const PutArgs a) {
   __syncthreads();
   const uint32_t seq = s_seq;
   const int slot = (int)(seq % (uint32_t)a.nslot);
-  uint4* dst = a.peer_slot0 + (size_t)slot * (a.slot_bytes / 16);
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < a.n16;
-       i += (long long)gridDim.x * blockDim.x)
-    dst[i] = a.src[i];
+  copy16(a.peer_slot0 + (size_t)slot * (a.slot_bytes / 16), a.src, a.n16);
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
@@ -149,10 +162,7 @@ __global__ void __launch_bounds__(256) recv_kernel(const RecvArgs a) {
   __syncthreads();
   const uint32_t seq = s_seq;
   const int slot = (int)(seq % (uint32_t)a.nslot);
-  const uint4* src = a.my_slot0 + (size_t)slot * (a.slot_bytes / 16);
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < a.n16;
-       i += (long long)gridDim.x * blockDim.x)
-    a.out[i] = src[i];
+  copy16(a.out, a.my_slot0 + (size_t)slot * (a.slot_bytes / 16), a.n16);
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
@@ -165,11 +175,13 @@ __global__ void __launch_bounds__(256) recv_kernel(const RecvArgs a) {
   }
 }
 
-// A few CTAs saturate a peer link (NVLink ~770 GB/s per direction) and keep
-// the waiting side from parking spinning CTAs on most SMs.
+// One CTA per 32 KiB, at most 128: small messages stay on a few SMs (only
+// thread 0 of each CTA spins, so a waiting receive parks little on the SMs),
+// large ones keep enough stores in flight to fill a peer link (~770 GB/s per
+// direction).
 inline int copy_grid(long long n16) {
-  long long g = (n16 + 1023) / 1024;
-  if (g > 32) g = 32;
+  long long g = (n16 + 2047) / 2048;
+  if (g > 128) g = 128;
   return (int)(g < 1 ? 1 : g);
 }
 

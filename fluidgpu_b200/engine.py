@@ -92,8 +92,9 @@ class DecodeEngine:
             with torch.cuda.stream(s), torch.inference_mode():
                 with torch.cuda.graph(g, stream=s):
                     logits = self.runner.decode_step(self._tok_dev)
-                    kernels.argmax(logits.reshape(B, -1), out=self._next_dev)
-                    self._tok_dev.copy_(self._next_dev)
+                    if logits is not None:  # the norm_lm_head rank closes the loop
+                        kernels.argmax(logits.reshape(B, -1), out=self._next_dev)
+                        self._tok_dev.copy_(self._next_dev)
         finally:
             kv.plan_len_override = None
             kv.restore_host(snap)
@@ -114,8 +115,8 @@ class DecodeEngine:
         """One greedy step from host tokens [B] to host tokens [B]."""
         assert self._tok_dev is not None, "call start() first"
         self._tok_dev.copy_(tokens_host, non_blocking=True)
-        if self.use_graph and self.rank == 0 and self.comm.get_world_size() == 1:
-            nxt = self.replay()
+        if self.use_graph:
+            nxt = self.replay() if self.rank == 0 else (self.replay(), None)[1]
         else:
             nxt = self.step_device(self._tok_dev)
         if nxt is None:

@@ -3,6 +3,9 @@
   python -m fluidgpu_b200.microbench attn  [--batch B] [--context L] [--window W]
   python -m fluidgpu_b200.microbench gemm  [--T T] [--N N] [--K K] [--epilogue store|residual|swiglu]
   python -m fluidgpu_b200.microbench sweep-attn      # B in {1,32,256} x ctx in {512,4096,32768}
+  torchrun --nproc-per-node 2 -m fluidgpu_b200.microbench handoff
+      # [T,H] bf16 hand-off GPU0 -> GPU1, T in {1,8,64,256,1024,8192}, H in {2880,4096}:
+      # NVLink mailbox put/recv (P2PComm) against NCCL send/recv, one-way time
 
 Each prints one JSON line per case: device time per launch (CUDA events,
 median of --iters after --warmup), algorithmic bytes and GB/s, and the
@@ -129,9 +132,85 @@ def bench_gemm(T: int, N: int, K: int, epilogue: str = "store", iters: int = 20,
             "frac_hbm": gbs / peak, "peak": f"{src} {peak} GB/s", "timing": "graph" if GRAPH else "eager"}
 
 
+def bench_handoff(iters: int = 50, warmup: int = 10) -> None:
+    """Ping-pong [T,H] between ranks 0 and 1; one-way time = round trip / 2."""
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from .comm import P2PComm
+
+    rank = int(os.environ["RANK"])
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    comm = P2PComm(slot_bytes=8192 * 4096 * 2, nslot=2)
+    peer = 1 - rank
+    for H in (2880, 4096):
+        for T in (1, 8, 64, 256, 1024, 8192):
+            x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+            y = torch.empty_like(x)
+
+            def p2p():
+                if rank == 0:
+                    comm.send_tensor(x, peer)
+                    comm.recv_tensor(y, peer)
+                else:
+                    comm.recv_tensor(y, peer)
+                    comm.send_tensor(y, peer)
+
+            def nccl():
+                if rank == 0:
+                    dist.send(x, peer)
+                    dist.recv(y, peer)
+                else:
+                    dist.recv(y, peer)
+                    dist.send(y, peer)
+
+            def timed(fn, n):
+                torch.cuda.synchronize()
+                dist.barrier()
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record()
+                fn(n)
+                b.record()
+                torch.cuda.synchronize()
+                return a.elapsed_time(b) / n / 2 * 1e3  # us, one way
+
+            res = {}
+            for name, fn in (("nvlink_put", p2p), ("nccl_sendrecv", nccl)):
+                for _ in range(warmup):
+                    fn()
+                res[name] = timed(lambda n: [fn() for _ in range(n)], iters)
+            # the same NVLink ping-pong captured in one graph per rank: device
+            # time without host launch overhead (as in the graphed decode step)
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+                for _ in range(iters):
+                    p2p()
+            torch.cuda.current_stream().wait_stream(s)
+            g.replay()
+            res["nvlink_graph"] = timed(lambda n: g.replay(), iters)
+            del g
+            if rank == 0:
+                nbytes = T * H * 2
+                print(json.dumps({"kernel": "fg_handoff_put/recv", "T": T, "H": H, "bytes": nbytes,
+                                  "nvlink_graph_us": res["nvlink_graph"], "nvlink_eager_us": res["nvlink_put"],
+                                  "nccl_eager_us": res["nccl_sendrecv"],
+                                  "nvlink_graph_GBps": nbytes / res["nvlink_graph"] / 1e3,
+                                  "nccl_GBps": nbytes / res["nccl_sendrecv"] / 1e3,
+                                  "link_peak_GBps": 770.0}), flush=True)
+    kernels.check_device("handoff microbench")
+    comm.close()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["attn", "gemm", "sweep-attn", "llama-gemms"])
+    ap.add_argument("what", choices=["attn", "gemm", "sweep-attn", "llama-gemms", "handoff"])
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--window", type=int, default=0)
@@ -151,6 +230,9 @@ def main() -> None:
     global GRAPH
     GRAPH = not a.eager
     build.build()
+    if a.what == "handoff":
+        bench_handoff()
+        return
     torch.cuda.set_device(0)
     if a.what == "attn":
         print(json.dumps(bench_attn(a.batch, a.context, a.nq, a.nkv, a.hd, a.window, a.iters, a.warmup)))
