@@ -27,7 +27,7 @@ from .comm import LocalComm
 from .config import EngineConfig
 from .executor import LayerExecutor
 from .model import ModelWeights
-from .profile import RuntimeProfile, colocated_profile, owned_layer_ids, profile_from_dict
+from .profile import RuntimeProfile, colocated_profile, kv_layer_ids, profile_from_dict
 from .runner import FluidRunner
 
 
@@ -43,7 +43,7 @@ class DecodeEngine:
         self.profile = profile
         self.executor = LayerExecutor(profile, cfg, self.comm)
         self.runner = FluidRunner(weights, None, self.executor, cfg,
-                                  owned_layer_ids(profile, self.rank), num_blocks=num_blocks)
+                                  kv_layer_ids(profile, self.rank), num_blocks=num_blocks)
         self.cfg = cfg
         self.device = cfg.torch_device
         self._tok_dev: torch.Tensor | None = None

@@ -35,6 +35,7 @@ class LayerExecutor:
         self.device = cfg.torch_device
         self._decode_bufs: dict[int, torch.Tensor] = {}
         self._prefill_buf: torch.Tensor | None = None
+        self._wide_bufs: dict[tuple, torch.Tensor] = {}
         if cfg.preallocate_recv_buffers:
             self._decode_bufs[cfg.max_batch] = torch.empty(
                 (cfg.max_batch, 1, profile.hidden_size), dtype=cfg.dtype, device=self.device)
@@ -67,7 +68,10 @@ class LayerExecutor:
         return self.tasks[self.task_index_by_name[task_name]].rank_for(mode)
 
     def _run(self, task_name: str, fn: Callable[..., Any], value: torch.Tensor | None, *, mode: str,
-             seq_len: int | None, batch: int | None = None, **kwargs: Any) -> torch.Tensor | None:
+             seq_len: int | None, batch: int | None = None, recv_width: int | None = None,
+             **kwargs: Any) -> torch.Tensor | None:
+        """`recv_width`: last dimension of the incoming value when it is not the
+        hidden size (the sdpa -> o_proj edge carries n_q * head_dim features)."""
         assert mode in ("prefill", "decode"), f"invalid mode {mode}"
         idx = self.task_index_by_name[task_name]
         task = self.tasks[idx]
@@ -76,7 +80,8 @@ class LayerExecutor:
         prev_rank = self._prev_rank(idx, mode)
         if prev_rank is not None and prev_rank != self.my_rank:
             b = batch if batch is not None else (value.shape[0] if value is not None else 1)
-            value = self._recv(mode=mode, batch=b, seq_len=self._seq_len(value, seq_len), src=prev_rank)
+            value = self._recv(mode=mode, batch=b, seq_len=self._seq_len(value, seq_len), src=prev_rank,
+                               width=recv_width)
         assert value is not None, f"rank {self.my_rank} entered {task_name} without input"
         with trace_region(kind="compute", name=task_name, device=self.device, mode=mode):
             out = _first_tensor(fn(value, **kwargs))
@@ -87,14 +92,22 @@ class LayerExecutor:
             self._comm.send_tensor(out, dst=next_rank)
         return out
 
-    def _recv(self, *, mode: str, batch: int, seq_len: int, src: int) -> torch.Tensor:
-        buf = self._recv_buffer(mode=mode, batch=batch, seq_len=seq_len)
+    def _recv(self, *, mode: str, batch: int, seq_len: int, src: int, width: int | None = None) -> torch.Tensor:
+        buf = self._recv_buffer(mode=mode, batch=batch, seq_len=seq_len, width=width)
         self._comm.recv_tensor(buf, src=src)
         return buf
 
-    def _recv_buffer(self, *, mode: str, batch: int, seq_len: int) -> torch.Tensor:
+    def _recv_buffer(self, *, mode: str, batch: int, seq_len: int, width: int | None = None) -> torch.Tensor:
         assert seq_len > 0, f"seq_len must be positive, got {seq_len}"
         H = self.profile.hidden_size
+        if width is not None and width != H:
+            # a second buffer per (batch, width): the o_proj input of a split attention
+            key = (batch, seq_len, width, mode)
+            buf = self._wide_bufs.get(key)
+            if buf is None:
+                buf = torch.empty((batch, seq_len, width), dtype=self.cfg.dtype, device=self.device)
+                self._wide_bufs[key] = buf
+            return buf
         if mode == "decode":
             assert seq_len == 1, f"decode seq_len must be 1, got {seq_len}"
             buf = self._decode_bufs.get(batch)

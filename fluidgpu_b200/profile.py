@@ -209,6 +209,21 @@ def owned_layer_ids(profile: RuntimeProfile, rank: int) -> list[int]:
     return owned
 
 
+def kv_layer_ids(profile: RuntimeProfile, rank: int) -> list[int]:
+    """Layers whose paged KV lives on `rank`: where the attention reads it
+    (attn, or sdpa in a split plan). Equal to owned_layer_ids except when
+    qkv and sdpa sit on different ranks: the reference then appends on the
+    qkv rank and ships q plus the whole K/V view to sdpa every step
+    (runner.py:284-296, :462-472); here the qkv rank ships only the new
+    token's projected qkv row and the sdpa rank appends it to its own pages."""
+    owned = []
+    for t in profile.tasks:
+        p = parse_layer_task(t.name)
+        if p is not None and p[1] in ("attn", "sdpa") and t.rank == rank:
+            owned.append(p[0])
+    return owned
+
+
 def make_ranked_task_profile(*, model: str, task_assignments: list[tuple[str, int]],
                              hidden_size: int, num_kv_heads: int, head_dim: int,
                              max_seq_len: int = 2048, dtype: torch.dtype = torch.bfloat16,

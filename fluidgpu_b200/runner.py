@@ -16,6 +16,21 @@ sm_100a kernels of libfgb200.so instead of HF modules:
   MoE FFN    : fg_rmsnorm -> router top-k -> expert grouped GEMMs (moe.py)
   _norm_head : fg_rmsnorm -> fg_gemm_bf16 (lm_head)
 
+Fine-grained plans split the groups as the reference does (runner.py:196-254,
+:362-414): layer_i_{qkv,sdpa,o_proj}, layer_i_{mlp_gate_up,mlp_down_proj},
+layer_i_{moe_router,moe_experts,moe_combine}. The value on the main path is
+the reference's (qkv and gate_up pass the normalised hidden on, sdpa the
+attention output); what a later group needs from an earlier one on another
+rank travels as aux tensors in a fixed order (runner.py:462-654):
+  qkv -> sdpa        : projected qkv row [B, (n_q + 2 n_kv) hd], residual [B, H]
+  sdpa -> o_proj     : residual
+  gate_up -> down    : SwiGLU intermediate [B, I], residual
+  router -> experts  : top-k weights [B, k] bf16, expert ids [B, k] int32, residual
+  experts -> combine : residual
+The reference ships q plus the whole K/V view from qkv to sdpa; here the KV
+pages live on the sdpa rank (profile.kv_layer_ids) and RoPE + append run
+there, so only the new token's projection crosses.
+
 Generalisations over the reference: a batch of B requests decodes together
 (hidden [B, 1, H], the reference asserts batch 1 at runner.py:67, :120), and
 the KV cache is paged (kv_cache.PagedKVCache). prefill() feeds the prompt
@@ -52,6 +67,8 @@ class FluidRunner:
             max_seq_len=cfg.max_seq_len, num_kv_heads=self.spec.n_kv, head_dim=self.spec.head_dim,
             dtype=cfg.dtype, device=self.device, max_batch=cfg.max_batch, num_blocks=num_blocks)
         self._moe_states: dict[int, dict[str, torch.Tensor]] = {}
+        self._attn_states: dict[int, dict[str, torch.Tensor]] = {}
+        self._mlp_states: dict[int, dict[str, torch.Tensor]] = {}
         # scratch slots of this runner (runners on other streams use their own)
         self.slot = f"runner{id(self):x}"
         # MoE routing of the last step per layer (tests compare it with the oracle)
@@ -109,11 +126,34 @@ class FluidRunner:
         return name in self.executor.task_index_by_name
 
     def _run_attention_tasks(self, i: int, hidden: torch.Tensor | None, B: int) -> torch.Tensor | None:
-        out = self.executor.run_kernel_group(f"layer_{i}_attn", self._run_attn, hidden, mode="decode",
-                                             seq_len=1, batch=B, layer=i)
-        return out if out is not None else hidden
+        if not self._has_task(f"layer_{i}_qkv"):
+            out = self.executor.run_kernel_group(f"layer_{i}_attn", self._run_attn, hidden, mode="decode",
+                                                 seq_len=1, batch=B, layer=i)
+            return out if out is not None else hidden
+        s = self.spec
+        for suffix, fn in (("qkv", self._run_attn_qkv), ("sdpa", self._run_attn_sdpa),
+                           ("o_proj", self._run_attn_o_proj)):
+            kw = {"recv_width": s.n_q * s.head_dim} if suffix == "o_proj" else {}
+            out = self.executor.run_kernel_group(f"layer_{i}_{suffix}", fn, hidden, mode="decode",
+                                                 seq_len=1, batch=B, layer=i, **kw)
+            if out is not None:
+                hidden = out
+                if suffix == "qkv":
+                    self._after_attn_qkv(i)
+                elif suffix == "sdpa":
+                    self._after_attn_sdpa(i)
+        return hidden
 
     def _run_feed_forward_tasks(self, i: int, hidden: torch.Tensor | None, B: int) -> torch.Tensor | None:
+        if self._has_task(f"layer_{i}_mlp_gate_up"):
+            for suffix, fn in (("mlp_gate_up", self._run_mlp_gate_up), ("mlp_down_proj", self._run_mlp_down_proj)):
+                out = self.executor.run_kernel_group(f"layer_{i}_{suffix}", fn, hidden, mode="decode",
+                                                     seq_len=1, batch=B, layer=i)
+                if out is not None:
+                    hidden = out
+                    if suffix == "mlp_gate_up":
+                        self._after_mlp_gate_up(i)
+            return hidden
         if self._has_task(f"layer_{i}_mlp"):
             out = self.executor.run_kernel_group(f"layer_{i}_mlp", self._run_mlp, hidden,
                                                  mode="decode", seq_len=1, batch=B, layer=i)
@@ -124,6 +164,10 @@ class FluidRunner:
                                                  seq_len=1, batch=B, layer=i)
             if out is not None:
                 hidden = out
+                if suffix == "moe_router":
+                    self._after_moe_router(i)
+                elif suffix == "moe_experts":
+                    self._after_moe_experts(i)
         return hidden
 
     # -- kernel groups (override points of the reference runner) ---------------
@@ -150,6 +194,70 @@ class FluidRunner:
                            slot=self.slot + ".gemm")
         return out.view(B, 1, s.hidden)
 
+    # fine attention groups (runner.py:256-347)
+    def _run_attn_qkv(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+        s = self.spec
+        W = self.weights.layers[layer]
+        B = hidden.shape[0]
+        h = hidden.reshape(B, s.hidden)
+        x = kernels.rmsnorm(h, W["ln1"], s.eps, s.norm_mode)
+        qkv = kernels.gemm(x, W["wqkv"], bias=W.get("bqkv"), slot=self.slot + ".gemm")
+        self._attn_states[layer] = {"residual": h, "qkv": qkv}
+        return x.view(B, 1, s.hidden)
+
+    def _run_attn_sdpa(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+        s = self.spec
+        W = self.weights.layers[layer]
+        kv = self.kv_cache
+        B = hidden.shape[0]
+        st = self._ensure_attn_qkv_state(layer, B)
+        kp, vp = kv.layer_pages(layer)
+        bt = kv.block_table[:B]
+        q = kernels.rope_kv_append(st["qkv"], kv.positions[:B], self.weights.inv_freq,
+                                   self.weights.rope_scaling, bt, kp, vp, s.n_q, s.n_kv, s.head_dim)
+        a = kernels.paged_decode_attn(q, kp, vp, bt, kv.seq_lens[:B], kv.plan_len(),
+                                      window=s.window(layer), sinks=W.get("sinks"),
+                                      slot=self.slot + ".attn")
+        return a.view(B, 1, s.n_q * s.head_dim)
+
+    def _run_attn_o_proj(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+        s = self.spec
+        W = self.weights.layers[layer]
+        B = hidden.shape[0]
+        self._ensure_residual(self._attn_states, layer, B, src=self._rank_of(layer, "sdpa"))
+        st = self._attn_states.pop(layer)
+        a = hidden.reshape(B, s.n_q * s.head_dim)
+        out = kernels.gemm(a, W["wo"], epilogue=_lib.FG_EPI_RESIDUAL, residual=st["residual"],
+                           bias=W.get("bo"), slot=self.slot + ".gemm")
+        return out.view(B, 1, s.hidden)
+
+    def _after_attn_qkv(self, layer: int) -> None:
+        dst = self._rank_of(layer, "sdpa")
+        if dst == self._rank_of(layer, "qkv"):
+            return
+        st = self._attn_states.pop(layer)
+        self._send_aux(st["qkv"], dst)
+        self._send_aux(st["residual"], dst)
+
+    def _after_attn_sdpa(self, layer: int) -> None:
+        st = self._attn_states.get(layer)
+        if st is None:
+            return
+        st.pop("qkv", None)
+        dst = self._rank_of(layer, "o_proj")
+        if dst == self._rank_of(layer, "sdpa"):
+            return
+        self._send_aux(st["residual"], dst)
+        self._attn_states.pop(layer, None)
+
+    def _ensure_attn_qkv_state(self, layer: int, B: int) -> dict[str, torch.Tensor]:
+        st = self._attn_states.setdefault(layer, {})
+        if "qkv" not in st:
+            src = self._rank_of(layer, "qkv")
+            st["qkv"] = self._recv_aux((B, self.spec.qkv_width), torch.bfloat16, src)
+            st["residual"] = self._recv_aux((B, self.spec.hidden), torch.bfloat16, src)
+        return st
+
     def _run_mlp(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
         s = self.spec
         W = self.weights.layers[layer]
@@ -160,6 +268,39 @@ class FluidRunner:
         out = kernels.gemm(act, W["w_down"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h,
                            slot=self.slot + ".gemm")
         return out.view(B, 1, s.hidden)
+
+    # fine dense FFN groups (runner.py:416-430)
+    def _run_mlp_gate_up(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+        s = self.spec
+        W = self.weights.layers[layer]
+        B = hidden.shape[0]
+        h = hidden.reshape(B, s.hidden)
+        x = kernels.rmsnorm(h, W["ln2"], s.eps, s.norm_mode)
+        act = kernels.gemm(x, W["w_gate_up"], epilogue=_lib.FG_EPI_SWIGLU, slot=self.slot + ".gemm")
+        self._mlp_states[layer] = {"residual": h, "intermediate": act}
+        return x.view(B, 1, s.hidden)
+
+    def _run_mlp_down_proj(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+        s = self.spec
+        W = self.weights.layers[layer]
+        B = hidden.shape[0]
+        st = self._mlp_states.setdefault(layer, {})
+        if "intermediate" not in st:
+            src = self._rank_of(layer, "mlp_gate_up")
+            st["intermediate"] = self._recv_aux((B, s.intermediate), torch.bfloat16, src)
+            st["residual"] = self._recv_aux((B, s.hidden), torch.bfloat16, src)
+        st = self._mlp_states.pop(layer)
+        out = kernels.gemm(st["intermediate"], W["w_down"], epilogue=_lib.FG_EPI_RESIDUAL,
+                           residual=st["residual"], slot=self.slot + ".gemm")
+        return out.view(B, 1, s.hidden)
+
+    def _after_mlp_gate_up(self, layer: int) -> None:
+        dst = self._rank_of(layer, "mlp_down_proj")
+        if dst == self._rank_of(layer, "mlp_gate_up"):
+            return
+        st = self._mlp_states.pop(layer)
+        self._send_aux(st["intermediate"], dst)
+        self._send_aux(st["residual"], dst)
 
     def _run_moe_router(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
         from . import moe
@@ -179,13 +320,17 @@ class FluidRunner:
         from . import moe
 
         s = self.spec
-        st = self._moe_states.get(layer)
-        assert st is not None, (
-            f"layer {layer}: moe_experts needs the router state on this rank "
-            "(router and experts groups must share a rank)")
         B = hidden.shape[0]
+        st = self._moe_states.setdefault(layer, {})
+        if "indices" not in st:
+            src = self._rank_of(layer, "moe_router")
+            st["weights"] = self._recv_aux((B, s.top_k), torch.bfloat16, src)
+            st["indices"] = self._recv_aux((B, s.top_k), torch.int32, src)
+            st["residual"] = self._recv_aux((B, s.hidden), torch.bfloat16, src)
+            if self.record_routing:
+                self.last_routing[layer] = st["indices"]
         # the combine group's residual add is fused when it runs here too
-        fuse = self.executor.task_rank(f"layer_{layer}_moe_combine", "decode") == self.executor.my_rank
+        fuse = self._rank_of(layer, "moe_combine") == self.executor.my_rank
         y = moe.experts_forward(hidden.reshape(B, s.hidden), st["indices"], st["weights"],
                                 self.weights.layers[layer], s,
                                 residual=st["residual"] if fuse else None)
@@ -195,11 +340,50 @@ class FluidRunner:
     def _run_moe_combine(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
         from . import moe
 
+        B = hidden.shape[0]
+        self._ensure_residual(self._moe_states, layer, B, src=self._rank_of(layer, "moe_experts"))
         st = self._moe_states.pop(layer)
         if st.get("fused"):
             return hidden
-        B = hidden.shape[0]
         return moe.residual_add(st["residual"], hidden.reshape(B, -1)).view(B, 1, -1)
+
+    def _after_moe_router(self, layer: int) -> None:
+        dst = self._rank_of(layer, "moe_experts")
+        if dst == self._rank_of(layer, "moe_router"):
+            return
+        st = self._moe_states.pop(layer)
+        self._send_aux(st["weights"], dst)
+        self._send_aux(st["indices"], dst)
+        self._send_aux(st["residual"], dst)
+
+    def _after_moe_experts(self, layer: int) -> None:
+        st = self._moe_states.get(layer)
+        if st is None:
+            return
+        st.pop("weights", None)
+        st.pop("indices", None)
+        dst = self._rank_of(layer, "moe_combine")
+        if dst == self._rank_of(layer, "moe_experts"):
+            return
+        self._send_aux(st["residual"], dst)
+        self._moe_states.pop(layer, None)
+
+    # -- aux routing (runner.py:462-670) ----------------------------------------
+    def _rank_of(self, layer: int, suffix: str) -> int:
+        return self.executor.task_rank(f"layer_{layer}_{suffix}", "decode")
+
+    def _send_aux(self, t: torch.Tensor, dst: int) -> None:
+        self.executor.send_aux_tensor(t if t.is_contiguous() else t.contiguous(), dst=dst)
+
+    def _recv_aux(self, shape: tuple[int, ...], dtype: torch.dtype, src: int) -> torch.Tensor:
+        out = torch.empty(shape, dtype=dtype, device=self.device)
+        self.executor.recv_aux_tensor(out, src=src)
+        return out
+
+    def _ensure_residual(self, states: dict, layer: int, B: int, *, src: int) -> None:
+        st = states.setdefault(layer, {})
+        if "residual" not in st:
+            st["residual"] = self._recv_aux((B, self.spec.hidden), torch.bfloat16, src)
 
     def _norm_head(self, hidden: torch.Tensor) -> torch.Tensor:
         s = self.spec
@@ -209,6 +393,18 @@ class FluidRunner:
 
     def _skip_head(self, hidden: torch.Tensor) -> torch.Tensor:
         return hidden
+
+    def max_message_bytes(self, batch: int) -> int:
+        """Largest tensor this plan sends between two ranks in a decode step of
+        `batch` sequences (the P2PComm slot must hold it)."""
+        s = self.spec
+        names = self.executor.task_index_by_name
+        sizes = [batch * s.hidden * 2]
+        if any(n.endswith("_qkv") for n in names):
+            sizes += [batch * s.qkv_width * 2, batch * s.n_q * s.head_dim * 2]
+        if any(n.endswith("_mlp_gate_up") for n in names):
+            sizes.append(batch * s.intermediate * 2)
+        return max(sizes)
 
     def reserve_workspaces(self, batch: int, plan_len: int) -> None:
         """Allocate this runner's scratch at the size a step of `batch`

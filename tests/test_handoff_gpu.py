@@ -3,9 +3,11 @@
 - A receive whose flag nobody sets gives up after its bound, records the
   peer-flag-timeout status and leaves the context usable (single GPU).
 - Two ranks as two processes on two GPUs: round trips through the mailboxes
-  with slot reuse, the same exchange replayed from CUDA graphs, and a
-  disaggregated decode (attention + head on rank 0, FFN on rank 1) whose
-  logits equal a co-located run bit for bit.
+  with slot reuse, the same exchange replayed from CUDA graphs, and two
+  disaggregated decodes whose logits equal a co-located run bit for bit:
+  attention + head on rank 0 with the FFN on rank 1, and a fine-grained plan
+  (qkv / sdpa / o_proj and gate_up / down_proj on alternating ranks, with
+  their aux tensors crossing over NVLink).
 Multi-GPU cases are skipped on a single-GPU box."""
 import ctypes
 import os
@@ -92,13 +94,30 @@ def _graphed(rank, comm):
     del g
 
 
-def _disaggregated(rank, comm):
+def _attn_ffn_plan():
+    from fluidgpu_b200.profile import attn_ffn_profile
+
+    return attn_ffn_profile("disagg", 3, 512, 2, 64, 64)
+
+
+def _fine_plan():
+    from fluidgpu_b200.profile import make_ranked_task_profile
+
+    return make_ranked_task_profile(model="disagg", task_assignments=[
+        ("layer_0_qkv", 0), ("layer_0_sdpa", 1), ("layer_0_o_proj", 0),
+        ("layer_0_mlp_gate_up", 1), ("layer_0_mlp_down_proj", 0),
+        ("layer_1_qkv", 1), ("layer_1_sdpa", 0), ("layer_1_o_proj", 1), ("layer_1_mlp", 0),
+        ("layer_2_attn", 1), ("layer_2_mlp_gate_up", 0), ("layer_2_mlp_down_proj", 1),
+    ], hidden_size=512, num_kv_heads=2, head_dim=64, max_seq_len=64, rank_count=2)
+
+
+def _disaggregated(rank, comm, plan=_attn_ffn_plan):
     from transformers.models.llama import LlamaConfig, LlamaForCausalLM
 
     from fluidgpu_b200.config import EngineConfig
     from fluidgpu_b200.engine import DecodeEngine
     from fluidgpu_b200.model import ModelWeights
-    from fluidgpu_b200.profile import attn_ffn_profile, profile_from_dict
+    from fluidgpu_b200.profile import profile_from_dict
 
     torch.manual_seed(0)
     cfg = LlamaConfig(num_hidden_layers=3, vocab_size=2048, hidden_size=512, intermediate_size=1024,
@@ -107,7 +126,7 @@ def _disaggregated(rank, comm):
     B, prompt, steps = 4, 10, 6
     ecfg = EngineConfig(model_name="disagg", max_seq_len=64, world_size=2, device=f"cuda:{rank}",
                         max_batch=B)
-    prof = profile_from_dict(attn_ffn_profile("disagg", 3, 512, 2, 64, 64))
+    prof = profile_from_dict(plan())
     eng = DecodeEngine(ModelWeights.from_hf(model, f"cuda:{rank}"), ecfg, profile=prof, comm=comm)
     g = torch.Generator().manual_seed(1)
     prompts = torch.randint(0, 2048, (B, prompt), generator=g)
@@ -136,7 +155,8 @@ def _disaggregated(rank, comm):
         out = ref.runner.decode_step(lg.argmax(-1).cuda())
 
 
-CASES = {"roundtrip": _roundtrip, "graphed": _graphed, "disaggregated": _disaggregated}
+CASES = {"roundtrip": _roundtrip, "graphed": _graphed, "disaggregated": _disaggregated,
+         "fine_split": lambda rank, comm: _disaggregated(rank, comm, _fine_plan)}
 
 
 def _worker(rank, world, port, case, q):

@@ -174,3 +174,32 @@ def test_lost_message_times_out_on_host():
     c = QueueComm(1, ch, timeout_s=0.2)
     with pytest.raises(TimeoutError):
         c.recv_tensor(torch.zeros(2, 1, 4), src=0)
+
+
+def test_fine_attention_edge_widths_and_kv_placement():
+    """A split attention: qkv and o_proj on rank 0, sdpa on rank 1. Rank 0
+    receives the sdpa output at its own width (n_q * head_dim, here 6 while the
+    hidden size is 4); the KV pages live where sdpa reads them."""
+    from fluidgpu_b200.profile import kv_layer_ids
+
+    prof = profile_from_dict(make_ranked_task_profile(model="m", task_assignments=[
+        ("layer_0_qkv", 0), ("layer_0_sdpa", 1), ("layer_0_o_proj", 0), ("layer_0_mlp", 1)],
+        hidden_size=4, num_kv_heads=2, head_dim=2))
+    assert owned_layer_ids(prof, 0) == [0]  # the reference's rule: the qkv rank
+    assert kv_layer_ids(prof, 0) == [] and kv_layer_ids(prof, 1) == [0]
+    comm = FakeComm(0)
+    ex = LayerExecutor(prof, _cfg(), comm)
+    h = torch.zeros(3, 1, 4, dtype=torch.bfloat16)
+    seen = {}
+    for name, width in (("layer_0_qkv", None), ("layer_0_sdpa", None), ("layer_0_o_proj", 6)):
+        kw = {"recv_width": width} if width else {}
+        def fn(x, name=name):
+            seen[name] = x.clone()
+            return torch.zeros(3, 1, 4, dtype=torch.bfloat16)
+
+        out = ex.run_kernel_group(name, fn, h, mode="decode", seq_len=1, batch=3, **kw)
+        h = out if out is not None else h
+    assert "layer_0_sdpa" not in seen
+    assert tuple(seen["layer_0_o_proj"].shape) == (3, 1, 6)
+    assert comm.send_log == [((3, 1, 4), 1), ((3, 1, 4), 1)]  # qkv -> sdpa, o_proj -> mlp
+    assert comm.recv_log == [((3, 1, 6), 1)]
