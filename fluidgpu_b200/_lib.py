@@ -63,7 +63,7 @@ SIGNATURES: dict[str, tuple] = {
         [_P, _P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
          c_float, _P],
     ),
-    "fg_attn_pages_per_split": (c_int, [c_int, c_int, c_int, c_int]),
+    "fg_attn_splits": (c_int, [c_int, c_int, c_int, c_int, c_int]),
     "fg_attn_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
     "fg_argmax": (c_int, [_P, _P, c_int, c_int, _P]),
     "fg_moe_router_topk": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P, _P, _P]),

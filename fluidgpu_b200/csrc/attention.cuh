@@ -34,6 +34,7 @@ constexpr int kConsumers = 4;  // consumer warps
 constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegBig = -1.0e30f;
+constexpr int kMinSlice = 8;   // fewest pages a split slice is given
 
 struct Params {
   const __nv_bfloat16* q;   // [B][nq][hd]
@@ -45,7 +46,7 @@ struct Params {
   float* part_ml;           // [B][nq][splits][2]
   int B, nq, nkv, G;
   int max_blocks, num_blocks;
-  int pages_per_split, splits;
+  int splits;               // slices per (sequence, kv head)
   int window;
   float scale_log2;         // softmax scale * log2(e)
 };
@@ -90,7 +91,7 @@ struct Layout {
 };
 
 template <int HD, int STAGES>
-__global__ void __launch_bounds__(kThreads) paged_attn_kernel(
+__global__ void __launch_bounds__(kThreads, 3) paged_attn_kernel(
     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
     const Params p) {
   using L = Layout<HD, STAGES>;
@@ -108,8 +109,13 @@ __global__ void __launch_bounds__(kThreads) paged_attn_kernel(
   const int Lq = p.seq_lens[b];
   const int lo = p.window > 0 ? max(0, Lq - p.window) : 0;
   const int pbeg = lo / kBlock, pend = (Lq + kBlock - 1) / kBlock;
-  const int my0 = pbeg + split * p.pages_per_split;
-  const int my1 = min(my0 + p.pages_per_split, pend);
+  // this sequence's pages split evenly over its active slices (>= kMinSlice
+  // pages each), from its actual length: a plan made for a longer bucket
+  // still gives every CTA of the sequence the same share
+  const int P = max(pend - pbeg, 0);
+  const int active = min(p.splits, max(1, (P + kMinSlice - 1) / kMinSlice));
+  const int my0 = split < active ? pbeg + (int)((int64_t)split * P / active) : pend;
+  const int my1 = split < active ? pbeg + (int)((int64_t)(split + 1) * P / active) : pend;
   const int npages = my1 - my0;
 
   if (npages <= 0) {
@@ -359,43 +365,71 @@ __global__ void attn_combine_kernel(const Params p, int hd) {
   p.out[((int64_t)b * p.nq + h) * hd + d] = f2bf(lsum > 0.f ? osum / lsum : 0.f);
 }
 
-// Split plan: pages per slice and slice count for a batch whose longest
-// sequence has max_seq_len tokens. Slices are counted from the first page in
-// the window, so a sliding window also bounds the slice count.
-inline void plan(int B, int nkv, int max_seq_len, int window, int* pps, int* splits) {
+// resident CTAs per SM of the attention kernel for head dim `hd` (sets the
+// kernel's dynamic shared-memory limit on first use per device)
+template <int HD, int STAGES>
+int ensure_attr_and_occupancy() {
+  using L = Layout<HD, STAGES>;
+  static int occ[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (occ[dev & 63] == 0) {
+    auto kern = paged_attn_kernel<HD, STAGES>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN_SMEM) !=
+        cudaSuccess)
+      return -1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, L::DYN_SMEM) != cudaSuccess ||
+        n < 1)
+      return -1;
+    occ[dev & 63] = n;
+  }
+  return occ[dev & 63];
+}
+
+inline int occupancy(int hd) {
+  return hd == 128 ? ensure_attr_and_occupancy<128, 8>() : ensure_attr_and_occupancy<64, 8>();
+}
+
+// Split plan: slices per (sequence, kv head) for a batch whose longest
+// sequence has max_seq_len tokens (window bounds the span). The kernel is
+// HBM-bound and its CTAs do equal work, so the slice count is chosen for
+// whole waves: among S with >= kMinSlice pages per slice, the one whose
+// B*nkv*S CTAs fill the last wave of (resident CTAs per SM x SMs) best, with
+// a small charge per slice for the extra partials. The kernel then splits
+// each sequence's actual pages evenly over its slices.
+inline int plan_splits(int B, int nkv, int hd, int max_seq_len, int window) {
   int span = max_seq_len;
   if (window > 0 && window + kBlock < span) span = window + kBlock;
   const int pages = (span + kBlock - 1) / kBlock;
-  if (pages <= 0 || B <= 0 || nkv <= 0) {
-    *pps = 1;
-    *splits = 1;
-    return;
+  if (pages <= 0 || B <= 0 || nkv <= 0) return 1;
+  const int occ = occupancy(hd);
+  const double slots = (double)(occ > 0 ? occ : 2) * num_sms();
+  const double pairs = (double)B * nkv;
+  int max_s = pages / kMinSlice;
+  if (max_s > 128) max_s = 128;
+  if (max_s < 1) max_s = 1;
+  int best_s = 1;
+  double best = -1.0;
+  for (int s = 1; s <= max_s; ++s) {
+    const double waves = pairs * s / slots;
+    const double eff = waves / ceil(waves);
+    const double score = eff - 0.002 * s;
+    if (score > best + 1e-9) {
+      best = score;
+      best_s = s;
+    }
   }
-  // about 2 waves of CTAs at 3 CTAs per SM, each slice >= 8 pages
-  const int target = 6 * num_sms();
-  const int groups = B * nkv;
-  int s = (target + groups - 1) / groups;
-  const int max_s = (pages + 7) / 8;
-  if (s > max_s) s = max_s;
-  if (s < 1) s = 1;
-  *pps = (pages + s - 1) / s;
-  *splits = (pages + *pps - 1) / *pps;
+  return best_s;
 }
 
 template <int HD, int STAGES>
 int launch(const Params& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t st) {
   using L = Layout<HD, STAGES>;
   auto kern = paged_attn_kernel<HD, STAGES>;
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_done[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN_SMEM);
-    if (e != cudaSuccess) {
-      set_last_error("fg_paged_decode_attn: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-      return FG_ERR_CUDA;
-    }
-    attr_done[dev & 63] = true;
+  if (ensure_attr_and_occupancy<HD, STAGES>() < 1) {
+    set_last_error("fg_paged_decode_attn: cannot set the kernel's shared-memory limit");
+    return FG_ERR_CUDA;
   }
   int rc = launch_k("fg_paged_decode_attn", kern, dim3(p.splits, p.nkv, p.B), dim3(kThreads),
                     L::DYN_SMEM, st, tk, tv, p);
@@ -409,16 +443,14 @@ int launch(const Params& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaSt
 
 extern "C" {
 
-int fg_attn_pages_per_split(int B, int nkv, int max_seq_len, int window) {
-  int pps, splits;
-  fg::attn::plan(B, nkv, max_seq_len, window, &pps, &splits);
-  return pps;
+int fg_attn_splits(int B, int nkv, int hd, int max_seq_len, int window) {
+  if (B <= 0 || nkv <= 0 || (hd != 64 && hd != 128) || max_seq_len <= 0) return 0;
+  return fg::attn::plan_splits(B, nkv, hd, max_seq_len, window);
 }
 
 size_t fg_attn_workspace_bytes(int B, int nq, int nkv, int hd, int max_seq_len, int window) {
-  if (B <= 0 || nq <= 0 || hd <= 0 || max_seq_len <= 0) return 0;
-  int pps, splits;
-  fg::attn::plan(B, nkv, max_seq_len, window, &pps, &splits);
+  if (B <= 0 || nq <= 0 || nkv <= 0 || (hd != 64 && hd != 128) || max_seq_len <= 0) return 0;
+  const int splits = fg::attn::plan_splits(B, nkv, hd, max_seq_len, window);
   if (splits <= 1) return 0;
   const size_t rows = (size_t)B * nq * splits;
   return ((rows * hd * sizeof(float) + 255) & ~size_t(255)) + rows * 2 * sizeof(float);
@@ -458,7 +490,7 @@ int fg_paged_decode_attn(const fg_bf16* q, const fg_bf16* k_cache, const fg_bf16
   p.num_blocks = num_blocks;
   p.window = window;
   p.scale_log2 = scale * kLog2e;
-  plan(B, nkv, max_seq_len, window, &p.pages_per_split, &p.splits);
+  p.splits = plan_splits(B, nkv, hd, max_seq_len, window);
   p.part_o = nullptr;
   p.part_ml = nullptr;
   if (p.splits > 1) {

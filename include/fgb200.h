@@ -154,9 +154,12 @@ int fg_paged_decode_attn(const fg_bf16* q, const fg_bf16* k_cache, const fg_bf16
                          fg_bf16* out, void* workspace, size_t workspace_bytes, int B, int nq,
                          int nkv, int hd, int block_size, int num_blocks, int max_blocks,
                          int max_seq_len, int window, float scale, fg_stream_t stream);
-/* Pages per split fg_paged_decode_attn uses for a batch of B sequences of at
- * most max_seq_len tokens (window as in fg_paged_decode_attn). */
-int fg_attn_pages_per_split(int B, int nkv, int max_seq_len, int window);
+/* Slices per (sequence, kv head) fg_paged_decode_attn plans for a batch of
+ * B sequences of at most max_seq_len tokens (window as in
+ * fg_paged_decode_attn): chosen so the B*nkv*slices CTAs fill whole waves of
+ * the GPU. Each sequence's actual pages are split evenly over its slices.
+ * 0 on bad sizes. */
+int fg_attn_splits(int B, int nkv, int hd, int max_seq_len, int window);
 /* Workspace bytes fg_paged_decode_attn needs for these sizes (0 if none). */
 size_t fg_attn_workspace_bytes(int B, int nq, int nkv, int hd, int max_seq_len, int window);
 
