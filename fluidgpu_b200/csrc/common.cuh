@@ -33,6 +33,7 @@ enum DeviceCode : unsigned int {
   DEV_MBAR_TIMEOUT = 1,    // an mbarrier wait ran past its deadline
   DEV_FLAG_TIMEOUT = 2,    // a peer flag wait ran past its deadline
   DEV_BAD_INDEX = 3,       // a block-table / slot / token index was out of range
+  DEV_SCALE_RANGE = 4,     // an MXFP4 block scale lies outside its row's exact window
 };
 
 __device__ __forceinline__ void record_device_error(unsigned int code, unsigned int site) {

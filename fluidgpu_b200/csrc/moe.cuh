@@ -11,15 +11,15 @@
 //                 y = act W2_e + b2_e (bf16)
 //   out[t] += y * score (bf16, experts in ascending order), then + residual.
 // Expert weights are MXFP4 (OCP microscaling: e2m1 values, one e8m0 scale per
-// 32 elements along K), dequantised to bf16 exactly as transformers'
-// convert_moe_packed_tensors does; the dequantisation happens in shared
-// memory, so HBM moves 4.25 bits per weight and only for routed experts.
+// 32 elements along K). The products equal those of transformers' exact bf16
+// dequantisation (convert_moe_packed_tensors); the values are decoded on the
+// SM into tensor memory, so HBM moves 4.25 bits per weight and only for
+// routed experts.
 //
 // Packed MXFP4 weight layout (fg_pack_mxfp4): per expert, per 128-row tile,
-// per 64-wide K step, a 4352-byte record: 128 rows x 32 bytes of e2m1 pairs
-// (low nibble = even k) followed by 128 rows x 2 e8m0 scales. For the fused
-// SwiGLU-OAI epilogue the gate/up rows are interleaved in blocks of 64 as in
-// the dense path (the caller orders rows before packing).
+// per 64-wide K step, a 4352-byte record (layout at pack_mxfp4_kernel). For
+// the fused SwiGLU-OAI epilogue the gate/up rows are interleaved in blocks of
+// 64 as in the dense path (the caller orders rows before packing).
 #pragma once
 #include "gemm.cuh"
 
@@ -182,7 +182,15 @@ __global__ void __launch_bounds__(1024) permute_kernel(
   }
 }
 
-// rows of x in permuted order: out[i] = x[perm_pair[i] / k]
+// bf16x2 -> f16x2 (exact in the f16 normal range)
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(__uint_as_float(w & 0xFFFF0000u)),
+      "f"(__uint_as_float(w << 16)));
+  return r;
+}
+
+// rows of x in permuted order, as f16: out[i] = x[perm_pair[i] / k]
 __global__ void gather_rows_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ perm_pair,
                                    int k, int H8, uint4* __restrict__ out) {
   griddep_wait();
@@ -191,7 +199,11 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ x, const int32_t* _
   const int t = perm_pair[i] / k;
   const uint4* src = x + (int64_t)t * H8;
   uint4* dst = out + (int64_t)i * H8;
-  for (int c = threadIdx.x; c < H8; c += blockDim.x) dst[c] = src[c];
+  for (int c = threadIdx.x; c < H8; c += blockDim.x) {
+    const uint4 v = src[c];
+    dst[c] = make_uint4(bf16x2_to_f16x2(v.x), bf16x2_to_f16x2(v.y), bf16x2_to_f16x2(v.z),
+                        bf16x2_to_f16x2(v.w));
+  }
 }
 
 // out[t] = residual[t] + sum over the k experts (ascending id) of y[inv] * w
@@ -230,6 +242,49 @@ __global__ void unpermute_kernel(const __nv_bfloat16* __restrict__ y, const int3
 // ---------------------------------------------------------------------------
 // MXFP4 packing: values [E][N][K/2] u8 + scales [E][N][K/32] u8 -> records
 // ---------------------------------------------------------------------------
+// Record (one expert, one 128-row tile, one 64-wide K step), 4352 bytes:
+//   [0, 2048)     K elements 0..31:  row r's 16 bytes of e2m1 pairs at r*16
+//   [2048, 4096)  K elements 32..63: row r at 2048 + r*16   (low nibble = even k)
+//   [4096, 4352)  row r's two block codes at 4096 + 2r: c = s - s_ref(row) + 24
+// The nkb records of one (expert, row tile) are followed by that tile's
+// s_ref int32 [128] (tile stride = nkb * 4352 + 512 bytes), s_ref(row) =
+// (largest exponent among the row's nonzero blocks) - 13. A block then dequantises
+// exactly in f16 as e2m1 * 2^(c-24) (c in [1, 37]: magnitudes 2^-24 .. 49152,
+// all multiples of the f16 subnormal step) and the epilogue multiplies the
+// fp32 accumulator by 2^(s_ref-127): the products are the bf16-dequantised
+// weights' products scaled by one power of two per row, so the result is
+// that of the exact bf16 dequantisation. A nonzero block more than 36
+// binades below its row's largest cannot be held exactly; packing records
+// DEV_SCALE_RANGE for it (real checkpoints stay far inside the window).
+constexpr int kRowRefBias = 13;
+constexpr int kSrefBytes = BM * 4;
+
+__host__ __device__ inline size_t tile_stride(int nkb) { return (size_t)nkb * kRecBytes + kSrefBytes; }
+
+__global__ void mxfp4_rowref_kernel(const uint8_t* __restrict__ vals, const uint8_t* __restrict__ scales,
+                                    uint8_t* __restrict__ packed, int E, int N, int K, int n_pad) {
+  griddep_wait();
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)E * n_pad) return;
+  const long long e = i / n_pad;
+  const int n = (int)(i % n_pad);
+  int smax = -1;
+  if (n < N) {
+    const uint8_t* v = vals + (e * N + n) * (K / 2);
+    const uint8_t* s = scales + (e * N + n) * (K / 32);
+    for (int b = 0; b < K / 32; ++b) {
+      const uint4 q = *reinterpret_cast<const uint4*>(v + b * 16);
+      // nonzero if any nibble has a nonzero magnitude (sign-only codes are zeros)
+      const bool nz = ((q.x | q.y | q.z | q.w) & 0x77777777u) != 0u;
+      if (nz && (int)s[b] > smax) smax = s[b];
+    }
+  }
+  const int nkb = K / BK;
+  int32_t* sref = reinterpret_cast<int32_t*>(packed + ((size_t)e * (n_pad / BM) + n / BM) * tile_stride(nkb) +
+                                             (size_t)nkb * kRecBytes);
+  sref[n % BM] = (smax < 0 ? 127 : smax) - kRowRefBias;
+}
+
 __global__ void pack_mxfp4_kernel(const uint8_t* __restrict__ vals, const uint8_t* __restrict__ scales,
                                   uint8_t* __restrict__ packed, int N, int K, int n_tiles, int nkb,
                                   long long records) {
@@ -239,65 +294,137 @@ __global__ void pack_mxfp4_kernel(const uint8_t* __restrict__ vals, const uint8_
   const int kb = (int)(rec % nkb);
   const int nt = (int)((rec / nkb) % n_tiles);
   const long long e = rec / ((long long)nkb * n_tiles);
-  uint8_t* dst = packed + rec * kRecBytes;
+  uint8_t* tile = packed + ((size_t)e * n_tiles + nt) * tile_stride(nkb);
+  uint8_t* dst = tile + (size_t)kb * kRecBytes;
+  const int32_t* sref = reinterpret_cast<const int32_t*>(tile + (size_t)nkb * kRecBytes);
   for (int i = threadIdx.x; i < kRecBytes; i += blockDim.x) {
     uint8_t v = 0;
     if (i < kValBytes) {
-      const int r = i >> 5, byte = i & 31;
-      const int n = nt * BM + r, kk = kb * BK + byte * 2;
+      const int h = i >> 11, r = (i & 2047) >> 4, j = i & 15;
+      const int n = nt * BM + r, kk = kb * BK + (h * 16 + j) * 2;
       if (n < N && kk < K) v = vals[(e * N + n) * (K / 2) + (kk >> 1)];
     } else {
-      const int j = i - kValBytes;
-      const int r = j >> 1, blk = j & 1;
+      const int q = i - kValBytes;
+      const int r = q >> 1, blk = q & 1;
       const int n = nt * BM + r, kk = kb * BK + blk * 32;
-      v = 127;  // scale 1.0 for padding (its values are zero)
-      if (n < N && kk < K) v = scales[(e * N + n) * (K / 32) + (kk >> 5)];
+      v = 24;  // multiplier 1 for padding (its values are zero)
+      if (n < N && kk < K) {
+        int c = (int)scales[(e * N + n) * (K / 32) + (kk >> 5)] - sref[r] + 24;
+        if (c < 1) {
+          const uint4 w = *reinterpret_cast<const uint4*>(vals + (e * N + n) * (K / 2) + (kk >> 1));
+          if (((w.x | w.y | w.z | w.w) & 0x77777777u) != 0u) record_device_error(DEV_SCALE_RANGE, 0x320);
+          c = 0;
+        }
+        v = (uint8_t)c;
+      }
     }
     dst[i] = v;
   }
 }
 
 // ---------------------------------------------------------------------------
-// MXFP4 x bf16 grouped GEMM (swap-AB, tcgen05 kind::f16 after an exact
-// in-shared-memory dequantisation of the weight tile)
+// MXFP4 x activation grouped GEMM (swap-AB). Weights are dequantised by the
+// hardware e2m1 -> f16 conversion straight into tensor memory and used as
+// the A operand of tcgen05.mma kind::f16 (A from TMEM, B = the f16
+// activation tile from shared memory). Nothing but the 4.25-bit records and
+// the activation tiles crosses shared memory, so the kernel streams HBM
+// instead of saturating shared-memory bandwidth with expanded tiles.
+//
+// Persistent: one CTA per SM walks the work units (permute item x 128-row
+// tile) u = blockIdx.x + j * gridDim.x. 16 warps:
+//   warp 0       producer: bulk copy of the record + 2-D TMA of the
+//                activation tile per K step into a deep ring
+//   warp 1       TMEM owner and MMA issuer (4 x K16 per K step into one of
+//                two accumulators, so the epilogue overlaps the next unit)
+//   warps 4-19   four converter warpgroups, K step i on warpgroup i % 4: a
+//                thread per weight row decodes its 64 values into the
+//                warpgroup's TMEM A stage with tcgen05.st
+//   warps 20-23  epilogue: accumulator x 2^(s_ref-127) + bias, SwiGLU-OAI
+//                (gate rows 0-63 of a tile, up rows 64-127; f16 out) or
+//                store (bf16 out)
 // ---------------------------------------------------------------------------
 struct GemmParams {
-  const uint8_t* w;           // packed records [E][n_tiles][nkb]
+  const uint8_t* w;           // packed tiles [E][n_tiles] of nkb records + s_ref[128]
   const __nv_bfloat16* bias;  // [E][N] (packed row order) or null
   const int32_t* offsets;     // [E+1] rows of each expert in x / out
   const int32_t* items;       // [max_items][2] = (expert, token tile)
   const int32_t* item_count;
-  __nv_bfloat16* out;         // [rows][ldo]
+  void* out;                  // [rows][ldo]: f16 after SwiGLU-OAI, else bf16
   int N, K, n_tiles, nkb, ldo, epilogue;
 };
 
-constexpr int kConvWarps = 8;
-constexpr int kMoeThreads = (2 + kConvWarps) * 32;  // producer, MMA, converters
+constexpr int kConvWG = 4;        // converter warpgroups
+constexpr int kConvWarp0 = 4;
+constexpr int kEpiWarp0 = kConvWarp0 + 4 * kConvWG;
+constexpr int kMoeWarps = kEpiWarp0 + 4;
+constexpr int kMoeThreads = kMoeWarps * 32;
+constexpr int kAStages = kConvWG; // TMEM A stage per converter warpgroup, 32 columns
+constexpr int kDCol0 = kAStages * 32;
 
-template <int BN, int STAGES>
+template <int BN>
 struct MLayout {
-  static constexpr int A_BYTES = BM * BK * 2;   // dequantised bf16 tile
-  static constexpr int X_BYTES = BN * BK * 2;
-  static constexpr int RAW_BYTES = 5120;         // >= kRecBytes, keeps 1 KB alignment
-  static constexpr int STAGE_BYTES = A_BYTES + X_BYTES + RAW_BYTES;
-  static constexpr int LUT_OFFSET = STAGES * STAGE_BYTES;   // 256 x bf16x2
-  static constexpr int XCH_OFFSET = LUT_OFFSET + 1024;      // bf16 [BN][64]
-  static constexpr int BAR_OFFSET = XCH_OFFSET + BN * 64 * 2;
-  static constexpr int MISC_OFFSET = BAR_OFFSET + (3 * STAGES + 1) * 8;
-  static constexpr int TOTAL = MISC_OFFSET + 32;
+  static constexpr int STAGES = BN <= 32 ? 16 : 12;
+  static constexpr int X_BYTES = BN * BK * 2;                  // [BN][64] 16-bit, 128B swizzle
+  static constexpr int REC_OFFSET = STAGES * X_BYTES;
+  static constexpr int XCH_OFFSET = REC_OFFSET + STAGES * kRecBytes;  // bf16 [BN][64]
+  static constexpr int BAR_OFFSET = (XCH_OFFSET + BN * 64 * 2 + 7) / 8 * 8;
+  // raw_full[S] raw_empty[S] a_full[A] a_empty[A] acc_full[2] acc_empty[2] mma_done
+  static constexpr int MISC_OFFSET = BAR_OFFSET + (2 * STAGES + 2 * kAStages + 5) * 8;
+  static constexpr int TOTAL = MISC_OFFSET + 16;
   static constexpr int DYN_SMEM = TOTAL + 1024;
-  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
-  static_assert(RAW_BYTES >= kRecBytes && STAGE_BYTES % 1024 == 0, "stage layout");
+  static constexpr uint32_t TMEM_COLS = 256;  // A ring 128 + two accumulators of BN <= 64
+  static_assert(X_BYTES % 1024 == 0 && kRecBytes % 16 == 0, "stage alignment");
+  static_assert(kDCol0 + 2 * BN <= (int)TMEM_COLS, "tensor memory budget");
 };
 
-// bf16 bits of the 16 e2m1 codes (sign, 2-bit exponent, 1-bit mantissa)
-__device__ __forceinline__ uint32_t e2m1_bf16_bits(uint32_t c) {
-  const uint32_t mag = c & 7u;
-  uint32_t bits;
-  if (mag == 0) bits = 0;
-  else if (mag == 1) bits = 0x3F00u;  // 0.5
-  else bits = ((mag >> 1) + 126u) << 7 | ((mag & 1u) << 6);  // 2^(e-1) * (1 + m/2)
-  return bits | ((c & 8u) << 12);
+// instruction descriptor for kind::f16 with f16 A/B, fp32 D, K-major
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&a)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]),
+      "r"(a[8]), "r"(a[9]), "r"(a[10]), "r"(a[11]), "r"(a[12]), "r"(a[13]), "r"(a[14]), "r"(a[15]),
+      "r"(a[16]), "r"(a[17]), "r"(a[18]), "r"(a[19]), "r"(a[20]), "r"(a[21]), "r"(a[22]), "r"(a[23]),
+      "r"(a[24]), "r"(a[25]), "r"(a[26]), "r"(a[27]), "r"(a[28]), "r"(a[29]), "r"(a[30]), "r"(a[31])
+      : "memory");
+}
+
+// four bytes of e2m1 pairs -> four f16x2 (low nibble in the low half)
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t v, uint32_t* o) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(v));
+}
+
+// f16 bits of 2^(c-24), c in [0, 37], in both halves
+__device__ __forceinline__ uint32_t pow2_f16x2(uint32_t c) {
+  const uint32_t h = c >= 10u ? (c - 9u) << 10 : 1u << c;
+  return h | (h << 16);
+}
+
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
 }
 
 __device__ __forceinline__ float swiglu_oai(float g, float u) {
@@ -310,51 +437,63 @@ __device__ __forceinline__ float swiglu_oai(float g, float u) {
   return rbf(rbf(u + 1.f) * glu);
 }
 
-template <int BN, int STAGES>
+// (expert, first row, end row, row tile) of work unit u
+struct Unit {
+  int e, row0, row_end, nt;
+};
+__device__ __forceinline__ Unit unit_of(const GemmParams& p, int u, int BN) {
+  const int item = u / p.n_tiles;
+  Unit w;
+  w.nt = u - item * p.n_tiles;
+  w.e = p.items[2 * item];
+  w.row0 = p.offsets[w.e] + p.items[2 * item + 1] * BN;
+  w.row_end = p.offsets[w.e + 1];
+  return w;
+}
+
+template <int BN>
 __global__ void __launch_bounds__(kMoeThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const GemmParams p) {
-  using L = MLayout<BN, STAGES>;
+  using L = MLayout<BN>;
+  constexpr int S = L::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  griddep_wait();  // routing results come from the permute kernel
-  if (threadIdx.x == 0) griddep_launch_dependents();
-  const int item = blockIdx.y;
-  if (item >= *p.item_count) return;
-  const int e = p.items[2 * item];
-  const int t_tile = p.items[2 * item + 1];
-  const int row0 = p.offsets[e] + t_tile * BN;
-  const int row_end = p.offsets[e + 1];
-  const int n_tile = blockIdx.x;
-  const int nkb = p.nkb;
-
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar_full = sbase + L::BAR_OFFSET;  // TMA landed (raw + x)
-  const uint32_t bar_conv = bar_full + STAGES * 8;  // converters done
-  const uint32_t bar_empty = bar_conv + STAGES * 8; // MMA done with the stage
-  const uint32_t bar_accf = bar_empty + STAGES * 8;
+  const uint32_t raw_full = sbase + L::BAR_OFFSET;
+  const uint32_t raw_empty = raw_full + S * 8;
+  const uint32_t a_full = raw_empty + S * 8;
+  const uint32_t a_empty = a_full + kAStages * 8;
+  const uint32_t acc_full = a_empty + kAStages * 8;
+  const uint32_t acc_empty = acc_full + 2 * 8;
+  const uint32_t mma_done = acc_empty + 2 * 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFFSET);
-  int* misc = reinterpret_cast<int*>(smem + L::MISC_OFFSET + 16);
-  uint32_t* lut = reinterpret_cast<uint32_t*>(smem + L::LUT_OFFSET);
+  int* issued_out = reinterpret_cast<int*>(smem + L::MISC_OFFSET + 8);
   __nv_bfloat16* xch = reinterpret_cast<__nv_bfloat16*>(smem + L::XCH_OFFSET);
 
-  // byte -> two bf16 (low nibble first) lookup table
-  for (int i = threadIdx.x; i < 256; i += blockDim.x)
-    lut[i] = e2m1_bf16_bits(i & 15u) | (e2m1_bf16_bits(i >> 4) << 16);
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(bar_full + 8 * s, 1);
-      mbar_init(bar_conv + 8 * s, kConvWarps);
-      mbar_init(bar_empty + 8 * s, 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(raw_full + 8 * s, 1);
+      mbar_init(raw_empty + 8 * s, 4 + 1);  // converter warps + MMA commit
     }
-    mbar_init(bar_accf, 1);
-    misc[0] = 0;
-    misc[1] = 0;
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(a_full + 8 * s, 4);
+      mbar_init(a_empty + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + 8 * b, 1);
+      mbar_init(acc_empty + 8 * b, 4);
+    }
+    mbar_init(mma_done, 1);
+    *issued_out = 0;
     fence_mbar_init();
     prefetch_tensormap(&tm_x);
   }
-  if (warp == 0) {
+  // routing results come from the permute kernel; the tensor memory is
+  // allocated only after the previous kernel has finished with the SM's
+  griddep_wait();
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
                  "r"(L::TMEM_COLS)
@@ -365,126 +504,159 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
   __syncthreads();
   gemm::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) griddep_launch_dependents();
+
+  const int U = *p.item_count * p.n_tiles;
+  const int G = gridDim.x;
+  const int my_units = (int)blockIdx.x < U ? (U - 1 - (int)blockIdx.x) / G + 1 : 0;
+  const int nkb = p.nkb;
+  const int NK = my_units * nkb;  // K steps this CTA runs
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- producer ----------------
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
-      const uint8_t* wrec = p.w + ((size_t)e * p.n_tiles + n_tile) * nkb * kRecBytes;
-      int issued = 0;
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-        if (!mbar_wait(bar_empty + 8 * s, ph ^ 1u, 0x311)) break;
-        const uint32_t st = sbase + s * L::STAGE_BYTES;
-        mbar_arrive_expect_tx(bar_full + 8 * s, kRecBytes + L::X_BYTES);
-        bulk_load(st + L::A_BYTES + L::X_BYTES, wrec + (size_t)i * kRecBytes, kRecBytes,
-                  bar_full + 8 * s, pol_w);
-        tma_load_2d_hint(st + L::A_BYTES, &tm_x, bar_full + 8 * s, i * BK, row0, pol_x);
-        ++issued;
+      int i = 0;
+      bool ok = true;
+      for (int j = 0; j < my_units && ok; ++j) {
+        const Unit w = unit_of(p, blockIdx.x + j * G, BN);
+        const uint8_t* wrec = p.w + ((size_t)w.e * p.n_tiles + w.nt) * tile_stride(nkb);
+        for (int kb = 0; kb < nkb; ++kb, ++i) {
+          const int s = i % S;
+          if (!mbar_wait(raw_empty + 8 * s, ((uint32_t)(i / S) & 1u) ^ 1u, 0x321)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(raw_full + 8 * s, kRecBytes + L::X_BYTES);
+          bulk_load(sbase + L::REC_OFFSET + s * kRecBytes, wrec + (size_t)kb * kRecBytes, kRecBytes,
+                    raw_full + 8 * s, pol_w);
+          tma_load_2d_hint(sbase + s * L::X_BYTES, &tm_x, raw_full + 8 * s, kb * BK, w.row0, pol_x);
+        }
       }
-      misc[0] = issued;
+      *issued_out = i;
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = gemm::idesc_bf16(BM, BN);
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-        if (!mbar_wait(bar_conv + 8 * s, ph, 0x312)) break;
+      constexpr uint32_t idesc = idesc_f16(BM, BN);
+      int i = 0;
+      bool ok = true;
+      for (int j = 0; j < my_units && ok; ++j) {
+        const int buf = j & 1;
+        if (!mbar_wait(acc_empty + 8 * buf, ((uint32_t)(j >> 1) & 1u) ^ 1u, 0x322)) break;
         gemm::tc_fence_after();
-        const uint32_t st = sbase + s * L::STAGE_BYTES;
-        const uint64_t adesc = gemm::sw128_kmajor_desc(st);
-        const uint64_t bdesc = gemm::sw128_kmajor_desc(st + L::A_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          gemm::tc_mma(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-        gemm::tc_commit(bar_empty + 8 * s);
-        misc[1] = i + 1;
-      }
-      gemm::tc_commit(bar_accf);
-    }
-  } else {
-    // ---------------- converters: e2m1 + e8m0 -> bf16, 128-byte-swizzled K-major ----------------
-    const int ct = threadIdx.x - 64;  // 0 .. 255
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % STAGES;
-      const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-      const bool ok = mbar_wait(bar_full + 8 * s, ph, 0x313);
-      uint8_t* st = smem + s * L::STAGE_BYTES;
-      const uint8_t* raw = st + L::A_BYTES + L::X_BYTES;
-      if (ok) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int q = ct + j * 256;  // 16-byte output chunk: row r, chunk c (8 values)
-          const int r = q >> 3, c = q & 7;
-          const uint32_t v4 = *reinterpret_cast<const uint32_t*>(raw + r * 32 + c * 4);
-          const uint32_t sc = raw[kValBytes + r * 2 + (c >> 2)];
-          // 2^(sc-127) as bf16x2 (exact power of two; e8m0 0 and 255 are not produced here)
-          const uint32_t sb = (sc & 0xFFu) << 7;
-          uint32_t sbits = sb | (sb << 16);
-          const __nv_bfloat162 s2 = *reinterpret_cast<const __nv_bfloat162*>(&sbits);
-          uint4 o;
-          uint32_t* po = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const uint32_t pair = lut[(v4 >> (8 * b)) & 0xFFu];
-            __nv_bfloat162 v2 = *reinterpret_cast<const __nv_bfloat162*>(&pair);
-            v2 = __hmul2(v2, s2);
-            po[b] = *reinterpret_cast<uint32_t*>(&v2);
+        const uint32_t d = tmem + kDCol0 + buf * BN;
+        for (int kb = 0; kb < nkb; ++kb, ++i) {
+          const int s = i % S, sa = i % kAStages;
+          if (!mbar_wait(a_full + 8 * sa, (uint32_t)(i / kAStages) & 1u, 0x323)) {
+            ok = false;
+            break;
           }
-          *reinterpret_cast<uint4*>(st + r * 128 + ((c ^ (r & 7)) << 4)) = o;
+          gemm::tc_fence_after();
+          const uint64_t bdesc = gemm::sw128_kmajor_desc(sbase + s * L::X_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc_mma_ts(d, tmem + sa * 32 + kk * 8, bdesc + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          gemm::tc_commit(a_empty + 8 * sa);
+          gemm::tc_commit(raw_empty + 8 * s);
         }
+        if (ok) gemm::tc_commit(acc_full + 8 * buf);
       }
-      fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_conv + 8 * s);
+      // every MMA of this thread has completed before the CTA moves on
+      gemm::tc_commit(mma_done);
+      mbar_wait(mma_done, 0, 0x324);
     }
-    // ---------------- epilogue: warps 2..5 read the four TMEM lane quarters ----------------
-    if (warp < 6) {
-      const int q = warp & 3;
-      const int row = q * 32 + lane;
-      const bool acc_ok = mbar_wait(bar_accf, 0, 0x314);
+  } else if (warp >= kConvWarp0 && warp < kEpiWarp0) {
+    // ---------------- converters ----------------
+    const int wg = (warp - kConvWarp0) >> 2, q = warp & 3;
+    const int t = q * 32 + lane;  // weight row of this thread, also its TMEM lane
+    for (int i = wg; i < NK; i += kConvWG) {
+      const int s = i % S, sa = i % kAStages;
+      if (!mbar_wait(raw_full + 8 * s, (uint32_t)(i / S) & 1u, 0x325)) break;
+      if (!mbar_wait(a_empty + 8 * sa, ((uint32_t)(i / kAStages) & 1u) ^ 1u, 0x326)) break;
       gemm::tc_fence_after();
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
-      const __nv_bfloat16* bias = p.bias ? p.bias + (size_t)e * p.N : nullptr;
+      // weight row t: 64 e2m1 values -> 32 f16x2 columns of the A stage
+      const uint8_t* rec = smem + L::REC_OFFSET + s * kRecBytes;
+      const uint4 v0 = *reinterpret_cast<const uint4*>(rec + t * 16);
+      const uint4 v1 = *reinterpret_cast<const uint4*>(rec + 2048 + t * 16);
+      const uint32_t codes = *reinterpret_cast<const uint16_t*>(rec + kValBytes + 2 * t);
+      const uint32_t m0 = pow2_f16x2(codes & 0xFFu), m1 = pow2_f16x2(codes >> 8);
+      uint32_t a[32];
+      e2m1x8_to_f16x2(v0.x, a + 0);
+      e2m1x8_to_f16x2(v0.y, a + 4);
+      e2m1x8_to_f16x2(v0.z, a + 8);
+      e2m1x8_to_f16x2(v0.w, a + 12);
+      e2m1x8_to_f16x2(v1.x, a + 16);
+      e2m1x8_to_f16x2(v1.y, a + 20);
+      e2m1x8_to_f16x2(v1.z, a + 24);
+      e2m1x8_to_f16x2(v1.w, a + 28);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) a[c] = hmul2_bits(a[c], m0);
+#pragma unroll
+      for (int c = 16; c < 32; ++c) a[c] = hmul2_bits(a[c], m1);
+      tc_st32(tmem + ((uint32_t)(q * 32) << 16) + sa * 32, a);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      gemm::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(a_full + 8 * sa);
+        mbar_arrive(raw_empty + 8 * s);
+      }
+    }
+  } else if (warp >= kEpiWarp0) {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    // every epilogue warp runs all units (the named barriers below stay
+    // matched); after a failed wait the rest are written as zeros unwaited
+    bool failed = false;
+    for (int j = 0; j < my_units; ++j) {
+      const int buf = j & 1;
+      const bool acc_ok = !failed && mbar_wait(acc_full + 8 * buf, (uint32_t)(j >> 1) & 1u, 0x327);
+      failed = !acc_ok;
+      gemm::tc_fence_after();
+      const Unit w = unit_of(p, blockIdx.x + j * G, BN);
+      const int nrow = w.nt * BM + row;
+      const int32_t* sref = reinterpret_cast<const int32_t*>(
+          p.w + ((size_t)w.e * p.n_tiles + w.nt) * tile_stride(p.nkb) + (size_t)p.nkb * kRecBytes);
+      const float rs = ldexpf(1.f, sref[row] - 127);
+      const float b = (p.bias && nrow < p.N) ? bf2f(p.bias[(size_t)w.e * p.N + nrow]) : 0.f;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + kDCol0 + buf * BN;
       if (p.epilogue == FG_EPI_SWIGLU_OAI) {
         if (q >= 2) {
-          const int nrow = n_tile * BM + row;
-          const float b = (bias && nrow < p.N) ? bf2f(bias[nrow]) : 0.f;
 #pragma unroll 1
           for (int j0 = 0; j0 < BN; j0 += 16) {
             float v[16];
             gemm::tc_ld16(taddr + j0, v);
 #pragma unroll
-            for (int ii = 0; ii < 16; ++ii) xch[(j0 + ii) * 64 + (row - 64)] = f2bf(acc_ok ? v[ii] + b : 0.f);
+            for (int ii = 0; ii < 16; ++ii)
+              xch[(j0 + ii) * 64 + (row - 64)] = f2bf(acc_ok ? v[ii] * rs + b : 0.f);
           }
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (q < 2) {
-          const int nrow = n_tile * BM + row;
-          const float b = (bias && nrow < p.N) ? bf2f(bias[nrow]) : 0.f;
-          const int f = n_tile * 64 + row;
+          const int f = w.nt * 64 + row;
 #pragma unroll 1
           for (int j0 = 0; j0 < BN; j0 += 16) {
             float v[16];
             gemm::tc_ld16(taddr + j0, v);
 #pragma unroll
             for (int ii = 0; ii < 16; ++ii) {
-              const int rr = row0 + j0 + ii;
-              if (rr < row_end && nrow < p.N) {
-                const float g = rbf((acc_ok ? v[ii] : 0.f) + b);
+              const int rr = w.row0 + j0 + ii;
+              if (rr < w.row_end && nrow < p.N) {
+                const float g = rbf((acc_ok ? v[ii] : 0.f) * rs + b);
                 const float u = bf2f(xch[(j0 + ii) * 64 + row]);
-                p.out[(int64_t)rr * p.ldo + f] = f2bf(swiglu_oai(g, u));
+                reinterpret_cast<__half*>(p.out)[(int64_t)rr * p.ldo + f] = __float2half_rn(swiglu_oai(g, u));
               }
             }
           }
         }
+        gemm::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + 8 * buf);
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // xch is free for the next unit
       } else {
-        const int nrow = n_tile * BM + row;
-        const float b = (bias && nrow < p.N) ? bf2f(bias[nrow]) : 0.f;
 #pragma unroll 1
         for (int j0 = 0; j0 < BN; j0 += 16) {
           float v[16];
@@ -492,10 +664,15 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
           if (nrow >= p.N) continue;
 #pragma unroll
           for (int ii = 0; ii < 16; ++ii) {
-            const int rr = row0 + j0 + ii;
-            if (rr < row_end) p.out[(int64_t)rr * p.ldo + nrow] = f2bf((acc_ok ? v[ii] : 0.f) + b);
+            const int rr = w.row0 + j0 + ii;
+            if (rr < w.row_end)
+              reinterpret_cast<__nv_bfloat16*>(p.out)[(int64_t)rr * p.ldo + nrow] =
+                  f2bf((acc_ok ? v[ii] : 0.f) * rs + b);
           }
         }
+        gemm::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + 8 * buf);
       }
     }
   }
@@ -503,14 +680,15 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
   gemm::tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int i = misc[1]; i < misc[0]; ++i)
-      mbar_wait(bar_full + 8 * (i % STAGES), (uint32_t)(i / STAGES) & 1u, 0x315);
+    // no copy may land after the CTA exits: wait for the last issued K steps
+    const int issued = *issued_out;
+    for (int i = issued - S < 0 ? 0 : issued - S; i < issued; ++i)
+      mbar_wait(raw_full + 8 * (i % S), (uint32_t)(i / S) & 1u, 0x328);
   }
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     gemm::tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(L::TMEM_COLS)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::TMEM_COLS)
                  : "memory");
   }
 }
@@ -543,8 +721,10 @@ int fg_moe_max_items(int T, int k, int E, int BN) {
 }
 
 int fg_moe_tile_tokens(int T, int k, int E) {
+  // room for twice the mean rows per expert, so most experts stream their
+  // weights once (one token tile)
   const int avg = (T * k + E - 1) / (E > 0 ? E : 1);
-  return avg <= 16 ? 16 : (avg <= 32 ? 32 : 64);
+  return avg <= 8 ? 16 : (avg <= 16 ? 32 : 64);
 }
 
 int fg_moe_permute(const int32_t* indices, int T, int k, int E, int BN, int32_t* offsets,
@@ -559,7 +739,7 @@ int fg_moe_permute(const int32_t* indices, int T, int k, int E, int BN, int32_t*
                       offsets, perm_pair, inv, items, item_count);
 }
 
-int fg_moe_gather(const fg_bf16* x, const int32_t* perm_pair, int T, int k, int H, fg_bf16* out,
+int fg_moe_gather(const fg_bf16* x, const int32_t* perm_pair, int T, int k, int H, fg_f16* out,
                   fg_stream_t stream) {
   FG_REQUIRE(x && perm_pair && out, "fg_moe_gather: null pointer");
   FG_REQUIRE(T >= 0 && k > 0 && H % 8 == 0, "fg_moe_gather: bad sizes");
@@ -583,24 +763,29 @@ int fg_moe_unpermute(const fg_bf16* y, const int32_t* inv, const int32_t* indice
 }
 
 size_t fg_mxfp4_packed_bytes(int E, int N, int K) {
-  if (E <= 0 || N <= 0 || K <= 0) return 0;
-  return (size_t)E * ((N + 127) / 128) * ((K + 63) / 64) * fg::moe::kRecBytes;
+  if (E <= 0 || N <= 0 || K <= 0 || K % 64) return 0;
+  return (size_t)E * ((N + 127) / 128) * fg::moe::tile_stride(K / 64);
 }
 
 int fg_pack_mxfp4(const uint8_t* values, const uint8_t* scales, void* packed, int E, int N, int K,
                   fg_stream_t stream) {
   FG_REQUIRE(values && scales && packed, "fg_pack_mxfp4: null pointer");
-  FG_REQUIRE(E > 0 && N > 0 && K > 0 && K % 32 == 0, "fg_pack_mxfp4: K=%d must be a multiple of 32", K);
-  const int n_tiles = (N + 127) / 128, nkb = (K + 63) / 64;
+  FG_REQUIRE(E > 0 && N > 0 && K > 0 && K % 64 == 0, "fg_pack_mxfp4: K=%d must be a multiple of 64", K);
+  FG_REQUIRE((((uintptr_t)values | (uintptr_t)packed) & 15) == 0, "fg_pack_mxfp4: values/packed alignment");
+  const int n_tiles = (N + 127) / 128, nkb = K / 64, n_pad = n_tiles * 128;
   const long long records = (long long)E * n_tiles * nkb;
-  return fg::launch_k("fg_pack_mxfp4", fg::moe::pack_mxfp4_kernel, dim3((unsigned)records), dim3(256),
-                      0, (cudaStream_t)stream, values, scales, reinterpret_cast<uint8_t*>(packed), N, K,
-                      n_tiles, nkb, records);
+  uint8_t* out = reinterpret_cast<uint8_t*>(packed);
+  const long long rows = (long long)E * n_pad;
+  int rc = fg::launch_k("fg_pack_mxfp4(rows)", fg::moe::mxfp4_rowref_kernel, dim3((unsigned)((rows + 255) / 256)),
+                        dim3(256), 0, (cudaStream_t)stream, values, scales, out, E, N, K, n_pad);
+  if (rc) return rc;
+  return fg::launch_k("fg_pack_mxfp4", fg::moe::pack_mxfp4_kernel, dim3((unsigned)records), dim3(256), 0,
+                      (cudaStream_t)stream, values, scales, out, N, K, n_tiles, nkb, records);
 }
 
-int fg_moe_gemm_mxfp4(const fg_bf16* x, const void* w_packed, const fg_bf16* bias,
+int fg_moe_gemm_mxfp4(const fg_f16* x, const void* w_packed, const fg_bf16* bias,
                       const int32_t* offsets, const int32_t* items, const int32_t* item_count,
-                      int max_items, fg_bf16* out, int rows, int N, int K, int BN, int epilogue,
+                      int max_items, void* out, int rows, int N, int K, int BN, int epilogue,
                       fg_stream_t stream) {
   using namespace fg::moe;
   FG_REQUIRE(x && w_packed && offsets && items && item_count && out, "fg_moe_gemm_mxfp4: null pointer");
@@ -618,7 +803,7 @@ int fg_moe_gemm_mxfp4(const fg_bf16* x, const void* w_packed, const fg_bf16* bia
   p.offsets = offsets;
   p.items = items;
   p.item_count = item_count;
-  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.out = out;
   p.N = N;
   p.K = K;
   p.n_tiles = (N + 127) / 128;
@@ -630,6 +815,7 @@ int fg_moe_gemm_mxfp4(const fg_bf16* x, const void* w_packed, const fg_bf16* bia
                                  CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   cudaStream_t st = (cudaStream_t)stream;
+  const int grid = std::min(fg::num_sms(), max_items * p.n_tiles);
   auto go = [&](auto kern, int smem) -> int {
     static bool done[3][64] = {{false}};
     int dev = 0;
@@ -643,12 +829,11 @@ int fg_moe_gemm_mxfp4(const fg_bf16* x, const void* w_packed, const fg_bf16* bia
       }
       done[slot][dev & 63] = true;
     }
-    return fg::launch_k("fg_moe_gemm_mxfp4", kern, dim3(p.n_tiles, max_items), dim3(kMoeThreads), smem,
-                        st, tx, p);
+    return fg::launch_k("fg_moe_gemm_mxfp4", kern, dim3(grid), dim3(kMoeThreads), smem, st, tx, p);
   };
-  if (BN == 16) return go(moe_gemm_kernel<16, 4>, MLayout<16, 4>::DYN_SMEM);
-  if (BN == 32) return go(moe_gemm_kernel<32, 4>, MLayout<32, 4>::DYN_SMEM);
-  return go(moe_gemm_kernel<64, 4>, MLayout<64, 4>::DYN_SMEM);
+  if (BN == 16) return go(moe_gemm_kernel<16>, MLayout<16>::DYN_SMEM);
+  if (BN == 32) return go(moe_gemm_kernel<32>, MLayout<32>::DYN_SMEM);
+  return go(moe_gemm_kernel<64>, MLayout<64>::DYN_SMEM);
 }
 
 }  // extern "C"

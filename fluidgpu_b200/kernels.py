@@ -119,7 +119,8 @@ def check_device(what: str = "fgb200") -> None:
     if st:
         kind = st & 0xFF
         site = st >> 8
-        names = {1: "pipeline wait timeout", 2: "peer flag timeout", 3: "index out of range"}
+        names = {1: "pipeline wait timeout", 2: "peer flag timeout", 3: "index out of range",
+                 4: "MXFP4 block scale outside the row's exact range"}
         raise RuntimeError(f"{what}: device-side failure '{names.get(kind, kind)}' at site {site:#x}")
 
 

@@ -3,6 +3,7 @@
   python -m fluidgpu_b200.microbench attn  [--batch B] [--context L] [--window W]
   python -m fluidgpu_b200.microbench gemm  [--T T] [--N N] [--K K] [--epilogue store|residual|swiglu]
   python -m fluidgpu_b200.microbench sweep-attn      # B in {1,32,256} x ctx in {512,4096,32768}
+  python -m fluidgpu_b200.microbench moe   [--T T]  # gpt-oss MXFP4 expert GEMMs, 32 experts top-4
   torchrun --nproc-per-node 2 -m fluidgpu_b200.microbench handoff
       # [T,H] bf16 hand-off GPU0 -> GPU1, T in {1,8,64,256,1024,8192}, H in {2880,4096}:
       # NVLink mailbox put/recv (P2PComm) against NCCL send/recv, one-way time
@@ -132,6 +133,46 @@ def bench_gemm(T: int, N: int, K: int, epilogue: str = "store", iters: int = 20,
             "frac_hbm": gbs / peak, "peak": f"{src} {peak} GB/s", "timing": "graph" if GRAPH else "eager"}
 
 
+def bench_moe(T: int = 128, E: int = 32, k: int = 4, H: int = 2880, I: int = 2880, iters: int = 20,
+              warmup: int = 5, seed: int = 3) -> list[dict]:
+    """gpt-oss expert GEMMs: MXFP4 gate_up (+bias, SwiGLU-OAI) and down (+bias)
+    over T tokens routed top-k among E experts (uniform random routing)."""
+    from . import moe
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    w1 = torch.empty((E, 2 * I, H), device="cuda").normal_(0, 0.02, generator=g)
+    w2 = torch.empty((E, H, I), device="cuda").normal_(0, 0.02, generator=g)
+    v1, s1 = moe.quantize_mxfp4(w1)
+    v2, s2 = moe.quantize_mxfp4(w2)
+    del w1, w2
+    p1, p2 = moe.pack_mxfp4(v1.contiguous(), s1.contiguous()), moe.pack_mxfp4(v2.contiguous(), s2.contiguous())
+    b1 = torch.zeros((E, 2 * I), dtype=torch.bfloat16, device="cuda")
+    b2 = torch.zeros((E, H), dtype=torch.bfloat16, device="cuda")
+    idx = torch.stack([torch.randperm(E, device="cuda", generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    r = moe.Routing(idx, E)
+    x = torch.empty((T * k, H), dtype=torch.float16, device="cuda").normal_(generator=g)
+    act = torch.empty((T * k, I), dtype=torch.float16, device="cuda").normal_(generator=g)
+    touched = int((torch.bincount(idx.reshape(-1).long(), minlength=E) > 0).sum())
+    peak, src = _peak_hbm()
+    out = []
+    for name, xin, wp, bias, N, K, epi in (
+            ("gate_up", x, p1, b1, 2 * I, H, _lib.FG_EPI_SWIGLU_OAI),
+            ("down", act, p2, b2, H, I, _lib.FG_EPI_STORE)):
+        fn = lambda: moe.grouped_gemm(xin, wp, bias, r, N, K, epi)  # noqa: E731
+        ms = _time(fn, iters, warmup)
+        wbytes = touched * ((N + 127) // 128) * (K // 64) * 4352
+        n_out = N // 2 if epi == _lib.FG_EPI_SWIGLU_OAI else N
+        nbytes = wbytes + T * k * (K + n_out) * 2
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out.append({"kernel": "fg_moe_gemm_mxfp4", "gemm": name, "T": T, "E": E, "k": k, "N": N, "K": K,
+                    "experts_touched": touched, "BN": r.BN, "items": int(r.item_count.item()),
+                    "ms": ms, "bytes": nbytes, "GBps": gbs, "frac_hbm": gbs / peak,
+                    "TFLOPs": 2.0 * T * k * N * K / (ms * 1e-3) / 1e12,
+                    "peak": f"{src} {peak} GB/s", "timing": "graph" if GRAPH else "eager"})
+    kernels.check_device("moe microbench")
+    return out
+
+
 def bench_handoff(iters: int = 50, warmup: int = 10) -> None:
     """Ping-pong [T,H] between ranks 0 and 1; one-way time = round trip / 2."""
     import os
@@ -210,7 +251,7 @@ def bench_handoff(iters: int = 50, warmup: int = 10) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["attn", "gemm", "sweep-attn", "llama-gemms", "handoff"])
+    ap.add_argument("what", choices=["attn", "gemm", "sweep-attn", "llama-gemms", "handoff", "moe"])
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--window", type=int, default=0)
@@ -239,6 +280,9 @@ def main() -> None:
     elif a.what == "gemm":
         print(json.dumps(bench_gemm(a.T, a.N, a.K, a.epilogue, a.iters, a.warmup, splits=a.splits,
                                     packed=not a.rowmajor)))
+    elif a.what == "moe":
+        for line in bench_moe(a.T, iters=a.iters, warmup=a.warmup):
+            print(json.dumps(line), flush=True)
     elif a.what == "sweep-attn":
         for B in (1, 32, 256):
             for ctx in (512, 4096, 32768):

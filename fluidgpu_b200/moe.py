@@ -171,9 +171,14 @@ class Routing:
 
 def grouped_gemm(x_perm: torch.Tensor, w_packed: torch.Tensor, bias: torch.Tensor | None,
                  routing: Routing, N: int, K: int, epilogue: int) -> torch.Tensor:
+    """x_perm: f16 rows (fg_moe_gather's output, or a previous SwiGLU-OAI call's).
+    Returns f16 [rows, N/2] after SwiGLU-OAI (bf16-rounded values), bf16 [rows, N]
+    after a plain store."""
+    assert x_perm.dtype == torch.float16, f"expert GEMM operands are f16 rows, got {x_perm.dtype}"
     rows = x_perm.shape[0]
-    n_out = N // 2 if epilogue == _lib.FG_EPI_SWIGLU_OAI else N
-    out = torch.empty((rows, n_out), dtype=torch.bfloat16, device=x_perm.device)
+    swiglu = epilogue == _lib.FG_EPI_SWIGLU_OAI
+    n_out = N // 2 if swiglu else N
+    out = torch.empty((rows, n_out), dtype=torch.float16 if swiglu else torch.bfloat16, device=x_perm.device)
     call("fg_moe_gemm_mxfp4", x_perm.data_ptr(), w_packed.data_ptr(),
          None if bias is None else bias.data_ptr(), routing.offsets.data_ptr(),
          routing.items.data_ptr(), routing.item_count.data_ptr(), routing.max_items,
@@ -189,7 +194,7 @@ def experts_forward(x: torch.Tensor, idx: torch.Tensor, weights: torch.Tensor, W
     E, H_, I = W["moe_shape"]
     k = idx.shape[1]
     routing = Routing(idx, E)
-    x_perm = torch.empty((T * k, H), dtype=torch.bfloat16, device=x.device)
+    x_perm = torch.empty((T * k, H), dtype=torch.float16, device=x.device)
     call("fg_moe_gather", x.data_ptr(), routing.perm_pair.data_ptr(), T, k, H, x_perm.data_ptr(),
          kernels._stream(x.device))
     act = grouped_gemm(x_perm, W["moe_w1"], W["moe_b1"], routing, 2 * I, H, _lib.FG_EPI_SWIGLU_OAI)

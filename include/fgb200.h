@@ -27,6 +27,7 @@ extern "C" {
 #endif
 
 typedef uint16_t fg_bf16;          /* bfloat16 bit pattern */
+typedef uint16_t fg_f16;           /* IEEE binary16 bit pattern */
 typedef struct CUstream_st* fg_stream_t; /* == cudaStream_t */
 
 /* status codes (ProcessGroupComm raises AssertionError / RuntimeError in the
@@ -204,8 +205,10 @@ int fg_moe_max_items(int T, int k, int E, int BN);
 int fg_moe_permute(const int32_t* indices, int T, int k, int E, int BN, int32_t* offsets,
                    int32_t* perm_pair, int32_t* inv, int32_t* items, int32_t* item_count,
                    fg_stream_t stream);
-/* out[i,:] = x[perm_pair[i] / k, :] for the T*k permuted rows. */
-int fg_moe_gather(const fg_bf16* x, const int32_t* perm_pair, int T, int k, int H, fg_bf16* out,
+/* out[i,:] = x[perm_pair[i] / k, :] for the T*k permuted rows, as f16 (the
+ * operand type of fg_moe_gemm_mxfp4; every bf16 value with |x| >= 2^-17 is
+ * exact in f16, smaller ones round to the f16 subnormal step 2^-24). */
+int fg_moe_gather(const fg_bf16* x, const int32_t* perm_pair, int T, int k, int H, fg_f16* out,
                   fg_stream_t stream);
 /* Pack MXFP4 expert weights: values:[E][N][K/2] (e2m1 pairs, low nibble =
  * even k), scales:[E][N][K/32] (e8m0) -> records of 128 rows x 64 K
@@ -214,14 +217,19 @@ int fg_pack_mxfp4(const uint8_t* values, const uint8_t* scales, void* packed, in
                   fg_stream_t stream);
 size_t fg_mxfp4_packed_bytes(int E, int N, int K);
 /* Grouped expert GEMM on tcgen05: for every work item (expert e, token tile),
- * acc = x[rows of e] . dequant(W_e)^T with W_e packed MXFP4 [N,K], dequantised
- * to bf16 in shared memory (exactly as transformers dequantises MXFP4), fp32
- * accumulation; epilogue FG_EPI_STORE (+ bias[e]) -> out:[rows,N], or
- * FG_EPI_SWIGLU_OAI (+ bias, gate/up rows interleaved per 64) -> out:[rows,N/2].
- * Only experts that received tokens read their weights. */
-int fg_moe_gemm_mxfp4(const fg_bf16* x, const void* w_packed, const fg_bf16* bias,
+ * acc = x[rows of e] . W_e^T with W_e packed MXFP4 [N,K] (fg_pack_mxfp4) and
+ * x f16 rows [rows,K]. The weights are decoded on the SM into tensor memory
+ * (e2m1 -> f16, times the block scale relative to a per-row reference
+ * exponent, exact) and multiplied with fp32 accumulation; the accumulator is
+ * rescaled by the row's reference power of two, so the result is that of the
+ * exact bf16 dequantisation transformers performs. Epilogue FG_EPI_STORE
+ * (+ bias[e]) -> out: bf16 [rows,N]; FG_EPI_SWIGLU_OAI (+ bias, gate/up rows
+ * interleaved per 64, SwiGLU-OAI rounded to bf16 per op) -> out: f16
+ * [rows,N/2] (the bf16 values, the next call's operand). Only experts that
+ * received tokens read their weights. */
+int fg_moe_gemm_mxfp4(const fg_f16* x, const void* w_packed, const fg_bf16* bias,
                       const int32_t* offsets, const int32_t* items, const int32_t* item_count,
-                      int max_items, fg_bf16* out, int rows, int N, int K, int BN, int epilogue,
+                      int max_items, void* out, int rows, int N, int K, int BN, int epilogue,
                       fg_stream_t stream);
 /* out[t] = residual[t] + sum over the k slots in ascending expert id of
  * bf16(y[inv[t*k+j]] * weights[t,j]), each addition rounded to bf16 (the

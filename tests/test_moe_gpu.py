@@ -114,7 +114,9 @@ def test_grouped_mxfp4_gemms(T, k, E, H, I):
     r = moe.Routing(idx.to(DEV), E)
     x_perm = x[r.perm_pair.cpu().long() // k]
     offsets = r.offsets.cpu().tolist()
-    act = moe.grouped_gemm(x_perm.to(DEV).contiguous(), p1, b1.to(DEV), r, 2 * I, H, _lib.FG_EPI_SWIGLU_OAI)
+    act = moe.grouped_gemm(x_perm.to(DEV, torch.float16).contiguous(), p1, b1.to(DEV), r, 2 * I, H,
+                           _lib.FG_EPI_SWIGLU_OAI)
+    assert act.dtype == torch.float16
     exp_act = _ref_expert_gemm(x_perm, d1, b1, offsets, "swiglu_oai")
     err = (act.cpu().float() - exp_act).abs().max().item()
     assert err <= 2e-2 * exp_act.abs().max().item() + 1e-3, err
@@ -212,3 +214,38 @@ def test_gpt_oss_decode_matches_oracle():
                 tie_flips += 1
     assert tie_flips <= 2, f"{tie_flips} router decisions differ"
     kernels.check_device("gpt-oss decode")
+
+
+def test_mxfp4_scale_window():
+    """Rows whose block scales spread over up to 36 binades (and all-zero
+    blocks with arbitrary scales) give the exact dequantised products; a
+    nonzero block further below its row's largest is refused at packing."""
+    from fluidgpu_b200 import _lib, kernels, moe
+
+    g = _g(6)
+    E, N, K, T, k = 2, 128, 256, 8, 1
+    v = torch.randint(0, 256, (E, N, K // 2), generator=g, dtype=torch.int32).to(torch.uint8)
+    s = torch.full((E, N, K // 32), 120, dtype=torch.uint8)
+    s[:, :, 1] = 120 + 13        # largest block of the row
+    s[:, :, 2] = 120 + 13 - 36   # lowest exact block
+    s[:, 5, 3] = 250             # an all-zero block with a huge scale does not count
+    v[:, 5, 48:64] = 0
+    p = moe.pack_mxfp4(v.to(DEV), s.to(DEV))
+    kernels.check_device("in-window packing")
+    w = moe.dequantize_mxfp4(v, s, torch.float32)
+    idx = torch.zeros((T, k), dtype=torch.int32)
+    idx[T // 2:] = 1
+    r = moe.Routing(idx.to(DEV), E)
+    x = torch.randn(T, K, generator=g).to(torch.bfloat16)
+    x_perm = x[r.perm_pair.cpu().long() // k]
+    y = moe.grouped_gemm(x_perm.to(DEV, torch.float16).contiguous(), p, None, r, N, K,
+                         _lib.FG_EPI_STORE).cpu().float()
+    offs = r.offsets.cpu().tolist()
+    ref = torch.cat([x_perm[offs[e]:offs[e + 1]].double() @ w[e].double().T for e in range(E)])
+    ref = ref.float()
+    assert torch.allclose(y, ref, rtol=2 ** -7, atol=1e-4 * ref.abs().max().item()), (y - ref).abs().max()
+    s[0, 7, 4] = 120 + 13 - 37   # one binade too far, with nonzero values
+    v[0, 7, 64:80] = 0x11
+    moe.pack_mxfp4(v.to(DEV), s.to(DEV))
+    with pytest.raises(RuntimeError, match="MXFP4 block scale"):
+        kernels.check_device("out-of-window packing")
