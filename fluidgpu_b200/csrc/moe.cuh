@@ -323,23 +323,24 @@ __global__ void pack_mxfp4_kernel(const uint8_t* __restrict__ vals, const uint8_
 }
 
 // ---------------------------------------------------------------------------
-// MXFP4 x activation grouped GEMM (swap-AB). Weights are dequantised by the
-// hardware e2m1 -> f16 conversion straight into tensor memory and used as
-// the A operand of tcgen05.mma kind::f16 (A from TMEM, B = the f16
-// activation tile from shared memory). Nothing but the 4.25-bit records and
-// the activation tiles crosses shared memory, so the kernel streams HBM
+// MXFP4 x activation grouped GEMM (swap-AB). Weights are decoded (e2m1 ->
+// f16 by table lookup, times the block scale) straight into tensor memory
+// and used as the A operand of tcgen05.mma kind::f16 (A from TMEM, B = the
+// f16 activation tile from shared memory). Only the 4.25-bit records and
+// the activation tiles cross shared memory, so the kernel streams HBM
 // instead of saturating shared-memory bandwidth with expanded tiles.
 //
 // Persistent: one CTA per SM walks the work units (permute item x 128-row
-// tile) u = blockIdx.x + j * gridDim.x. 16 warps:
-//   warp 0       producer: bulk copy of the record + 2-D TMA of the
-//                activation tile per K step into a deep ring
-//   warp 1       TMEM owner and MMA issuer (4 x K16 per K step into one of
+// tile) u = blockIdx.x + j * gridDim.x; a unit's K runs in steps of two
+// 64-wide records. 16 warps:
+//   warp 0       weight producer: one bulk copy per step into a deep ring
+//   warp 2       activation producer: the step's 2-D TMA tiles, own ring
+//   warp 1       TMEM owner and MMA issuer (8 x K16 per step into one of
 //                two accumulators, so the epilogue overlaps the next unit)
-//   warps 4-19   four converter warpgroups, K step i on warpgroup i % 4: a
-//                thread per weight row decodes its 64 values into the
-//                warpgroup's TMEM A stage with tcgen05.st
-//   warps 20-23  epilogue: accumulator x 2^(s_ref-127) + bias, SwiGLU-OAI
+//   warps 4-11   two converter warpgroups taking alternate steps: a thread
+//                per weight row decodes its 128 values into a TMEM A stage
+//                (tcgen05.st); four A stages
+//   warps 12-15  epilogue: accumulator x 2^(s_ref-127) + bias, SwiGLU-OAI
 //                (gate rows 0-63 of a tile, up rows 64-127; f16 out) or
 //                store (bf16 out)
 // ---------------------------------------------------------------------------
@@ -353,28 +354,38 @@ struct GemmParams {
   int N, K, n_tiles, nkb, ldo, epilogue;
 };
 
-constexpr int kConvWG = 4;        // converter warpgroups
+constexpr int kKS = 2;            // records per step
 constexpr int kConvWarp0 = 4;
-constexpr int kEpiWarp0 = kConvWarp0 + 4 * kConvWG;
-constexpr int kMoeWarps = kEpiWarp0 + 4;
+constexpr int kEpiWarp0 = 12;
+constexpr int kMoeWarps = 16;
 constexpr int kMoeThreads = kMoeWarps * 32;
-constexpr int kAStages = kConvWG; // TMEM A stage per converter warpgroup, 32 columns
-constexpr int kDCol0 = kAStages * 32;
+constexpr int kAStages = 4;       // TMEM A stages of kKS * 32 columns
+constexpr int kDCol0 = kAStages * kKS * 32;  // two accumulators of BN columns follow the A stages
+// byte -> f16x2 decode table, one copy per lane: entry (byte b, lane l) at
+// b * 256 + l * 4, so a warp's 32 lookups hit 32 different banks and the
+// address is one byte permute of (b, 4l)
+constexpr int kLutBytes = 256 * 256;
 
 template <int BN>
 struct MLayout {
-  static constexpr int STAGES = BN <= 32 ? 16 : 12;
-  static constexpr int X_BYTES = BN * BK * 2;                  // [BN][64] 16-bit, 128B swizzle
-  static constexpr int REC_OFFSET = STAGES * X_BYTES;
-  static constexpr int XCH_OFFSET = REC_OFFSET + STAGES * kRecBytes;  // bf16 [BN][64]
+  static constexpr int WS = BN <= 16 ? 14 : (BN <= 32 ? 12 : 10);  // weight ring (steps)
+  static constexpr int XS = BN <= 32 ? 4 : 3;                      // activation ring (steps)
+  static constexpr int X_TILE = BN * BK * 2;                       // [BN][64] f16, 128B swizzle
+  static constexpr int X_STAGE = kKS * X_TILE;
+  static constexpr int W_STAGE = kKS * kRecBytes;
+  static constexpr int W_OFFSET = XS * X_STAGE;
+  static constexpr int XCH_OFFSET = W_OFFSET + WS * W_STAGE;       // bf16 [BN][64]
   static constexpr int BAR_OFFSET = (XCH_OFFSET + BN * 64 * 2 + 7) / 8 * 8;
-  // raw_full[S] raw_empty[S] a_full[A] a_empty[A] acc_full[2] acc_empty[2] mma_done
-  static constexpr int MISC_OFFSET = BAR_OFFSET + (2 * STAGES + 2 * kAStages + 5) * 8;
+  // w_full[WS] w_empty[WS] x_full[XS] x_empty[XS] a_full[A] a_empty[A] acc_full[2] acc_empty[2] mma_done
+  static constexpr int MISC_OFFSET = BAR_OFFSET + (2 * WS + 2 * XS + 2 * kAStages + 5) * 8;
   static constexpr int TOTAL = MISC_OFFSET + 16;
-  static constexpr int DYN_SMEM = TOTAL + 1024;
-  static constexpr uint32_t TMEM_COLS = 256;  // A ring 128 + two accumulators of BN <= 64
-  static_assert(X_BYTES % 1024 == 0 && kRecBytes % 16 == 0, "stage alignment");
+  // the decode table sits at the start of dynamic shared memory, the
+  // 1024-aligned region above starts after it
+  static constexpr int DYN_SMEM = kLutBytes + TOTAL + 1024;
+  static constexpr uint32_t TMEM_COLS = 512;  // A stages 256 + two accumulators of BN <= 64
+  static_assert(X_TILE % 1024 == 0 && kRecBytes % 16 == 0, "stage alignment");
   static_assert(kDCol0 + 2 * BN <= (int)TMEM_COLS, "tensor memory budget");
+  static_assert(DYN_SMEM <= 232448, "shared memory budget");
 };
 
 // instruction descriptor for kind::f16 with f16 A/B, fp32 D, K-major
@@ -403,16 +414,23 @@ __device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&a)[32])
       : "memory");
 }
 
-// four bytes of e2m1 pairs -> four f16x2 (low nibble in the low half)
-__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t v, uint32_t* o) {
-  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
-      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
-      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
-      : "r"(v));
+// f16 bits of the e2m1 code n (sign, 2-bit exponent, 1-bit mantissa)
+__device__ __forceinline__ uint32_t e2m1_f16_bits(uint32_t n) {
+  const uint32_t mag = n & 7u;
+  // 0, 0.5, then 2^(e-1) * (1 + m/2): f16 exponent field e + 14, mantissa bit 9
+  const uint32_t bits = mag == 0u ? 0u : (mag == 1u ? 0x3800u : ((mag >> 1) + 14u) << 10 | (mag & 1u) << 9);
+  return bits | (n & 8u) << 12;
+}
+
+// four bytes of e2m1 pairs -> four f16x2 (low nibble in the low half) by
+// table lookup; the hardware e2m1 conversion issues on the narrow XU pipe
+// and would bound the kernel well below HBM speed
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t v, uint32_t lane4, const uint8_t* lut, uint32_t* o) {
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const uint32_t off = __byte_perm(v, lane4, 0x5504u | ((uint32_t)b << 4));  // byte b << 8 | 4*lane
+    o[b] = *reinterpret_cast<const uint32_t*>(lut + off);
+  }
 }
 
 // f16 bits of 2^(c-24), c in [0, 37], in both halves
@@ -455,27 +473,41 @@ template <int BN>
 __global__ void __launch_bounds__(kMoeThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const GemmParams p) {
   using L = MLayout<BN>;
-  constexpr int S = L::STAGES;
+  constexpr int WS = L::WS, XS = L::XS;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+  const uint8_t* lut = smem_raw;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw + kLutBytes) + 1023) &
                                              ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  {
+    uint32_t* t = reinterpret_cast<uint32_t*>(smem_raw);
+    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
+      const uint32_t b = (uint32_t)i >> 5, l = (uint32_t)i & 31u;
+      t[b * 64 + l] = e2m1_f16_bits(b & 15u) | e2m1_f16_bits(b >> 4) << 16;
+    }
+  }
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t raw_full = sbase + L::BAR_OFFSET;
-  const uint32_t raw_empty = raw_full + S * 8;
-  const uint32_t a_full = raw_empty + S * 8;
+  const uint32_t w_full = sbase + L::BAR_OFFSET;
+  const uint32_t w_empty = w_full + WS * 8;
+  const uint32_t x_full = w_empty + WS * 8;
+  const uint32_t x_empty = x_full + XS * 8;
+  const uint32_t a_full = x_empty + XS * 8;
   const uint32_t a_empty = a_full + kAStages * 8;
   const uint32_t acc_full = a_empty + kAStages * 8;
   const uint32_t acc_empty = acc_full + 2 * 8;
   const uint32_t mma_done = acc_empty + 2 * 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFFSET);
-  int* issued_out = reinterpret_cast<int*>(smem + L::MISC_OFFSET + 8);
+  int* issued = reinterpret_cast<int*>(smem + L::MISC_OFFSET + 4);  // [0] weights, [1] activations
   __nv_bfloat16* xch = reinterpret_cast<__nv_bfloat16*>(smem + L::XCH_OFFSET);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(raw_full + 8 * s, 1);
-      mbar_init(raw_empty + 8 * s, 4 + 1);  // converter warps + MMA commit
+    for (int s = 0; s < WS; ++s) {
+      mbar_init(w_full + 8 * s, 1);
+      mbar_init(w_empty + 8 * s, 4);  // the converter warps of the step's warpgroup
+    }
+    for (int s = 0; s < XS; ++s) {
+      mbar_init(x_full + 8 * s, 1);
+      mbar_init(x_empty + 8 * s, 1);  // MMA commit
     }
     for (int s = 0; s < kAStages; ++s) {
       mbar_init(a_full + 8 * s, 4);
@@ -486,7 +518,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
       mbar_init(acc_empty + 8 * b, 4);
     }
     mbar_init(mma_done, 1);
-    *issued_out = 0;
+    issued[0] = issued[1] = 0;
     fence_mbar_init();
     prefetch_tensormap(&tm_x);
   }
@@ -510,98 +542,131 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
   const int G = gridDim.x;
   const int my_units = (int)blockIdx.x < U ? (U - 1 - (int)blockIdx.x) / G + 1 : 0;
   const int nkb = p.nkb;
-  const int NK = my_units * nkb;  // K steps this CTA runs
+  const int nsteps = (nkb + kKS - 1) / kKS;  // steps per unit
+  const int NS = my_units * nsteps;            // steps this CTA runs
+  auto step_count = [&](int t) { return min(kKS, nkb - t * kKS); };  // records in step t of a unit
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- producer ----------------
+      // ---------------- weight producer ----------------
       const uint64_t pol_w = l2_policy_evict_first();
-      const uint64_t pol_x = l2_policy_evict_last();
-      int i = 0;
+      int g = 0;
       bool ok = true;
       for (int j = 0; j < my_units && ok; ++j) {
         const Unit w = unit_of(p, blockIdx.x + j * G, BN);
         const uint8_t* wrec = p.w + ((size_t)w.e * p.n_tiles + w.nt) * tile_stride(nkb);
-        for (int kb = 0; kb < nkb; ++kb, ++i) {
-          const int s = i % S;
-          if (!mbar_wait(raw_empty + 8 * s, ((uint32_t)(i / S) & 1u) ^ 1u, 0x321)) {
+        for (int t = 0; t < nsteps; ++t, ++g) {
+          const int s = g % WS;
+          if (!mbar_wait(w_empty + 8 * s, ((uint32_t)(g / WS) & 1u) ^ 1u, 0x321)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(raw_full + 8 * s, kRecBytes + L::X_BYTES);
-          bulk_load(sbase + L::REC_OFFSET + s * kRecBytes, wrec + (size_t)kb * kRecBytes, kRecBytes,
-                    raw_full + 8 * s, pol_w);
-          tma_load_2d_hint(sbase + s * L::X_BYTES, &tm_x, raw_full + 8 * s, kb * BK, w.row0, pol_x);
+          const uint32_t bytes = (uint32_t)step_count(t) * kRecBytes;
+          mbar_arrive_expect_tx(w_full + 8 * s, bytes);
+          bulk_load(sbase + L::W_OFFSET + s * L::W_STAGE, wrec + (size_t)t * L::W_STAGE, bytes,
+                    w_full + 8 * s, pol_w);
         }
       }
-      *issued_out = i;
+      issued[0] = g;
+    }
+  } else if (warp == 2) {
+    if (lane == 0) {
+      // ---------------- activation producer ----------------
+      const uint64_t pol_x = l2_policy_evict_last();
+      int g = 0;
+      bool ok = true;
+      for (int j = 0; j < my_units && ok; ++j) {
+        const Unit w = unit_of(p, blockIdx.x + j * G, BN);
+        for (int t = 0; t < nsteps; ++t, ++g) {
+          const int s = g % XS;
+          if (!mbar_wait(x_empty + 8 * s, ((uint32_t)(g / XS) & 1u) ^ 1u, 0x322)) {
+            ok = false;
+            break;
+          }
+          const int cnt = step_count(t);
+          mbar_arrive_expect_tx(x_full + 8 * s, (uint32_t)(cnt * L::X_TILE));
+          for (int kk = 0; kk < cnt; ++kk)
+            tma_load_2d_hint(sbase + s * L::X_STAGE + kk * L::X_TILE, &tm_x, x_full + 8 * s,
+                             (t * kKS + kk) * BK, w.row0, pol_x);
+        }
+      }
+      issued[1] = g;
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc = idesc_f16(BM, BN);
-      int i = 0;
+      int g = 0;
       bool ok = true;
       for (int j = 0; j < my_units && ok; ++j) {
         const int buf = j & 1;
-        if (!mbar_wait(acc_empty + 8 * buf, ((uint32_t)(j >> 1) & 1u) ^ 1u, 0x322)) break;
+        if (!mbar_wait(acc_empty + 8 * buf, ((uint32_t)(j >> 1) & 1u) ^ 1u, 0x323)) break;
         gemm::tc_fence_after();
         const uint32_t d = tmem + kDCol0 + buf * BN;
-        for (int kb = 0; kb < nkb; ++kb, ++i) {
-          const int s = i % S, sa = i % kAStages;
-          if (!mbar_wait(a_full + 8 * sa, (uint32_t)(i / kAStages) & 1u, 0x323)) {
+        for (int t = 0; t < nsteps; ++t, ++g) {
+          const int sa = g % kAStages, sx = g % XS;
+          if (!mbar_wait(a_full + 8 * sa, (uint32_t)(g / kAStages) & 1u, 0x324) ||
+              !mbar_wait(x_full + 8 * sx, (uint32_t)(g / XS) & 1u, 0x325)) {
             ok = false;
             break;
           }
           gemm::tc_fence_after();
-          const uint64_t bdesc = gemm::sw128_kmajor_desc(sbase + s * L::X_BYTES);
+          const int cnt = step_count(t);
+          for (int kk = 0; kk < cnt; ++kk) {
+            const uint64_t bdesc = gemm::sw128_kmajor_desc(sbase + sx * L::X_STAGE + kk * L::X_TILE);
+            const uint32_t a = tmem + sa * (kKS * 32) + kk * 32;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            tc_mma_ts(d, tmem + sa * 32 + kk * 8, bdesc + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            for (int k16 = 0; k16 < BK / 16; ++k16)
+              tc_mma_ts(d, a + k16 * 8, bdesc + 2 * k16, idesc, (t > 0 || kk > 0 || k16 > 0) ? 1u : 0u);
+          }
           gemm::tc_commit(a_empty + 8 * sa);
-          gemm::tc_commit(raw_empty + 8 * s);
+          gemm::tc_commit(x_empty + 8 * sx);
         }
         if (ok) gemm::tc_commit(acc_full + 8 * buf);
       }
       // every MMA of this thread has completed before the CTA moves on
       gemm::tc_commit(mma_done);
-      mbar_wait(mma_done, 0, 0x324);
+      mbar_wait(mma_done, 0, 0x326);
     }
   } else if (warp >= kConvWarp0 && warp < kEpiWarp0) {
     // ---------------- converters ----------------
     const int wg = (warp - kConvWarp0) >> 2, q = warp & 3;
-    const int t = q * 32 + lane;  // weight row of this thread, also its TMEM lane
-    for (int i = wg; i < NK; i += kConvWG) {
-      const int s = i % S, sa = i % kAStages;
-      if (!mbar_wait(raw_full + 8 * s, (uint32_t)(i / S) & 1u, 0x325)) break;
-      if (!mbar_wait(a_empty + 8 * sa, ((uint32_t)(i / kAStages) & 1u) ^ 1u, 0x326)) break;
+    const int row = q * 32 + lane;  // weight row of this thread, also its TMEM lane
+    const uint32_t lane4 = (uint32_t)lane * 4u;
+    for (int g = wg; g < NS; g += 2) {
+      const int s = g % WS, sa = g % kAStages;
+      if (!mbar_wait(w_full + 8 * s, (uint32_t)(g / WS) & 1u, 0x327)) break;
+      if (!mbar_wait(a_empty + 8 * sa, ((uint32_t)(g / kAStages) & 1u) ^ 1u, 0x328)) break;
       gemm::tc_fence_after();
-      // weight row t: 64 e2m1 values -> 32 f16x2 columns of the A stage
-      const uint8_t* rec = smem + L::REC_OFFSET + s * kRecBytes;
-      const uint4 v0 = *reinterpret_cast<const uint4*>(rec + t * 16);
-      const uint4 v1 = *reinterpret_cast<const uint4*>(rec + 2048 + t * 16);
-      const uint32_t codes = *reinterpret_cast<const uint16_t*>(rec + kValBytes + 2 * t);
-      const uint32_t m0 = pow2_f16x2(codes & 0xFFu), m1 = pow2_f16x2(codes >> 8);
-      uint32_t a[32];
-      e2m1x8_to_f16x2(v0.x, a + 0);
-      e2m1x8_to_f16x2(v0.y, a + 4);
-      e2m1x8_to_f16x2(v0.z, a + 8);
-      e2m1x8_to_f16x2(v0.w, a + 12);
-      e2m1x8_to_f16x2(v1.x, a + 16);
-      e2m1x8_to_f16x2(v1.y, a + 20);
-      e2m1x8_to_f16x2(v1.z, a + 24);
-      e2m1x8_to_f16x2(v1.w, a + 28);
+      const int cnt = step_count(g % nsteps);
+      for (int kk = 0; kk < cnt; ++kk) {
+        // weight row `row` of record kk: 64 e2m1 values -> 32 f16x2 columns
+        const uint8_t* rec = smem + L::W_OFFSET + s * L::W_STAGE + kk * kRecBytes;
+        const uint4 v0 = *reinterpret_cast<const uint4*>(rec + row * 16);
+        const uint4 v1 = *reinterpret_cast<const uint4*>(rec + 2048 + row * 16);
+        const uint32_t codes = *reinterpret_cast<const uint16_t*>(rec + kValBytes + 2 * row);
+        const uint32_t m0 = pow2_f16x2(codes & 0xFFu), m1 = pow2_f16x2(codes >> 8);
+        uint32_t a[32];
+        e2m1x8_to_f16x2(v0.x, lane4, lut, a + 0);
+        e2m1x8_to_f16x2(v0.y, lane4, lut, a + 4);
+        e2m1x8_to_f16x2(v0.z, lane4, lut, a + 8);
+        e2m1x8_to_f16x2(v0.w, lane4, lut, a + 12);
+        e2m1x8_to_f16x2(v1.x, lane4, lut, a + 16);
+        e2m1x8_to_f16x2(v1.y, lane4, lut, a + 20);
+        e2m1x8_to_f16x2(v1.z, lane4, lut, a + 24);
+        e2m1x8_to_f16x2(v1.w, lane4, lut, a + 28);
 #pragma unroll
-      for (int c = 0; c < 16; ++c) a[c] = hmul2_bits(a[c], m0);
+        for (int c = 0; c < 16; ++c) a[c] = hmul2_bits(a[c], m0);
 #pragma unroll
-      for (int c = 16; c < 32; ++c) a[c] = hmul2_bits(a[c], m1);
-      tc_st32(tmem + ((uint32_t)(q * 32) << 16) + sa * 32, a);
+        for (int c = 16; c < 32; ++c) a[c] = hmul2_bits(a[c], m1);
+        tc_st32(tmem + ((uint32_t)(q * 32) << 16) + sa * (kKS * 32) + kk * 32, a);
+      }
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       gemm::tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(a_full + 8 * sa);
-        mbar_arrive(raw_empty + 8 * s);
+        mbar_arrive(w_empty + 8 * s);
       }
     }
   } else if (warp >= kEpiWarp0) {
@@ -613,7 +678,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     bool failed = false;
     for (int j = 0; j < my_units; ++j) {
       const int buf = j & 1;
-      const bool acc_ok = !failed && mbar_wait(acc_full + 8 * buf, (uint32_t)(j >> 1) & 1u, 0x327);
+      const bool acc_ok = !failed && mbar_wait(acc_full + 8 * buf, (uint32_t)(j >> 1) & 1u, 0x329);
       failed = !acc_ok;
       gemm::tc_fence_after();
       const Unit w = unit_of(p, blockIdx.x + j * G, BN);
@@ -679,11 +744,15 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
 
   gemm::tc_fence_before();
   __syncthreads();
+  // no copy may land after the CTA exits: wait for each ring's last issued steps
   if (threadIdx.x == 0) {
-    // no copy may land after the CTA exits: wait for the last issued K steps
-    const int issued = *issued_out;
-    for (int i = issued - S < 0 ? 0 : issued - S; i < issued; ++i)
-      mbar_wait(raw_full + 8 * (i % S), (uint32_t)(i / S) & 1u, 0x328);
+    const int n = issued[0];
+    for (int g = n - WS < 0 ? 0 : n - WS; g < n; ++g)
+      mbar_wait(w_full + 8 * (g % WS), (uint32_t)(g / WS) & 1u, 0x32a);
+  } else if (threadIdx.x == 64) {
+    const int n = issued[1];
+    for (int g = n - XS < 0 ? 0 : n - XS; g < n; ++g)
+      mbar_wait(x_full + 8 * (g % XS), (uint32_t)(g / XS) & 1u, 0x32b);
   }
   __syncthreads();
   if (warp == 1) {
