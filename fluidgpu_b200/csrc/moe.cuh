@@ -37,7 +37,10 @@ constexpr int kMaxE = 64;
 // ---------------------------------------------------------------------------
 // router: logits, top-k (value desc, index asc), softmax over the selected
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) router_topk_kernel(
+// One CTA of 32 warps per token: warp w computes the logits of experts w,
+// w+32 (one dot product each, its loads all in flight together), then warp 0
+// selects the top-k.
+__global__ void __launch_bounds__(1024) router_topk_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
     const __nv_bfloat16* __restrict__ bias, int H, int E, int k, __nv_bfloat16* __restrict__ out_w,
     int32_t* __restrict__ out_idx, __nv_bfloat16* __restrict__ out_logits) {
@@ -48,9 +51,10 @@ __global__ void __launch_bounds__(256) router_topk_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)t * H);
   const int H8 = H >> 3;
-  for (int e = warp; e < E; e += 8) {
+  for (int e = warp; e < E; e += 32) {
     const uint4* wr = reinterpret_cast<const uint4*>(w + (int64_t)e * H);
     float acc = 0.f;
+#pragma unroll 4
     for (int i = lane; i < H8; i += 32) {
       const uint4 a = xr[i], b = wr[i];
       const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
@@ -137,27 +141,40 @@ __global__ void __launch_bounds__(1024) permute_kernel(
     }
     atomicAdd(&cnt[warp][e], 1);
   }
+  __shared__ int tot[kMaxE], tile0[kMaxE + 1];
+  __syncthreads();
+  if (threadIdx.x < E) {
+    int c = 0;
+    for (int w = 0; w < 32; ++w) c += cnt[w][threadIdx.x];
+    tot[threadIdx.x] = c;
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
-    int run = 0;
+    // expert row offsets and the first work item of each expert
+    int run = 0, ti = 0;
     for (int e = 0; e < E; ++e) {
       base[e] = run;
-      for (int w = 0; w < 32; ++w) {
-        const int c = cnt[w][e];
-        cnt[w][e] = run;  // start of warp w's pairs for expert e
-        run += c;
-      }
+      tile0[e] = ti;
+      run += tot[e];
+      ti += (tot[e] + BN - 1) / BN;
     }
     base[E] = run;
-    int ni = 0;
-    for (int e = 0; e < E; ++e) {
-      const int ne = base[e + 1] - base[e];
-      for (int tt = 0; tt * BN < ne && ni < max_items; ++tt, ++ni) {
-        items[2 * ni] = e;
-        items[2 * ni + 1] = tt;
-      }
+    tile0[E] = ti;
+    *item_count = min(ti, max_items);
+  }
+  __syncthreads();
+  if (threadIdx.x < E) {
+    const int e = threadIdx.x;
+    int run = base[e];
+    for (int w = 0; w < 32; ++w) {
+      const int c = cnt[w][e];
+      cnt[w][e] = run;  // start of warp w's pairs for expert e
+      run += c;
     }
-    *item_count = ni;
+    for (int i = tile0[e]; i < tile0[e + 1] && i < max_items; ++i) {
+      items[2 * i] = e;
+      items[2 * i + 1] = i - tile0[e];
+    }
   }
   __syncthreads();
   for (int e = threadIdx.x; e <= E; e += blockDim.x) offsets[e] = base[e];
@@ -206,36 +223,70 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ x, const int32_t* _
   }
 }
 
-// out[t] = residual[t] + sum over the k experts (ascending id) of y[inv] * w
-__global__ void unpermute_kernel(const __nv_bfloat16* __restrict__ y, const int32_t* __restrict__ inv,
-                                 const int32_t* __restrict__ idx,
-                                 const __nv_bfloat16* __restrict__ wts,
-                                 const __nv_bfloat16* __restrict__ residual,
-                                 __nv_bfloat16* __restrict__ out, int k, int H) {
+// out[t] = residual[t] + sum over the k experts (ascending id) of y[inv] * w,
+// each product and partial sum rounded to bf16 as transformers' index_add_
+// accumulation does; 8 features per thread step (H % 8 == 0)
+__global__ void __launch_bounds__(128) unpermute_kernel(const __nv_bfloat16* __restrict__ y,
+                                                        const int32_t* __restrict__ inv,
+                                                        const int32_t* __restrict__ idx,
+                                                        const __nv_bfloat16* __restrict__ wts,
+                                                        const __nv_bfloat16* __restrict__ residual,
+                                                        __nv_bfloat16* __restrict__ out, int k, int H) {
   griddep_wait();
   griddep_launch_dependents();
+  __shared__ int s_row[8];
+  __shared__ float s_w[8];
   const int t = blockIdx.x;
-  int order[8];
-  for (int j = 0; j < k; ++j) order[j] = j;
-  // insertion sort of the k slots by expert id (k <= 8)
-  for (int a = 1; a < k; ++a) {
-    const int v = order[a];
-    int b = a - 1;
-    while (b >= 0 && idx[(int64_t)t * k + order[b]] > idx[(int64_t)t * k + v]) {
-      order[b + 1] = order[b];
-      --b;
+  if (threadIdx.x == 0) {
+    int order[8];
+    for (int j = 0; j < k; ++j) order[j] = j;
+    // insertion sort of the k slots by expert id (k <= 8), stable
+    for (int a = 1; a < k; ++a) {
+      const int v = order[a];
+      int b = a - 1;
+      while (b >= 0 && idx[(int64_t)t * k + order[b]] > idx[(int64_t)t * k + v]) {
+        order[b + 1] = order[b];
+        --b;
+      }
+      order[b + 1] = v;
     }
-    order[b + 1] = v;
-  }
-  for (int h = threadIdx.x; h < H; h += blockDim.x) {
-    float acc = 0.f;
     for (int a = 0; a < k; ++a) {
-      const int j = order[a];
-      const int row = inv[(int64_t)t * k + j];
-      const float wv = bf2f(wts[(int64_t)t * k + j]);
-      acc = rbf(acc + rbf(bf2f(y[(int64_t)row * H + h]) * wv));
+      s_row[a] = inv[(int64_t)t * k + order[a]];
+      s_w[a] = bf2f(wts[(int64_t)t * k + order[a]]);
     }
-    out[(int64_t)t * H + h] = f2bf(residual ? bf2f(residual[(int64_t)t * H + h]) + acc : acc);
+  }
+  __syncthreads();
+  const int H8 = H >> 3;
+  for (int c = threadIdx.x; c < H8; c += blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int a = 0; a < k; ++a) {
+      const uint4 v = reinterpret_cast<const uint4*>(y + (int64_t)s_row[a] * H)[c];
+      const uint32_t* pv = reinterpret_cast<const uint32_t*>(&v);
+      const float wv = s_w[a];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(pv[i]);
+        acc[2 * i] = rbf(acc[2 * i] + rbf(f.x * wv));
+        acc[2 * i + 1] = rbf(acc[2 * i + 1] + rbf(f.y * wv));
+      }
+    }
+    uint4 o;
+    uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+    if (residual) {
+      const uint4 r = reinterpret_cast<const uint4*>(residual + (int64_t)t * H)[c];
+      const uint32_t* pr = reinterpret_cast<const uint32_t*>(&r);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(pr[i]);
+        po[i] = pack_bf16x2(f.x + acc[2 * i], f.y + acc[2 * i + 1]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) po[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
+    }
+    reinterpret_cast<uint4*>(out + (int64_t)t * H)[c] = o;
   }
 }
 
@@ -776,7 +827,7 @@ int fg_moe_router_topk(const fg_bf16* x, const fg_bf16* w, const fg_bf16* bias, 
              "fg_moe_router_topk: bad sizes T=%d H=%d E=%d k=%d", T, H, E, k);
   FG_REQUIRE((((uintptr_t)x | (uintptr_t)w) & 15) == 0, "fg_moe_router_topk: x/w must be 16-byte aligned");
   if (T == 0) return FG_OK;
-  return fg::launch_k("fg_moe_router_topk", fg::moe::router_topk_kernel, dim3(T), dim3(256), 0,
+  return fg::launch_k("fg_moe_router_topk", fg::moe::router_topk_kernel, dim3(T), dim3(1024), 0,
                       (cudaStream_t)stream, reinterpret_cast<const __nv_bfloat16*>(x),
                       reinterpret_cast<const __nv_bfloat16*>(w),
                       reinterpret_cast<const __nv_bfloat16*>(bias), H, E, k,
@@ -822,9 +873,11 @@ int fg_moe_unpermute(const fg_bf16* y, const int32_t* inv, const int32_t* indice
                      const fg_bf16* weights, const fg_bf16* residual, fg_bf16* out, int T, int k,
                      int H, fg_stream_t stream) {
   FG_REQUIRE(y && inv && indices && weights && out, "fg_moe_unpermute: null pointer");
-  FG_REQUIRE(T >= 0 && k > 0 && k <= 8 && H > 0, "fg_moe_unpermute: bad sizes");
+  FG_REQUIRE(T >= 0 && k > 0 && k <= 8 && H > 0 && H % 8 == 0, "fg_moe_unpermute: bad sizes (H %% 8 == 0)");
+  FG_REQUIRE((((uintptr_t)y | (uintptr_t)out | (uintptr_t)residual) & 15) == 0,
+             "fg_moe_unpermute: y/residual/out must be 16-byte aligned");
   if (T == 0) return FG_OK;
-  return fg::launch_k("fg_moe_unpermute", fg::moe::unpermute_kernel, dim3(T), dim3(256), 0,
+  return fg::launch_k("fg_moe_unpermute", fg::moe::unpermute_kernel, dim3(T), dim3(128), 0,
                       (cudaStream_t)stream, reinterpret_cast<const __nv_bfloat16*>(y), inv, indices,
                       reinterpret_cast<const __nv_bfloat16*>(weights),
                       reinterpret_cast<const __nv_bfloat16*>(residual),

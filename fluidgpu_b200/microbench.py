@@ -169,6 +169,26 @@ def bench_moe(T: int = 128, E: int = 32, k: int = 4, H: int = 2880, I: int = 288
                     "ms": ms, "bytes": nbytes, "GBps": gbs, "frac_hbm": gbs / peak,
                     "TFLOPs": 2.0 * T * k * N * K / (ms * 1e-3) / 1e12,
                     "peak": f"{src} {peak} GB/s", "timing": "graph" if GRAPH else "eager"})
+    # the small kernels around the expert GEMMs
+    xr = torch.empty((T, H), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
+    rw = torch.empty((E, H), dtype=torch.bfloat16, device="cuda").normal_(0, 0.02, generator=g)
+    wts = torch.softmax(torch.randn(T, k, device="cuda", generator=g), -1).to(torch.bfloat16)
+    y = torch.empty((T * k, H), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
+    res = torch.empty((T, H), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
+    o = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
+    xp = torch.empty((T * k, H), dtype=torch.float16, device="cuda")
+    st = lambda: kernels._stream(xr.device)  # noqa: E731
+    small = {
+        "router_topk": lambda: moe.router_topk(xr, rw, None, k),
+        "permute": lambda: moe.Routing(idx, E),
+        "gather": lambda: _lib.call("fg_moe_gather", xr.data_ptr(), r.perm_pair.data_ptr(), T, k, H,
+                                    xp.data_ptr(), st()),
+        "unpermute": lambda: _lib.call("fg_moe_unpermute", y.data_ptr(), r.inv.data_ptr(), idx.data_ptr(),
+                                       wts.data_ptr(), res.data_ptr(), o.data_ptr(), T, k, H, st()),
+    }
+    for name, fn in small.items():
+        out.append({"kernel": name, "gemm": name, "T": T, "BN": r.BN, "items": int(r.item_count.item()),
+                    "ms": _time(fn, iters, warmup), "GBps": 0.0, "frac_hbm": 0.0})
     kernels.check_device("moe microbench")
     return out
 

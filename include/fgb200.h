@@ -233,7 +233,8 @@ int fg_moe_gemm_mxfp4(const fg_f16* x, const void* w_packed, const fg_bf16* bias
                       fg_stream_t stream);
 /* out[t] = residual[t] + sum over the k slots in ascending expert id of
  * bf16(y[inv[t*k+j]] * weights[t,j]), each addition rounded to bf16 (the
- * index_add_ order of GptOssExperts.forward); residual may be NULL. */
+ * index_add_ order of GptOssExperts.forward); residual may be NULL.
+ * H % 8 == 0; y, residual and out 16-byte aligned. */
 int fg_moe_unpermute(const fg_bf16* y, const int32_t* inv, const int32_t* indices,
                      const fg_bf16* weights, const fg_bf16* residual, fg_bf16* out, int T, int k,
                      int H, fg_stream_t stream);
