@@ -28,6 +28,7 @@ FG_EPI_STORE = 0
 FG_EPI_RESIDUAL = 1
 FG_EPI_SWIGLU = 2
 FG_EPI_SWIGLU_OAI = 3
+FG_EPI_F32 = 4
 
 FG_NORM_LLAMA = 0
 FG_NORM_FP32MUL = 1
@@ -69,16 +70,17 @@ SIGNATURES: dict[str, tuple] = {
     "fg_moe_router_topk": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P, _P, _P]),
     "fg_moe_tile_tokens": (c_int, [c_int, c_int, c_int]),
     "fg_moe_max_items": (c_int, [c_int, c_int, c_int, c_int]),
-    "fg_moe_permute": (c_int, [_P, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P, _P]),
+    "fg_moe_permute": (c_int, [_P, c_int, c_int, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P, _P]),
     "fg_moe_gather": (c_int, [_P, _P, c_int, c_int, c_int, _P, _P]),
     "fg_pack_mxfp4": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P]),
     "fg_mxfp4_packed_bytes": (c_size_t, [c_int, c_int, c_int]),
     "fg_moe_gemm_mxfp4": (
-        c_int, [_P, _P, _P, _P, _P, _P, c_int, _P, c_int, c_int, c_int, c_int, c_int, _P],
+        c_int, [_P, _P, _P, _P, _P, _P, c_int, _P, c_int, c_int, c_int, c_int, c_int, c_int, _P],
     ),
-    "fg_moe_unpermute": (c_int, [_P, _P, _P, _P, _P, _P, c_int, c_int, c_int, _P]),
+    "fg_moe_unpermute": (c_int, [_P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, _P]),
     "fg_advance": (c_int, [_P, _P, c_int, _P]),
     "fg_add_bf16": (c_int, [_P, _P, _P, ctypes.c_longlong, _P]),
+    "fg_sum_partials": (c_int, [_P, c_int, ctypes.c_longlong, _P, _P]),
     "fg_mailbox_bytes": (c_size_t, [c_int, c_int, c_size_t]),
     "fg_ipc_export": (c_int, [_P, _P, ctypes.POINTER(c_size_t)]),
     "fg_ipc_import": (c_int, [_P, c_size_t, ctypes.POINTER(c_void_p)]),

@@ -232,6 +232,24 @@ __global__ void kv_append_kernel(const uint4* __restrict__ k, const uint4* __res
 }
 
 // out = bf16(a + b), 8 elements per thread
+// out[i] = bf16(p[0][i] + p[1][i] + ... + p[S-1][i]), fp32 sums in shard order
+__global__ void sum_partials_kernel(const float4* __restrict__ parts, int S, long long n4,
+                                    uint2* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  float4 a = parts[i];
+  for (int s = 1; s < S; ++s) {
+    const float4 b = parts[(long long)s * n4 + i];
+    a.x += b.x;
+    a.y += b.y;
+    a.z += b.z;
+    a.w += b.w;
+  }
+  out[i] = make_uint2(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w));
+}
+
 __global__ void add_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
                            uint4* __restrict__ out, long long n8) {
   griddep_wait();
@@ -350,6 +368,18 @@ int fg_add_bf16(const fg_bf16* a, const fg_bf16* b, fg_bf16* out, long long n, f
   return fg::launch_k("fg_add_bf16", fg::add_kernel, dim3((unsigned)((n8 + 255) / 256)), dim3(256), 0,
                       (cudaStream_t)stream, reinterpret_cast<const uint4*>(a),
                       reinterpret_cast<const uint4*>(b), reinterpret_cast<uint4*>(out), n8);
+}
+
+int fg_sum_partials(const float* partials, int S, long long n, fg_bf16* out, fg_stream_t stream) {
+  FG_REQUIRE(partials && out, "fg_sum_partials: null pointer");
+  FG_REQUIRE(S >= 1 && n >= 0 && n % 4 == 0, "fg_sum_partials: S=%d n=%lld (n %% 4 == 0)", S, n);
+  FG_REQUIRE((((uintptr_t)partials) & 15) == 0 && (((uintptr_t)out) & 7) == 0,
+             "fg_sum_partials: alignment");
+  if (n == 0) return FG_OK;
+  const long long n4 = n / 4;
+  return fg::launch_k("fg_sum_partials", fg::sum_partials_kernel, dim3((unsigned)((n4 + 255) / 256)),
+                      dim3(256), 0, (cudaStream_t)stream, reinterpret_cast<const float4*>(partials), S, n4,
+                      reinterpret_cast<uint2*>(out));
 }
 
 int fg_advance(int32_t* positions, int32_t* seq_lens, int B, fg_stream_t stream) {

@@ -208,6 +208,11 @@ __device__ __forceinline__ void apply_epilogue(const Params& p, int tile, int q,
       const int t = t_tile * BN + j0 + i;
       if (t < p.T) {
         float y = v[i] + b;
+        if (p.epilogue == FG_EPI_F32) {
+          if (p.residual) y += bf2f(p.residual[(int64_t)t * p.ldo + n]);
+          reinterpret_cast<float*>(p.out)[(int64_t)t * p.ldo + n] = y;
+          continue;
+        }
         if (p.epilogue == FG_EPI_RESIDUAL) y = bf2f(p.residual[(int64_t)t * p.ldo + n]) + rbf(y);
         p.out[(int64_t)t * p.ldo + n] = f2bf(y);
       }
@@ -686,6 +691,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int t = t_tile * BN + j4 * 4 + i;
         if (t < p.T) {
           float y = vv[i] + b;
+          if (p.epilogue == FG_EPI_F32) {
+            if (p.residual) y += bf2f(p.residual[(int64_t)t * p.ldo + nn]);
+            reinterpret_cast<float*>(p.out)[(int64_t)t * p.ldo + nn] = y;
+            continue;
+          }
           if (p.epilogue == FG_EPI_RESIDUAL) y = bf2f(p.residual[(int64_t)t * p.ldo + nn]) + rbf(y);
           p.out[(int64_t)t * p.ldo + nn] = f2bf(y);
         }
@@ -905,7 +915,8 @@ static int gemm_checks(const fg_bf16* x, const void* w, fg_bf16* out, const fg_b
   FG_REQUIRE(x && w && out, "fg_gemm_bf16: null pointer");
   FG_REQUIRE(T >= 0 && N > 0 && K > 0 && K % 8 == 0, "fg_gemm_bf16: bad sizes T=%d N=%d K=%d", T,
              N, K);
-  FG_REQUIRE(epilogue == FG_EPI_STORE || epilogue == FG_EPI_RESIDUAL || epilogue == FG_EPI_SWIGLU,
+  FG_REQUIRE(epilogue == FG_EPI_STORE || epilogue == FG_EPI_RESIDUAL || epilogue == FG_EPI_SWIGLU ||
+                 epilogue == FG_EPI_F32,
              "fg_gemm_bf16: bad epilogue %d", epilogue);
   FG_REQUIRE(epilogue != FG_EPI_RESIDUAL || residual != nullptr,
              "fg_gemm_bf16: residual epilogue needs a residual");

@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(
 // One CTA of 32 warps. Pair p = t*k + j goes to row offsets[e] + rank, rank =
 // number of earlier pairs (in p order) routed to the same expert.
 __global__ void __launch_bounds__(1024) permute_kernel(
-    const int32_t* __restrict__ idx, int n, int E, int BN, int max_items,
+    const int32_t* __restrict__ idx, int n, int E, int BN, int e_lo, int e_hi, int max_items,
     int32_t* __restrict__ offsets, int32_t* __restrict__ perm_pair, int32_t* __restrict__ inv,
     int32_t* __restrict__ items, int32_t* __restrict__ item_count) {
   griddep_wait();
@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(1024) permute_kernel(
       base[e] = run;
       tile0[e] = ti;
       run += tot[e];
-      ti += (tot[e] + BN - 1) / BN;
+      if (e >= e_lo && e < e_hi) ti += (tot[e] + BN - 1) / BN;  // work items of this shard's experts
     }
     base[E] = run;
     tile0[E] = ti;
@@ -226,22 +226,30 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ x, const int32_t* _
 // out[t] = residual[t] + sum over the k experts (ascending id) of y[inv] * w,
 // each product and partial sum rounded to bf16 as transformers' index_add_
 // accumulation does; 8 features per thread step (H % 8 == 0)
+// With an expert range [e_lo, e_hi) only those slots count (an expert-parallel
+// shard's part) and out_f32 writes the bf16-rounded sum as fp32 for
+// fg_sum_partials.
 __global__ void __launch_bounds__(128) unpermute_kernel(const __nv_bfloat16* __restrict__ y,
                                                         const int32_t* __restrict__ inv,
                                                         const int32_t* __restrict__ idx,
                                                         const __nv_bfloat16* __restrict__ wts,
                                                         const __nv_bfloat16* __restrict__ residual,
-                                                        __nv_bfloat16* __restrict__ out, int k, int H) {
+                                                        void* __restrict__ out_, int k, int H, int e_lo,
+                                                        int e_hi, int out_f32) {
   griddep_wait();
   griddep_launch_dependents();
   __shared__ int s_row[8];
   __shared__ float s_w[8];
+  __shared__ int s_k;
   const int t = blockIdx.x;
   if (threadIdx.x == 0) {
-    int order[8];
-    for (int j = 0; j < k; ++j) order[j] = j;
-    // insertion sort of the k slots by expert id (k <= 8), stable
-    for (int a = 1; a < k; ++a) {
+    int order[8], kk = 0;
+    for (int j = 0; j < k; ++j) {
+      const int e = idx[(int64_t)t * k + j];
+      if (e >= e_lo && e < e_hi) order[kk++] = j;
+    }
+    // insertion sort of the counted slots by expert id (k <= 8), stable
+    for (int a = 1; a < kk; ++a) {
       const int v = order[a];
       int b = a - 1;
       while (b >= 0 && idx[(int64_t)t * k + order[b]] > idx[(int64_t)t * k + v]) {
@@ -250,12 +258,14 @@ __global__ void __launch_bounds__(128) unpermute_kernel(const __nv_bfloat16* __r
       }
       order[b + 1] = v;
     }
-    for (int a = 0; a < k; ++a) {
+    for (int a = 0; a < kk; ++a) {
       s_row[a] = inv[(int64_t)t * k + order[a]];
       s_w[a] = bf2f(wts[(int64_t)t * k + order[a]]);
     }
+    s_k = kk;
   }
   __syncthreads();
+  k = s_k;
   const int H8 = H >> 3;
   for (int c = threadIdx.x; c < H8; c += blockDim.x) {
     float acc[8];
@@ -272,6 +282,12 @@ __global__ void __launch_bounds__(128) unpermute_kernel(const __nv_bfloat16* __r
         acc[2 * i + 1] = rbf(acc[2 * i + 1] + rbf(f.y * wv));
       }
     }
+    if (out_f32) {
+      float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(out_) + (int64_t)t * H) + 2 * c;
+      o4[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      o4[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      continue;
+    }
     uint4 o;
     uint32_t* po = reinterpret_cast<uint32_t*>(&o);
     if (residual) {
@@ -286,7 +302,7 @@ __global__ void __launch_bounds__(128) unpermute_kernel(const __nv_bfloat16* __r
 #pragma unroll
       for (int i = 0; i < 4; ++i) po[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
     }
-    reinterpret_cast<uint4*>(out + (int64_t)t * H)[c] = o;
+    reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out_) + (int64_t)t * H)[c] = o;
   }
 }
 
@@ -403,6 +419,7 @@ struct GemmParams {
   const int32_t* item_count;
   void* out;                  // [rows][ldo]: f16 after SwiGLU-OAI, else bf16
   int N, K, n_tiles, nkb, ldo, epilogue;
+  int e_base;                 // expert id of the first packed expert (expert-parallel shards)
 };
 
 constexpr int kKS = 2;            // records per step
@@ -514,9 +531,10 @@ __device__ __forceinline__ Unit unit_of(const GemmParams& p, int u, int BN) {
   const int item = u / p.n_tiles;
   Unit w;
   w.nt = u - item * p.n_tiles;
-  w.e = p.items[2 * item];
-  w.row0 = p.offsets[w.e] + p.items[2 * item + 1] * BN;
-  w.row_end = p.offsets[w.e + 1];
+  const int e = p.items[2 * item];  // global expert id: rows of x / out
+  w.row0 = p.offsets[e] + p.items[2 * item + 1] * BN;
+  w.row_end = p.offsets[e + 1];
+  w.e = e - p.e_base;               // index into this shard's packed weights and biases
   return w;
 }
 
@@ -847,15 +865,16 @@ int fg_moe_tile_tokens(int T, int k, int E) {
   return avg <= 8 ? 16 : (avg <= 16 ? 32 : 64);
 }
 
-int fg_moe_permute(const int32_t* indices, int T, int k, int E, int BN, int32_t* offsets,
-                   int32_t* perm_pair, int32_t* inv, int32_t* items, int32_t* item_count,
-                   fg_stream_t stream) {
+int fg_moe_permute(const int32_t* indices, int T, int k, int E, int BN, int e_lo, int e_hi,
+                   int32_t* offsets, int32_t* perm_pair, int32_t* inv, int32_t* items,
+                   int32_t* item_count, fg_stream_t stream) {
   FG_REQUIRE(indices && offsets && perm_pair && inv && items && item_count,
              "fg_moe_permute: null pointer");
   FG_REQUIRE(T >= 0 && k > 0 && E > 0 && E <= fg::moe::kMaxE && (BN == 16 || BN == 32 || BN == 64),
              "fg_moe_permute: bad sizes");
+  FG_REQUIRE(0 <= e_lo && e_lo < e_hi && e_hi <= E, "fg_moe_permute: bad expert range [%d, %d)", e_lo, e_hi);
   return fg::launch_k("fg_moe_permute", fg::moe::permute_kernel, dim3(1), dim3(1024), 0,
-                      (cudaStream_t)stream, indices, T * k, E, BN, fg_moe_max_items(T, k, E, BN),
+                      (cudaStream_t)stream, indices, T * k, E, BN, e_lo, e_hi, fg_moe_max_items(T, k, E, BN),
                       offsets, perm_pair, inv, items, item_count);
 }
 
@@ -870,18 +889,19 @@ int fg_moe_gather(const fg_bf16* x, const int32_t* perm_pair, int T, int k, int 
 }
 
 int fg_moe_unpermute(const fg_bf16* y, const int32_t* inv, const int32_t* indices,
-                     const fg_bf16* weights, const fg_bf16* residual, fg_bf16* out, int T, int k,
-                     int H, fg_stream_t stream) {
+                     const fg_bf16* weights, const fg_bf16* residual, void* out, int T, int k,
+                     int H, int e_lo, int e_hi, int out_f32, fg_stream_t stream) {
   FG_REQUIRE(y && inv && indices && weights && out, "fg_moe_unpermute: null pointer");
   FG_REQUIRE(T >= 0 && k > 0 && k <= 8 && H > 0 && H % 8 == 0, "fg_moe_unpermute: bad sizes (H %% 8 == 0)");
+  FG_REQUIRE(e_lo >= 0 && e_lo < e_hi, "fg_moe_unpermute: bad expert range [%d, %d)", e_lo, e_hi);
+  FG_REQUIRE(!out_f32 || residual == nullptr, "fg_moe_unpermute: an fp32 partial takes no residual");
   FG_REQUIRE((((uintptr_t)y | (uintptr_t)out | (uintptr_t)residual) & 15) == 0,
              "fg_moe_unpermute: y/residual/out must be 16-byte aligned");
   if (T == 0) return FG_OK;
   return fg::launch_k("fg_moe_unpermute", fg::moe::unpermute_kernel, dim3(T), dim3(128), 0,
                       (cudaStream_t)stream, reinterpret_cast<const __nv_bfloat16*>(y), inv, indices,
                       reinterpret_cast<const __nv_bfloat16*>(weights),
-                      reinterpret_cast<const __nv_bfloat16*>(residual),
-                      reinterpret_cast<__nv_bfloat16*>(out), k, H);
+                      reinterpret_cast<const __nv_bfloat16*>(residual), out, k, H, e_lo, e_hi, out_f32);
 }
 
 size_t fg_mxfp4_packed_bytes(int E, int N, int K) {
@@ -907,7 +927,7 @@ int fg_pack_mxfp4(const uint8_t* values, const uint8_t* scales, void* packed, in
 
 int fg_moe_gemm_mxfp4(const fg_f16* x, const void* w_packed, const fg_bf16* bias,
                       const int32_t* offsets, const int32_t* items, const int32_t* item_count,
-                      int max_items, void* out, int rows, int N, int K, int BN, int epilogue,
+                      int max_items, void* out, int rows, int N, int K, int BN, int epilogue, int e_base,
                       fg_stream_t stream) {
   using namespace fg::moe;
   FG_REQUIRE(x && w_packed && offsets && items && item_count && out, "fg_moe_gemm_mxfp4: null pointer");
@@ -932,6 +952,7 @@ int fg_moe_gemm_mxfp4(const fg_f16* x, const void* w_packed, const fg_bf16* bias
   p.nkb = K / 64;
   p.ldo = epilogue == FG_EPI_SWIGLU_OAI ? N / 2 : N;
   p.epilogue = epilogue;
+  p.e_base = e_base;
   CUtensorMap tx;
   int rc = fg::make_tmap_2d_bf16(&tx, x, (uint64_t)K, (uint64_t)rows, (uint64_t)K * 2, 64, BN,
                                  CU_TENSOR_MAP_SWIZZLE_128B);

@@ -8,6 +8,14 @@ reference does NCCL send/recv; here it goes to whatever comm backend is
 plugged in (P2PComm for the NVLink handoff, LocalComm on one GPU, or any
 object with get_rank / send_tensor / recv_tensor).
 
+Sharded feed-forward groups (TaskSpec.shard_ranks, a plan-format extension):
+the rank of the task before the group sends its output to every shard rank;
+each shard runs the group on its slice (the callable gets shard=(index,
+count)) and sends an fp32 partial to the rank of the task after the group,
+which receives the partials in shard order and adds them up (fg_sum_partials)
+before running that task: the reduce-by-consumer that replaces an
+all-reduce.
+
 Batch generalisation: the reference preallocates decode receive buffers of
 [1, 1, H] (executor.py:29-41); this executor keeps one [B, 1, H] buffer per
 batch size B seen, since the B200 step decodes a batch of requests.
@@ -36,6 +44,7 @@ class LayerExecutor:
         self._decode_bufs: dict[int, torch.Tensor] = {}
         self._prefill_buf: torch.Tensor | None = None
         self._wide_bufs: dict[tuple, torch.Tensor] = {}
+        self._partial_bufs: dict[tuple, tuple[torch.Tensor, torch.Tensor]] = {}
         if cfg.preallocate_recv_buffers:
             self._decode_bufs[cfg.max_batch] = torch.empty(
                 (cfg.max_batch, 1, profile.hidden_size), dtype=cfg.dtype, device=self.device)
@@ -75,27 +84,59 @@ class LayerExecutor:
         assert mode in ("prefill", "decode"), f"invalid mode {mode}"
         idx = self.task_index_by_name[task_name]
         task = self.tasks[idx]
-        if task.rank_for(mode) != self.my_rank:
+        if task.shard_ranks is not None:
+            # a sharded feed-forward group: every shard rank runs it on its slice
+            if self.my_rank not in task.shard_ranks:
+                return None
+            kwargs["shard"] = (task.shard_ranks.index(self.my_rank), len(task.shard_ranks))
+        elif task.rank_for(mode) != self.my_rank:
             return None
-        prev_rank = self._prev_rank(idx, mode)
-        if prev_rank is not None and prev_rank != self.my_rank:
-            b = batch if batch is not None else (value.shape[0] if value is not None else 1)
-            value = self._recv(mode=mode, batch=b, seq_len=self._seq_len(value, seq_len), src=prev_rank,
-                               width=recv_width)
+        b = batch if batch is not None else (value.shape[0] if value is not None else 1)
+        prev = self.tasks[idx - 1] if idx > 0 else None
+        if prev is not None and prev.shard_ranks is not None:
+            # consumer of a sharded group: add up the shards' fp32 partials
+            value = self._recv_partials(prev.shard_ranks, mode=mode, batch=b,
+                                        seq_len=self._seq_len(value, seq_len))
+        elif prev is not None and prev.rank_for(mode) != self.my_rank:
+            value = self._recv(mode=mode, batch=b, seq_len=self._seq_len(value, seq_len),
+                               src=prev.rank_for(mode), width=recv_width)
         assert value is not None, f"rank {self.my_rank} entered {task_name} without input"
         with trace_region(kind="compute", name=task_name, device=self.device, mode=mode):
             out = _first_tensor(fn(value, **kwargs))
-        next_rank = self._next_rank(idx, mode)
-        if next_rank is not None and next_rank != self.my_rank:
+        nxt = self.tasks[idx + 1] if idx < len(self.tasks) - 1 else None
+        if nxt is not None:
             if not out.is_contiguous():
                 out = out.contiguous()
-            self._comm.send_tensor(out, dst=next_rank)
+            if nxt.shard_ranks is not None:
+                for r in nxt.shard_ranks:  # scatter the group's input to every shard
+                    self._comm.send_tensor(out, dst=r)
+            elif nxt.rank_for(mode) != self.my_rank:
+                self._comm.send_tensor(out, dst=nxt.rank_for(mode))
         return out
 
     def _recv(self, *, mode: str, batch: int, seq_len: int, src: int, width: int | None = None) -> torch.Tensor:
         buf = self._recv_buffer(mode=mode, batch=batch, seq_len=seq_len, width=width)
         self._comm.recv_tensor(buf, src=src)
         return buf
+
+    def _recv_partials(self, shard_ranks: tuple[int, ...], *, mode: str, batch: int,
+                       seq_len: int) -> torch.Tensor:
+        """Receive each shard's fp32 partial [batch, seq_len, H] (shard order)
+        and return bf16(sum) (fg_sum_partials)."""
+        from . import kernels
+
+        H = self.profile.hidden_size
+        S = len(shard_ranks)
+        key = (S, batch, seq_len, mode)
+        bufs = self._partial_bufs.get(key)
+        if bufs is None:
+            bufs = (torch.empty((S, batch, seq_len, H), dtype=torch.float32, device=self.device),
+                    torch.empty((batch, seq_len, H), dtype=self.cfg.dtype, device=self.device))
+            self._partial_bufs[key] = bufs
+        parts, total = bufs
+        for i, r in enumerate(shard_ranks):
+            self._comm.recv_tensor(parts[i], src=r)
+        return kernels.sum_partials(parts, out=total)
 
     def _recv_buffer(self, *, mode: str, batch: int, seq_len: int, width: int | None = None) -> torch.Tensor:
         assert seq_len > 0, f"seq_len must be positive, got {seq_len}"
@@ -129,12 +170,6 @@ class LayerExecutor:
             return int(value.shape[1])
         assert seq_len is not None, "seq_len is required when receiving into an empty value"
         return seq_len
-
-    def _prev_rank(self, idx: int, mode: str) -> int | None:
-        return self.tasks[idx - 1].rank_for(mode) if idx > 0 else None
-
-    def _next_rank(self, idx: int, mode: str) -> int | None:
-        return self.tasks[idx + 1].rank_for(mode) if idx < len(self.tasks) - 1 else None
 
 
 def _first_tensor(value: Any) -> torch.Tensor:

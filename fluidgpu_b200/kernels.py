@@ -184,8 +184,10 @@ def gemm(x: torch.Tensor, w: "torch.Tensor | PackedWeight", *, epilogue: int = _
     N, Kw = w.shape
     assert Kw == K, f"gemm: x has K={K}, w has K={Kw}"
     n_out = N // 2 if epilogue == _lib.FG_EPI_SWIGLU else N
+    out_dtype = torch.float32 if epilogue == _lib.FG_EPI_F32 else _BF16
     if out is None:
-        out = torch.empty((*x.shape[:-1], n_out), dtype=_BF16, device=x.device)
+        out = torch.empty((*x.shape[:-1], n_out), dtype=out_dtype, device=x.device)
+    assert out.dtype == out_dtype, f"gemm: epilogue {epilogue} writes {out_dtype}, out is {out.dtype}"
     if residual is not None:
         _check(residual, "residual", _BF16)
         assert residual.numel() == T * n_out, "residual shape mismatch"
@@ -199,6 +201,19 @@ def gemm(x: torch.Tensor, w: "torch.Tensor | PackedWeight", *, epilogue: int = _
          _ptr(w.data) if packed else _ptr(w), _ptr(out), _ptr(residual), _ptr(bias), T, N, K,
          epilogue, splits, _ptr(ws), ws_bytes, _stream(x.device))
     KernelTimer.stop("gemm", ev, T=T, N=N, K=K)
+    return out
+
+
+def sum_partials(partials: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """[S, ...] fp32 partial sums -> bf16 [...] = sum over S in order (fg_sum_partials)."""
+    _check(partials, "partials", torch.float32)
+    S = partials.shape[0]
+    n = partials[0].numel()
+    if out is None:
+        out = torch.empty(partials.shape[1:], dtype=_BF16, device=partials.device)
+    _check(out, "out", _BF16)
+    assert out.numel() == n, "sum_partials: out size mismatch"
+    call("fg_sum_partials", _ptr(partials), S, n, _ptr(out), _stream(partials.device))
     return out
 
 

@@ -184,7 +184,7 @@ def bench_moe(T: int = 128, E: int = 32, k: int = 4, H: int = 2880, I: int = 288
         "gather": lambda: _lib.call("fg_moe_gather", xr.data_ptr(), r.perm_pair.data_ptr(), T, k, H,
                                     xp.data_ptr(), st()),
         "unpermute": lambda: _lib.call("fg_moe_unpermute", y.data_ptr(), r.inv.data_ptr(), idx.data_ptr(),
-                                       wts.data_ptr(), res.data_ptr(), o.data_ptr(), T, k, H, st()),
+                                       wts.data_ptr(), res.data_ptr(), o.data_ptr(), T, k, H, 0, E, 0, st()),
     }
     for name, fn in small.items():
         out.append({"kernel": name, "gemm": name, "T": T, "BN": r.BN, "items": int(r.item_count.item()),

@@ -121,6 +121,18 @@ def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return torch.stack([gate.view(I // 64, 64, H), up.view(I // 64, 64, H)], dim=1).reshape(2 * I, H)
 
 
+def shard_dense_ffn(w_gate_up: torch.Tensor, w_down: torch.Tensor,
+                    shard: tuple[int, int]) -> tuple[torch.Tensor, torch.Tensor]:
+    """Tensor-parallel slice (index, count) of a dense FFN over the intermediate
+    dimension: features [I*i/S, I*(i+1)/S) (a multiple of 64, so the 64-row
+    gate/up interleave stays whole) -> (gate_up rows, down columns)."""
+    i, S = shard
+    I = w_down.shape[1]
+    assert 0 <= i < S and I % (64 * S) == 0, f"intermediate {I} does not split into {S} shards of 64-multiples"
+    lo, hi = I * i // S, I * (i + 1) // S
+    return w_gate_up[2 * lo:2 * hi].contiguous(), w_down[:, lo:hi].contiguous()
+
+
 @dataclass
 class ModelWeights:
     spec: ModelSpec
@@ -130,6 +142,9 @@ class ModelWeights:
     layers: list[dict[str, torch.Tensor]] = field(default_factory=list)
     inv_freq: torch.Tensor | None = None
     rope_scaling: float = 1.0
+    # (index, count) when this rank holds one shard of every feed-forward
+    # group: the intermediate slice of a dense FFN, or a range of experts
+    ffn_shard: tuple[int, int] | None = None
 
     @property
     def device(self) -> torch.device:
@@ -160,10 +175,13 @@ class ModelWeights:
     @classmethod
     def random(cls, spec: ModelSpec, seed: int = 0, device: str | torch.device = "cuda",
                std: float = 0.02, layers: list[int] | None = None,
-               dtype: torch.dtype = torch.bfloat16) -> "ModelWeights":
+               dtype: torch.dtype = torch.bfloat16,
+               ffn_shard: tuple[int, int] | None = None) -> "ModelWeights":
         """N(0, std) weights from a seeded generator on `device` (norm weights 1,
         biases 0, as transformers initialises them). `layers` limits which
-        layers get weights (the others stay empty dicts)."""
+        layers get weights (the others stay empty dicts). `ffn_shard` keeps one
+        tensor-/expert-parallel shard of the FFNs (the same draws as the whole
+        model, then sliced)."""
         device = torch.device(device)
         g = torch.Generator(device=device).manual_seed(seed)
 
@@ -196,16 +214,21 @@ class ModelWeights:
             if spec.moe:
                 from . import moe
 
-                L.update(moe.random_expert_weights(spec, normal, device, dtype))
+                L.update(moe.random_expert_weights(spec, normal, device, dtype, ffn_shard))
             else:
                 L["w_gate_up"] = interleave_gate_up(normal(I, H), normal(I, H))
                 L["w_down"] = normal(H, I)
+                if ffn_shard is not None:
+                    L["w_gate_up"], L["w_down"] = shard_dense_ffn(L["w_gate_up"], L["w_down"], ffn_shard)
             out.layers.append(L)
+        out.ffn_shard = ffn_shard
         return out.finalize()
 
     @classmethod
-    def from_hf(cls, hf_model: Any, device: str | torch.device) -> "ModelWeights":
-        """Import an HF LlamaForCausalLM / GptOssForCausalLM (any dtype)."""
+    def from_hf(cls, hf_model: Any, device: str | torch.device,
+                ffn_shard: tuple[int, int] | None = None) -> "ModelWeights":
+        """Import an HF LlamaForCausalLM / GptOssForCausalLM (any dtype);
+        `ffn_shard` as in random()."""
         cfg = hf_model.config
         device = torch.device(device)
         bf = lambda t: t.detach().to(device=device, dtype=torch.bfloat16).contiguous()  # noqa: E731
@@ -248,12 +271,15 @@ class ModelWeights:
             if spec.moe:
                 from . import moe
 
-                L.update(moe.expert_weights_from_hf(layer.mlp, device))
+                L.update(moe.expert_weights_from_hf(layer.mlp, device, ffn_shard))
             else:
                 mlp = layer.mlp
                 L["w_gate_up"] = interleave_gate_up(bf(mlp.gate_proj.weight), bf(mlp.up_proj.weight))
                 L["w_down"] = bf(mlp.down_proj.weight)
+                if ffn_shard is not None:
+                    L["w_gate_up"], L["w_down"] = shard_dense_ffn(L["w_gate_up"], L["w_down"], ffn_shard)
             out.layers.append(L)
+        out.ffn_shard = ffn_shard
         return out.finalize()
 
 

@@ -91,10 +91,22 @@ def pack_mxfp4(values: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def expert_range(E: int, shard: tuple[int, int] | None) -> tuple[int, int]:
+    """Experts [lo, hi) held by expert-parallel shard (index, count): equal
+    contiguous ranges."""
+    if shard is None:
+        return 0, E
+    i, S = shard
+    assert 0 <= i < S and E % S == 0, f"{E} experts do not split evenly over {S} shards"
+    return E * i // S, E * (i + 1) // S
+
+
 def _expert_tensors(w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor, b2: torch.Tensor,
-                    device: torch.device) -> dict[str, Any]:
+                    device: torch.device, shard: tuple[int, int] | None = None) -> dict[str, Any]:
     """w1 [E, 2I, H] (transformers' gate/up row order), b1 [E, 2I], w2 [E, H, I],
-    b2 [E, H] (any float dtype) -> packed device tensors."""
+    b2 [E, H] (any float dtype) -> packed device tensors (of shard's experts)."""
+    lo, hi = expert_range(w1.shape[0], shard)
+    w1, b1, w2, b2 = w1[lo:hi], b1[lo:hi], w2[lo:hi], b2[lo:hi]
     E, N1, H = w1.shape
     I = N1 // 2
     w1 = interleave64(w1.to(device))
@@ -107,21 +119,23 @@ def _expert_tensors(w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor, b2: to
         "moe_w2": pack_mxfp4(v2.contiguous(), s2.contiguous()),
         "moe_b2": b2.to(device=device, dtype=torch.bfloat16).contiguous(),
         "moe_shape": (E, H, I),
+        "moe_expert_range": (lo, hi),
     }
 
 
-def random_expert_weights(spec, normal, device: torch.device, dtype: torch.dtype) -> dict[str, Any]:
+def random_expert_weights(spec, normal, device: torch.device, dtype: torch.dtype,
+                          shard: tuple[int, int] | None = None) -> dict[str, Any]:
     E, H, I = spec.num_experts, spec.hidden, spec.intermediate
     out = {"router_w": normal(E, H), "router_b": torch.zeros(E, dtype=dtype, device=device)}
     w1 = normal(E, 2 * I, H)
     w2 = normal(E, H, I)
     out.update(_expert_tensors(w1, torch.zeros(E, 2 * I, device=device), w2,
-                               torch.zeros(E, H, device=device), device))
+                               torch.zeros(E, H, device=device), device, shard))
     return out
 
 
-def expert_weights_from_hf(mlp: Any, device: torch.device) -> dict[str, Any]:
-    """transformers GptOssMLP -> router + packed MXFP4 experts."""
+def expert_weights_from_hf(mlp: Any, device: torch.device, shard: tuple[int, int] | None = None) -> dict[str, Any]:
+    """transformers GptOssMLP -> router + packed MXFP4 experts (of shard's experts)."""
     ex = mlp.experts
     bf = lambda t: t.detach().to(device=device, dtype=torch.bfloat16).contiguous()  # noqa: E731
     out = {"router_w": bf(mlp.router.weight), "router_b": bf(mlp.router.bias)}
@@ -129,7 +143,7 @@ def expert_weights_from_hf(mlp: Any, device: torch.device) -> dict[str, Any]:
     out.update(_expert_tensors(ex.gate_up_proj.detach().transpose(1, 2).float(),
                                ex.gate_up_proj_bias.detach().float(),
                                ex.down_proj.detach().transpose(1, 2).float(),
-                               ex.down_proj_bias.detach().float(), device))
+                               ex.down_proj_bias.detach().float(), device, shard))
     return out
 
 
@@ -150,13 +164,15 @@ def router_topk(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, k: int
 
 
 class Routing:
-    """Device buffers of one permutation (fg_moe_permute)."""
+    """Device buffers of one permutation (fg_moe_permute). expert_range limits
+    the work items to an expert-parallel shard's experts [lo, hi)."""
 
-    def __init__(self, idx: torch.Tensor, E: int) -> None:
+    def __init__(self, idx: torch.Tensor, E: int, expert_range: tuple[int, int] | None = None) -> None:
         T, k = idx.shape
         lib = _lib.lib()
         dev = idx.device
         self.T, self.k, self.E = T, k, E
+        self.lo, self.hi = expert_range if expert_range is not None else (0, E)
         self.BN = lib.fg_moe_tile_tokens(T, k, E)
         self.max_items = lib.fg_moe_max_items(T, k, E, self.BN)
         self.offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
@@ -164,7 +180,7 @@ class Routing:
         self.inv = torch.empty(T * k, dtype=torch.int32, device=dev)
         self.items = torch.empty(max(self.max_items, 1) * 2, dtype=torch.int32, device=dev)
         self.item_count = torch.empty(1, dtype=torch.int32, device=dev)
-        call("fg_moe_permute", idx.data_ptr(), T, k, E, self.BN, self.offsets.data_ptr(),
+        call("fg_moe_permute", idx.data_ptr(), T, k, E, self.BN, self.lo, self.hi, self.offsets.data_ptr(),
              self.perm_pair.data_ptr(), self.inv.data_ptr(), self.items.data_ptr(),
              self.item_count.data_ptr(), kernels._stream(dev))
 
@@ -182,26 +198,33 @@ def grouped_gemm(x_perm: torch.Tensor, w_packed: torch.Tensor, bias: torch.Tenso
     call("fg_moe_gemm_mxfp4", x_perm.data_ptr(), w_packed.data_ptr(),
          None if bias is None else bias.data_ptr(), routing.offsets.data_ptr(),
          routing.items.data_ptr(), routing.item_count.data_ptr(), routing.max_items,
-         out.data_ptr(), rows, N, K, routing.BN, epilogue, kernels._stream(x_perm.device))
+         out.data_ptr(), rows, N, K, routing.BN, epilogue, routing.lo, kernels._stream(x_perm.device))
     return out
 
 
 def experts_forward(x: torch.Tensor, idx: torch.Tensor, weights: torch.Tensor, W: dict, spec,
                     residual: torch.Tensor | None = None) -> torch.Tensor:
     """Routed experts for x [T, H] (post-norm): permute -> gate_up + SwiGLU-OAI
-    -> down -> weighted un-permute (+ residual when given)."""
+    -> down -> weighted un-permute (+ residual when given). Weights holding an
+    expert-parallel shard (W["moe_expert_range"]) give that shard's fp32
+    partial [T, H] (no residual) for fg_sum_partials."""
     T, H = x.shape
-    E, H_, I = W["moe_shape"]
+    E_local, H_, I = W["moe_shape"]
+    E = spec.num_experts
     k = idx.shape[1]
-    routing = Routing(idx, E)
+    lo, hi = W.get("moe_expert_range", (0, E))
+    assert hi - lo == E_local, f"packed experts {E_local} != range [{lo}, {hi})"
+    partial = (lo, hi) != (0, E)
+    assert not (partial and residual is not None), "an expert-parallel partial takes no residual"
+    routing = Routing(idx, E, (lo, hi))
     x_perm = torch.empty((T * k, H), dtype=torch.float16, device=x.device)
     call("fg_moe_gather", x.data_ptr(), routing.perm_pair.data_ptr(), T, k, H, x_perm.data_ptr(),
          kernels._stream(x.device))
     act = grouped_gemm(x_perm, W["moe_w1"], W["moe_b1"], routing, 2 * I, H, _lib.FG_EPI_SWIGLU_OAI)
     y = grouped_gemm(act, W["moe_w2"], W["moe_b2"], routing, H, I, _lib.FG_EPI_STORE)
-    out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+    out = torch.empty((T, H), dtype=torch.float32 if partial else torch.bfloat16, device=x.device)
     call("fg_moe_unpermute", y.data_ptr(), routing.inv.data_ptr(), idx.data_ptr(), weights.data_ptr(),
-         None if residual is None else residual.data_ptr(), out.data_ptr(), T, k, H,
+         None if residual is None else residual.data_ptr(), out.data_ptr(), T, k, H, lo, hi, int(partial),
          kernels._stream(x.device))
     return out
 

@@ -36,6 +36,9 @@ VALID_SEQUENCES = (
 )
 
 
+SHARDABLE = ("mlp", "moe_experts")
+
+
 @dataclass(frozen=True)
 class TaskSpec:
     task_id: int
@@ -43,6 +46,13 @@ class TaskSpec:
     name: str
     rank: int
     decode_rank: int | None = None
+    # Extension of the reference's plan format: a feed-forward group run by
+    # several ranks at once, each on one shard (dense `mlp`: a slice of the
+    # intermediate dimension; `moe_experts`: a range of experts). The rank of
+    # the task before it sends it its input, every shard returns an fp32
+    # partial, and the same rank, which runs the task after it, adds the
+    # partials up (reduce-by-consumer). `rank` is then shard_ranks[0].
+    shard_ranks: tuple[int, ...] | None = None
 
     def rank_for(self, mode: str) -> int:
         if mode == "decode" and self.decode_rank is not None:
@@ -120,8 +130,17 @@ def _parse_tasks(raw: list[dict[str, Any]]) -> tuple[TaskSpec, ...]:
                 out.append(TaskSpec(tid, tid, f"layer_{layer[0]}_{suffix}", rank,
                                     decode_rank if suffix == "mlp" else None))
             continue
+        shard_ranks = item.get("shard_ranks")
+        if shard_ranks is not None:
+            shard_ranks = tuple(int(r) for r in shard_ranks)
+            suffix = layer[1] if layer is not None else name
+            assert suffix in SHARDABLE, f"shard_ranks is only supported on {SHARDABLE} (got {name})"
+            assert decode_rank is None, f"{name}: shard_ranks and decode_rank cannot be combined"
+            assert len(shard_ranks) >= 1 and len(set(shard_ranks)) == len(shard_ranks), (
+                f"{name}: shard_ranks must be distinct, got {shard_ranks}")
+            assert rank == shard_ranks[0], f"{name}: rank must be shard_ranks[0]"
         tid = len(out)
-        out.append(TaskSpec(tid, tid, name, rank, decode_rank))
+        out.append(TaskSpec(tid, tid, name, rank, decode_rank, shard_ranks))
     return tuple(out)
 
 
@@ -178,6 +197,18 @@ def validate_profile(profile: RuntimeProfile, *, model_name: str | None = None,
         )
         if t.decode_rank is not None:
             assert 0 <= t.decode_rank < profile.rank_count, f"invalid decode_rank for {t.name}"
+        if t.shard_ranks is not None:
+            assert all(0 <= r < profile.rank_count for r in t.shard_ranks), (
+                f"invalid shard_ranks {t.shard_ranks} for {t.name} under rank_count={profile.rank_count}")
+            assert 0 < i < len(profile.tasks) - 1, f"{t.name}: a sharded group needs a task before and after"
+            before, after = profile.tasks[i - 1], profile.tasks[i + 1]
+            assert before.shard_ranks is None and after.shard_ranks is None, (
+                f"{t.name}: neighbouring tasks of a sharded group must not be sharded")
+            assert before.decode_rank is None and after.decode_rank is None, (
+                f"{t.name}: neighbouring tasks of a sharded group must keep one rank")
+            assert before.rank == after.rank and before.rank not in t.shard_ranks, (
+                f"{t.name}: the tasks before and after a sharded group must run on one rank outside it "
+                "(it scatters the input and adds up the partials)")
     by_name = profile.task_by_name
     assert by_name["embed"].rank == 0, "embed must be assigned to rank 0"
     assert by_name["norm_lm_head"].rank == 0, "norm_lm_head must be assigned to rank 0"
@@ -209,6 +240,18 @@ def owned_layer_ids(profile: RuntimeProfile, rank: int) -> list[int]:
     return owned
 
 
+def ffn_shard_of(profile: RuntimeProfile, rank: int) -> tuple[int, int] | None:
+    """(index, count) of the feed-forward shard `rank` holds in this plan (the
+    same for every sharded group), or None."""
+    found = None
+    for t in profile.tasks:
+        if t.shard_ranks is not None and rank in t.shard_ranks:
+            s = (t.shard_ranks.index(rank), len(t.shard_ranks))
+            assert found in (None, s), f"rank {rank} holds different shards in different layers"
+            found = s
+    return found
+
+
 def kv_layer_ids(profile: RuntimeProfile, rank: int) -> list[int]:
     """Layers whose paged KV lives on `rank`: where the attention reads it
     (attn, or sdpa in a split plan). Equal to owned_layer_ids except when
@@ -224,22 +267,51 @@ def kv_layer_ids(profile: RuntimeProfile, rank: int) -> list[int]:
     return owned
 
 
-def make_ranked_task_profile(*, model: str, task_assignments: list[tuple[str, int]],
+def make_ranked_task_profile(*, model: str, task_assignments: list[tuple[str, Any]],
                              hidden_size: int, num_kv_heads: int, head_dim: int,
                              max_seq_len: int = 2048, dtype: torch.dtype = torch.bfloat16,
                              rank_count: int | None = None) -> dict[str, Any]:
-    """Plan dict with embed/norm_lm_head on rank 0 around the given tasks."""
-    n_ranks = rank_count if rank_count is not None else max(1, max((r for _, r in task_assignments), default=0) + 1)
+    """Plan dict with embed/norm_lm_head on rank 0 around the given tasks. A
+    rank given as a list makes the task a sharded group over those ranks."""
+    def ranks_of(r: Any) -> list[int]:
+        return list(r) if isinstance(r, (list, tuple)) else [r]
+
+    top = max((x for _, r in task_assignments for x in ranks_of(r)), default=0)
+    n_ranks = rank_count if rank_count is not None else max(1, top + 1)
     tasks = [{"task_id": 0, "kernel_group_id": 0, "name": "embed", "rank": 0}]
     for name, rank in task_assignments:
-        assert 0 <= rank < n_ranks, f"invalid rank {rank} for {name} under rank_count={n_ranks}"
+        rs = ranks_of(rank)
+        assert all(0 <= x < n_ranks for x in rs), f"invalid rank {rank} for {name} under rank_count={n_ranks}"
         tid = len(tasks)
-        tasks.append({"task_id": tid, "kernel_group_id": tid, "name": name, "rank": rank})
+        t = {"task_id": tid, "kernel_group_id": tid, "name": name, "rank": rs[0]}
+        if isinstance(rank, (list, tuple)):
+            t["shard_ranks"] = rs
+        tasks.append(t)
     tid = len(tasks)
     tasks.append({"task_id": tid, "kernel_group_id": tid, "name": "norm_lm_head", "rank": 0})
     return {"model": model, "rank_count": n_ranks, "task_count": len(tasks),
             "hidden_size": hidden_size, "num_kv_heads": num_kv_heads, "head_dim": head_dim,
             "dtype": dtype_name(dtype), "max_seq_len": max_seq_len, "tasks": tasks}
+
+
+def sharded_ffn_profile(model: str, num_layers: int, hidden_size: int, num_kv_heads: int,
+                        head_dim: int, max_seq_len: int, shard_ranks: list[int],
+                        moe: bool = False) -> dict[str, Any]:
+    """Attention (and embed, head, MoE router and combine) on rank 0, every
+    layer's feed-forward group sharded over shard_ranks: the tensor-parallel
+    FFN of config 4 (intermediate split) or the expert-parallel MoE of
+    config 3 (experts split)."""
+    tasks: list[tuple[str, Any]] = []
+    for i in range(num_layers):
+        tasks.append((f"layer_{i}_attn", 0))
+        if moe:
+            tasks += [(f"layer_{i}_moe_router", 0), (f"layer_{i}_moe_experts", list(shard_ranks)),
+                      (f"layer_{i}_moe_combine", 0)]
+        else:
+            tasks.append((f"layer_{i}_mlp", list(shard_ranks)))
+    return make_ranked_task_profile(model=model, task_assignments=tasks, hidden_size=hidden_size,
+                                    num_kv_heads=num_kv_heads, head_dim=head_dim, max_seq_len=max_seq_len,
+                                    rank_count=1 + max(shard_ranks))
 
 
 def colocated_profile(model: str, num_layers: int, hidden_size: int, num_kv_heads: int,

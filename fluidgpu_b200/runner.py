@@ -27,6 +27,12 @@ rank travels as aux tensors in a fixed order (runner.py:462-654):
   gate_up -> down    : SwiGLU intermediate [B, I], residual
   router -> experts  : top-k weights [B, k] bf16, expert ids [B, k] int32, residual
   experts -> combine : residual
+A feed-forward group sharded over several ranks (plan extension shard_ranks,
+see executor.py) runs here on this rank's slice: a dense FFN on its
+intermediate columns (fp32 partial; shard 0 adds the residual), the MoE
+experts on its expert range (fp32 partial of the weighted sum; the router
+sends top-k weights and ids to every shard and keeps the residual for the
+combine group).
 The reference ships q plus the whole K/V view from qkv to sdpa; here the KV
 pages live on the sdpa rank (profile.kv_layer_ids) and RoPE + append run
 there, so only the new token's projection crosses.
@@ -258,13 +264,22 @@ class FluidRunner:
             st["residual"] = self._recv_aux((B, self.spec.hidden), torch.bfloat16, src)
         return st
 
-    def _run_mlp(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+    def _run_mlp(self, hidden: torch.Tensor, *, layer: int, shard: tuple[int, int] | None = None,
+                 **_: Any) -> torch.Tensor:
         s = self.spec
         W = self.weights.layers[layer]
         B = hidden.shape[0]
         h = hidden.reshape(B, s.hidden)
         x = kernels.rmsnorm(h, W["ln2"], s.eps, s.norm_mode)
         act = kernels.gemm(x, W["w_gate_up"], epilogue=_lib.FG_EPI_SWIGLU, slot=self.slot + ".gemm")
+        if shard is not None:
+            # tensor-parallel slice: fp32 partial of the down projection, the
+            # first shard carrying the residual; the consumer adds them up
+            assert self.weights.ffn_shard == shard, (
+                f"layer {layer}: plan shard {shard} != weights shard {self.weights.ffn_shard}")
+            out = kernels.gemm(act, W["w_down"], epilogue=_lib.FG_EPI_F32,
+                               residual=h if shard[0] == 0 else None, slot=self.slot + ".gemm")
+            return out.view(B, 1, s.hidden)
         out = kernels.gemm(act, W["w_down"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h,
                            slot=self.slot + ".gemm")
         return out.view(B, 1, s.hidden)
@@ -316,11 +331,23 @@ class FluidRunner:
             self.last_routing[layer] = idx
         return x.view(B, 1, s.hidden)
 
-    def _run_moe_experts(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+    def _run_moe_experts(self, hidden: torch.Tensor, *, layer: int, shard: tuple[int, int] | None = None,
+                         **_: Any) -> torch.Tensor:
         from . import moe
 
         s = self.spec
         B = hidden.shape[0]
+        if shard is not None:
+            # expert-parallel shard: fp32 partial over this rank's experts
+            assert self.weights.ffn_shard == shard, (
+                f"layer {layer}: plan shard {shard} != weights shard {self.weights.ffn_shard}")
+            src = self._rank_of(layer, "moe_router")
+            wts = self._recv_aux((B, s.top_k), torch.bfloat16, src)
+            idx = self._recv_aux((B, s.top_k), torch.int32, src)
+            if self.record_routing:
+                self.last_routing[layer] = idx
+            y = moe.experts_forward(hidden.reshape(B, s.hidden), idx, wts, self.weights.layers[layer], s)
+            return y.view(B, 1, s.hidden)
         st = self._moe_states.setdefault(layer, {})
         if "indices" not in st:
             src = self._rank_of(layer, "moe_router")
@@ -348,6 +375,15 @@ class FluidRunner:
         return moe.residual_add(st["residual"], hidden.reshape(B, -1)).view(B, 1, -1)
 
     def _after_moe_router(self, layer: int) -> None:
+        shards = self._shards_of(layer, "moe_experts")
+        if shards is not None:
+            # every shard needs the routing; the residual stays here for the
+            # combine group (same rank, checked by the plan validation)
+            st = self._moe_states[layer]
+            for r in shards:
+                self._send_aux(st["weights"], r)
+                self._send_aux(st["indices"], r)
+            return
         dst = self._rank_of(layer, "moe_experts")
         if dst == self._rank_of(layer, "moe_router"):
             return
@@ -357,6 +393,8 @@ class FluidRunner:
         self._send_aux(st["residual"], dst)
 
     def _after_moe_experts(self, layer: int) -> None:
+        if self._shards_of(layer, "moe_experts") is not None:
+            return  # partials go to the combine rank through the executor
         st = self._moe_states.get(layer)
         if st is None:
             return
@@ -371,6 +409,10 @@ class FluidRunner:
     # -- aux routing (runner.py:462-670) ----------------------------------------
     def _rank_of(self, layer: int, suffix: str) -> int:
         return self.executor.task_rank(f"layer_{layer}_{suffix}", "decode")
+
+    def _shards_of(self, layer: int, suffix: str) -> tuple[int, ...] | None:
+        ex = self.executor
+        return ex.tasks[ex.task_index_by_name[f"layer_{layer}_{suffix}"]].shard_ranks
 
     def _send_aux(self, t: torch.Tensor, dst: int) -> None:
         self.executor.send_aux_tensor(t if t.is_contiguous() else t.contiguous(), dst=dst)
@@ -404,6 +446,8 @@ class FluidRunner:
             sizes += [batch * s.qkv_width * 2, batch * s.n_q * s.head_dim * 2]
         if any(n.endswith("_mlp_gate_up") for n in names):
             sizes.append(batch * s.intermediate * 2)
+        if any(t.shard_ranks is not None for t in self.executor.tasks):
+            sizes.append(batch * s.hidden * 4)  # fp32 partials
         return max(sizes)
 
     def reserve_workspaces(self, batch: int, plan_len: int) -> None:

@@ -43,6 +43,8 @@ typedef struct CUstream_st* fg_stream_t; /* == cudaStream_t */
 #define FG_EPI_RESIDUAL 1  /* out[t,n] = bf16(residual[t,n] + bf16(acc (+ bias))) */
 #define FG_EPI_SWIGLU 2    /* out[t,j] = bf16(silu(g) * u), g/u rows interleaved per 64 */
 #define FG_EPI_SWIGLU_OAI 3 /* gpt-oss: (clamp(u,-7,7)+1) * g' * sigmoid(1.702 g'), g' = min(g,7) */
+#define FG_EPI_F32 4       /* out[t,n] = acc (+ bias) (+ residual[t,n] if given), fp32 out: a
+                            * tensor-parallel partial sum, added up by fg_sum_partials */
 
 /* RMSNorm weight application (fg_rmsnorm) */
 #define FG_NORM_LLAMA 0    /* w * bf16(x * rstd)    (LlamaRMSNorm)  */
@@ -202,9 +204,9 @@ int fg_moe_max_items(int T, int k, int E, int BN);
  * offsets:[E+1] rows of each expert; perm_pair:[T*k] pair id (t*k+j) of each
  * permuted row (pairs of one expert stay in (t, j) order); inv:[T*k] row of
  * each pair; items:[fg_moe_max_items][2] (expert, token tile), item_count:[1]. */
-int fg_moe_permute(const int32_t* indices, int T, int k, int E, int BN, int32_t* offsets,
-                   int32_t* perm_pair, int32_t* inv, int32_t* items, int32_t* item_count,
-                   fg_stream_t stream);
+int fg_moe_permute(const int32_t* indices, int T, int k, int E, int BN, int e_lo, int e_hi,
+                   int32_t* offsets, int32_t* perm_pair, int32_t* inv, int32_t* items,
+                   int32_t* item_count, fg_stream_t stream);
 /* out[i,:] = x[perm_pair[i] / k, :] for the T*k permuted rows, as f16 (the
  * operand type of fg_moe_gemm_mxfp4; every bf16 value with |x| >= 2^-17 is
  * exact in f16, smaller ones round to the f16 subnormal step 2^-24). */
@@ -226,23 +228,35 @@ size_t fg_mxfp4_packed_bytes(int E, int N, int K);
  * (+ bias[e]) -> out: bf16 [rows,N]; FG_EPI_SWIGLU_OAI (+ bias, gate/up rows
  * interleaved per 64, SwiGLU-OAI rounded to bf16 per op) -> out: f16
  * [rows,N/2] (the bf16 values, the next call's operand). Only experts that
- * received tokens read their weights. */
+ * received tokens read their weights. w_packed holds experts e_base, e_base+1,
+ * ... (an expert-parallel shard's slice; 0 for all experts). */
 int fg_moe_gemm_mxfp4(const fg_f16* x, const void* w_packed, const fg_bf16* bias,
                       const int32_t* offsets, const int32_t* items, const int32_t* item_count,
-                      int max_items, void* out, int rows, int N, int K, int BN, int epilogue,
+                      int max_items, void* out, int rows, int N, int K, int BN, int epilogue, int e_base,
                       fg_stream_t stream);
 /* out[t] = residual[t] + sum over the k slots in ascending expert id of
  * bf16(y[inv[t*k+j]] * weights[t,j]), each addition rounded to bf16 (the
  * index_add_ order of GptOssExperts.forward); residual may be NULL.
- * H % 8 == 0; y, residual and out 16-byte aligned. */
+ * Only slots whose expert lies in [e_lo, e_hi) count (an expert-parallel
+ * shard's part; 0, E for all); out_f32 != 0 writes that sum as fp32 (no
+ * residual) for fg_sum_partials, else bf16. H % 8 == 0; 16-byte aligned. */
 int fg_moe_unpermute(const fg_bf16* y, const int32_t* inv, const int32_t* indices,
-                     const fg_bf16* weights, const fg_bf16* residual, fg_bf16* out, int T, int k,
-                     int H, fg_stream_t stream);
+                     const fg_bf16* weights, const fg_bf16* residual, void* out, int T, int k,
+                     int H, int e_lo, int e_hi, int out_f32, fg_stream_t stream);
 
 /* out = bf16(a + b) over n bf16 elements (n % 8 == 0): the residual add of
  * the moe_combine group (runner.py:454-457) when it runs apart from the
  * experts group (otherwise fg_moe_unpermute fuses it). */
 int fg_add_bf16(const fg_bf16* a, const fg_bf16* b, fg_bf16* out, long long n, fg_stream_t stream);
+
+/* out[i] = bf16(partials[0][i] + ... + partials[S-1][i]), fp32 sums in shard
+ * order: the consumer side of a sharded feed-forward group (tensor-parallel
+ * FFN partials, the first carrying the residual; expert-parallel MoE
+ * partials), the reduce-by-consumer that replaces an all-reduce. partials
+ * [S][n] fp32, n % 4 == 0. No counterpart in the reference, which runs each
+ * FFN group on one rank (its vLLM path sums two expert halves with a torch
+ * add, vllm_integration.py:1085-1093). */
+int fg_sum_partials(const float* partials, int S, long long n, fg_bf16* out, fg_stream_t stream);
 
 /* ---- NVLink hand-off between ranks (replaces the NCCL send/recv of
  * ProcessGroupComm.send_tensor / recv_tensor, comm.py:24-46, at the task

@@ -139,7 +139,7 @@ def test_unpermute_order_and_residual():
     out = torch.empty(T, H, dtype=torch.bfloat16, device=DEV)
     yd, idxd, wd, rd = y.to(DEV), idx.to(DEV), wts.to(DEV), res.to(DEV)  # keep the device copies alive
     _lib.call("fg_moe_unpermute", yd.data_ptr(), r.inv.data_ptr(), idxd.data_ptr(), wd.data_ptr(),
-              rd.data_ptr(), out.data_ptr(), T, k, H, torch.cuda.current_stream().cuda_stream)
+              rd.data_ptr(), out.data_ptr(), T, k, H, 0, E, 0, torch.cuda.current_stream().cuda_stream)
     inv = r.inv.cpu().long()
     exp = torch.zeros(T, H, dtype=torch.bfloat16)
     for t in range(T):
@@ -147,6 +147,22 @@ def test_unpermute_order_and_residual():
             exp[t] += y[inv[t * k + j]] * wts[t, j]
     exp = res + exp
     assert torch.equal(out.cpu(), exp)
+    # expert-parallel halves: each shard's slots only, fp32 partials; their
+    # sum is the shard-ordered sum of the two bf16 partial sums
+    parts = torch.empty(2, T, H, dtype=torch.float32, device=DEV)
+    for sh, (lo, hi) in enumerate(((0, E // 2), (E // 2, E))):
+        _lib.call("fg_moe_unpermute", yd.data_ptr(), r.inv.data_ptr(), idxd.data_ptr(), wd.data_ptr(), None,
+                  parts[sh].data_ptr(), T, k, H, lo, hi, 1, torch.cuda.current_stream().cuda_stream)
+        ref = torch.zeros(T, H, dtype=torch.bfloat16)
+        for t in range(T):
+            for j in sorted(range(k), key=lambda j: int(idx[t, j])):
+                if lo <= int(idx[t, j]) < hi:
+                    ref[t] += y[inv[t * k + j]] * wts[t, j]
+        assert torch.equal(parts[sh].cpu(), ref.float()), f"shard {sh} partial"
+    from fluidgpu_b200 import kernels
+
+    total = kernels.sum_partials(parts)
+    assert torch.equal(total.cpu(), (parts[0].cpu() + parts[1].cpu()).to(torch.bfloat16))
 
 
 def _tiny_gptoss(seed=0):

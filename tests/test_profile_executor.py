@@ -203,3 +203,75 @@ def test_fine_attention_edge_widths_and_kv_placement():
     assert tuple(seen["layer_0_o_proj"].shape) == (3, 1, 6)
     assert comm.send_log == [((3, 1, 4), 1), ((3, 1, 4), 1)]  # qkv -> sdpa, o_proj -> mlp
     assert comm.recv_log == [((3, 1, 6), 1)]
+
+
+def test_sharded_group_plan_rules():
+    from fluidgpu_b200.profile import ffn_shard_of, sharded_ffn_profile
+
+    prof = profile_from_dict(sharded_ffn_profile("m", 2, 4, 2, 2, 8, shard_ranks=[1, 2, 3]))
+    assert prof.rank_count == 4
+    assert [ffn_shard_of(prof, r) for r in range(4)] == [None, (0, 3), (1, 3), (2, 3)]
+    assert owned_layer_ids(prof, 0) == [0, 1]
+    moe = profile_from_dict(sharded_ffn_profile("m", 1, 4, 2, 2, 8, shard_ranks=[1, 2], moe=True))
+    assert moe.task_by_name["layer_0_moe_experts"].shard_ranks == (1, 2)
+    bad = [
+        ([("layer_0_attn", 0), ("layer_0_mlp", [0, 1])], "outside it"),        # producer among the shards
+        ([("layer_0_attn", 1), ("layer_0_mlp", [2, 3])], "outside it"),        # producer 1, consumer 0
+        ([("layer_0_attn", [0, 1]), ("layer_0_mlp", 0)], "only supported on"),  # attention cannot shard
+    ]
+    for tasks, msg in bad:
+        raw = make_ranked_task_profile(model="m", task_assignments=tasks, hidden_size=4, num_kv_heads=2,
+                                       head_dim=2, rank_count=4)
+        with pytest.raises(AssertionError, match=msg):
+            profile_from_dict(raw)
+
+
+def test_sharded_group_scatter_and_reduce(monkeypatch):
+    """Rank 0 runs attention, ranks 1 and 2 each run a shard of the FFN: both
+    shards receive rank 0's output, each returns an fp32 partial, and rank 0
+    adds them up (shard order) before the next task."""
+    from fluidgpu_b200 import kernels
+    from fluidgpu_b200.profile import sharded_ffn_profile
+
+    def sum_partials(parts, out=None):
+        total = parts.sum(0).to(torch.bfloat16)
+        if out is not None:
+            out.copy_(total)
+            return out
+        return total
+
+    monkeypatch.setattr(kernels, "sum_partials", sum_partials)
+    prof = profile_from_dict(sharded_ffn_profile("m", 2, 4, 2, 2, 8, shard_ranks=[1, 2]))
+    ch = QueueComm.make_channels(3)
+    exs = [LayerExecutor(prof, _cfg(), QueueComm(r, ch)) for r in range(3)]
+    seen, results, errors = [], {}, []
+
+    def go(r):
+        try:
+            h = torch.zeros(2, 1, 4, dtype=torch.bfloat16)
+            h = exs[r].run_stage("embed", lambda x: x, h, mode="decode", seq_len=1)
+            for i in range(2):
+                out = exs[r].run_kernel_group(f"layer_{i}_attn", lambda x: x + 1, h, mode="decode",
+                                              seq_len=1, batch=2)
+                h = out if out is not None else h
+
+                def mlp(x, shard, r=r, i=i):
+                    seen.append((r, i, shard))
+                    return (x.float() * (shard[0] + 1))  # partial of shard k = (k+1) * input
+
+                out = exs[r].run_kernel_group(f"layer_{i}_mlp", mlp, h, mode="decode", seq_len=1, batch=2)
+                h = out if out is not None else h
+            results[r] = exs[r].run_stage("norm_lm_head", lambda x: x, h, mode="decode", seq_len=1, batch=2)
+        except BaseException as exc:  # noqa: BLE001
+            errors.append(exc)
+
+    ts = [threading.Thread(target=go, args=(r,)) for r in range(3)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join(timeout=10)
+    assert not errors and all(not t.is_alive() for t in ts), errors
+    assert sorted(seen) == [(1, 0, (0, 2)), (1, 1, (0, 2)), (2, 0, (1, 2)), (2, 1, (1, 2))]
+    assert results[1] is None and results[2] is None
+    # layer 0: attn 0 -> 1, mlp 1*1 + 2*1 = 3; layer 1: attn 4, mlp 4 + 8 = 12
+    assert torch.equal(results[0], torch.full((2, 1, 4), 12.0, dtype=torch.bfloat16))
