@@ -325,75 +325,119 @@ def run_fgb200(args) -> None:
 
 
 def run_disagg(args) -> None:
-    """Config 2 form: attention (+ embed, head) on rank 0, FFN on rank 1, hidden
-    states handed off over NVLink (P2PComm), M ping-pong micro-batches of
-    `batch` sequences each; every rank replays captured graphs."""
+    """Disaggregated decode over NVLink (P2PComm hand-offs, no NCCL on the data
+    path), every rank replaying captured graphs, M ping-pong micro-batches of
+    `batch` sequences per attention rank:
+      disagg : attention (+ embed, head) on GPU 0, the FFN on GPU 1 (config 2)
+      tp     : attention data-parallel on the first half of the GPUs, each
+               layer's dense FFN tensor-parallel over the second half (config 4)
+      ep     : gpt-oss, attention data-parallel on the first half, the experts
+               split over the second half (config 3)
+    Each attention rank is one pipeline through the FFN ranks; an FFN rank
+    serves every pipeline (its own engines and mailboxes per pipeline and
+    micro-batch)."""
     world, rank, local = dist_env()
     import torch.distributed as dist
     from datetime import timedelta
 
-    assert world == 2, "--mode disagg runs on two GPUs (attention rank 0, FFN rank 1)"
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
     from fluidgpu_b200 import build, kernels
     from fluidgpu_b200.comm import P2PComm
     from fluidgpu_b200.config import EngineConfig
-    from fluidgpu_b200.model import LLAMA3_8B, ModelWeights
+    from fluidgpu_b200.model import GPT_OSS_20B, LLAMA3_8B, ModelWeights
     from fluidgpu_b200.pingpong import PingPongEngine
-    from fluidgpu_b200.profile import attn_ffn_profile, profile_from_dict
+    from fluidgpu_b200.profile import attn_ffn_profile, ffn_shard_of, profile_from_dict, sharded_ffn_profile
 
     build.build()
-    spec = LLAMA3_8B
-    B, ctx, W, K, M = (args.batch or 64), args.context, args.warmup, args.steps, args.micro_batches
+    mode = args.mode
+    if mode == "disagg":
+        assert world == 2, "--mode disagg runs on two GPUs (attention rank 0, FFN rank 1)"
+        attn_ranks, ffn_ranks = [0], [1]
+    else:
+        assert world >= 2 and world % 2 == 0, f"--mode {mode} needs an even number of GPUs"
+        attn_ranks, ffn_ranks = list(range(world // 2)), list(range(world // 2, world))
+    spec = GPT_OSS_20B if mode == "ep" else LLAMA3_8B
+    base_cfg = CONFIG_GPTOSS if mode == "ep" else CONFIG
+    B = args.batch or 64
+    ctx, W, K, M = args.context, args.warmup, args.steps, args.micro_batches
     total = ctx + W + K + 8
-    prof = profile_from_dict(attn_ffn_profile(spec.name, spec.num_layers, spec.hidden, spec.n_kv,
-                                              spec.head_dim, total))
-    cfg = EngineConfig(model_name=spec.name, max_seq_len=total, world_size=2, device=f"cuda:{local}",
-                       max_batch=B, cuda_graph_decode=True)
-    weights = ModelWeights.random(spec, seed=0, device=dev)
-    pp = PingPongEngine(weights, cfg, prof,
-                        lambda m: P2PComm(slot_bytes=B * spec.hidden * 2, nslot=2, tag=m),
-                        micro_batches=M)
-    pp.start(B, prompt_lens=[ctx] * B, reserve_tokens=total)
+
+    # one process group per pipeline: its attention rank is the plan's rank 0
+    # (embed and head there), the FFN ranks follow in order
+    if mode == "disagg":
+        raw = attn_ffn_profile(spec.name, spec.num_layers, spec.hidden, spec.n_kv, spec.head_dim, total)
+    else:
+        raw = sharded_ffn_profile(spec.name, spec.num_layers, spec.hidden, spec.n_kv, spec.head_dim, total,
+                                  shard_ranks=list(range(1, 1 + len(ffn_ranks))), moe=spec.moe)
+    prof = profile_from_dict(raw)
+    groups = {a: dist.new_group([a] + ffn_ranks) for a in attn_ranks}  # collective: every rank, same order
+    mine = [a for a in attn_ranks if rank == a or rank in ffn_ranks]
+    group_rank = 0 if rank in attn_ranks else 1 + ffn_ranks.index(rank)
+    weights = ModelWeights.random(spec, seed=0, device=dev, ffn_shard=ffn_shard_of(prof, group_rank))
+    cfg = EngineConfig(model_name=spec.name, max_seq_len=total, world_size=prof.rank_count,
+                       device=f"cuda:{local}", max_batch=B, cuda_graph_decode=True)
+    slot = max(B * spec.hidden * 4, B * spec.qkv_width * 2)
+    comms = {(a, m): P2PComm(slot_bytes=slot, nslot=2, group=groups[a], tag=m, timeout_ms=10000)
+             for a in mine for m in range(M)}
+    pps = [PingPongEngine(weights, cfg, prof, lambda m, a=a: comms[(a, m)], micro_batches=M) for a in mine]
     g = torch.Generator(device=dev).manual_seed(1)
-    for eng in pp.engines:
-        if eng.kv_cache.pool is not None:
-            eng.kv_cache.pool.normal_(0.0, 1.0, generator=g)
-        eng._tok_dev.copy_(torch.randint(0, spec.vocab, (B,), generator=g, device=dev))
-    for _ in range(W):
-        pp.step()
+    for pp in pps:
+        pp.start(B, prompt_lens=[ctx] * B, reserve_tokens=total)
+        for eng in pp.engines:
+            if eng.kv_cache.pool is not None:
+                eng.kv_cache.pool.normal_(0.0, 1.0, generator=g)
+            eng._tok_dev.copy_(torch.randint(0, spec.vocab, (B,), generator=g, device=dev))
+
+    for pp in pps:
+        pp.capture()
     torch.cuda.synchronize()
-    kernels.check_device("disagg warm-up")
+    dist.barrier()
+
+    def step():
+        for pp in pps:
+            pp.step()
+
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+    kernels.check_device(f"{mode} warm-up")
     dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(K):
-        pp.step()
+        step()
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    kernels.check_device("disagg timed region")
+    kernels.check_device(f"{mode} timed region")
     t = torch.tensor([ms], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t[0])
+    tokens = len(attn_ranks) * M * B * K
     if rank == 0:
+        par = {"disagg": "attention GPU0 / FFN GPU1",
+               "tp": f"attention dp{len(attn_ranks)} / FFN tp{len(ffn_ranks)} (reduce-by-consumer)",
+               "ep": f"attention dp{len(attn_ranks)} / experts ep{len(ffn_ranks)} (reduce-by-consumer)"}[mode]
         line = {
-            "metric": METRIC, "value": M * B * K / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 2,
+            "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {**CONFIG, "batch_per_micro_batch": B, "micro_batches": M,
-                       "parallelism": "attention GPU0 / FFN GPU1, NVLink hand-off, ping-pong"},
-            "mode": "disagg",
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {**base_cfg, "batch_per_micro_batch": B, "micro_batches": M,
+                       "attention_ranks": len(attn_ranks), "ffn_ranks": len(ffn_ranks),
+                       "parallelism": par + ", NVLink hand-offs, ping-pong"},
+            "mode": mode,
         }
         print(json.dumps(line), flush=True)
-    for eng in pp.engines:
-        eng._graphs.clear()
+    for pp in pps:
+        for eng in pp.engines:
+            eng._graphs.clear()
     torch.cuda.synchronize()
     dist.barrier()
-    for eng in pp.engines:
-        eng.comm.close()
+    for c in comms.values():
+        c.close()
     dist.destroy_process_group()
 
 
@@ -408,14 +452,15 @@ def main() -> None:
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch every kernel from the host (no CUDA graph)")
-    ap.add_argument("--mode", default="replicas", choices=["replicas", "disagg"],
-                    help="N>1: independent co-located replicas (default) or attention/FFN disaggregation")
+    ap.add_argument("--mode", default="replicas", choices=["replicas", "disagg", "tp", "ep"],
+                    help="N>1: independent co-located replicas (default); attention/FFN disaggregation "
+                         "(disagg: 2 GPUs; tp: dense FFN tensor-parallel; ep: gpt-oss experts split)")
     ap.add_argument("--micro-batches", type=int, default=2, help="ping-pong micro-batches (disagg)")
     args = ap.parse_args()
     assert args.warmup >= 0 and args.steps > 0
     if args.impl == "reference":
         run_reference(args)
-    elif args.mode == "disagg":
+    elif args.mode in ("disagg", "tp", "ep"):
         run_disagg(args)
     else:
         run_fgb200(args)

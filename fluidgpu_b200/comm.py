@@ -145,7 +145,9 @@ class P2PComm:
              self.world, self.rank, src, self.nslot, self.slot_bytes, self.timeout_ms, self._stream())
 
     def broadcast_tensor(self, t: torch.Tensor, src: int = 0) -> None:
-        self._dist.broadcast(t, src=src, group=self.group)
+        # src is a rank of this comm's group
+        g = src if self.group is None else self._dist.get_global_rank(self.group, src)
+        self._dist.broadcast(t, src=g, group=self.group)
 
     def close(self) -> None:
         from ._lib import call

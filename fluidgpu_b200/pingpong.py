@@ -44,6 +44,13 @@ class PingPongEngine:
         for eng in self.engines:
             eng.start(batch, prompt_lens, reserve_tokens)
 
+    def capture(self) -> None:
+        """Capture every micro-batch's graph for the current length bucket now
+        (ranks capture before any of them replays, so no receive waits on a
+        peer that is still capturing)."""
+        for eng in self.engines:
+            eng.capture(eng.bucket(eng.kv_cache.max_attended()))
+
     @property
     def kv_caches(self):
         return [e.kv_cache for e in self.engines]
