@@ -379,7 +379,9 @@ def run_disagg(args) -> None:
     cfg = EngineConfig(model_name=spec.name, max_seq_len=total, world_size=prof.rank_count,
                        device=f"cuda:{local}", max_batch=B, cuda_graph_decode=True)
     slot = max(B * spec.hidden * 4, B * spec.qkv_width * 2)
-    comms = {(a, m): P2PComm(slot_bytes=slot, nslot=2, group=groups[a], tag=m, timeout_ms=10000)
+    # zero-copy main-path hand-offs where the plan allows them (disagg)
+    comms = {(a, m): P2PComm(slot_bytes=slot, nslot=2, group=groups[a], tag=m, timeout_ms=10000,
+                             direct=mode == "disagg")
              for a in mine for m in range(M)}
     pps = [PingPongEngine(weights, cfg, prof, lambda m, a=a: comms[(a, m)], micro_batches=M) for a in mine]
     g = torch.Generator(device=dev).manual_seed(1)

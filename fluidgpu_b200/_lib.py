@@ -87,6 +87,9 @@ SIGNATURES: dict[str, tuple] = {
     "fg_ipc_close": (c_int, [_P, c_size_t]),
     "fg_handoff_put": (c_int, [_P, c_size_t, _P, _P, c_int, c_int, c_int, c_int, c_size_t, c_int, _P]),
     "fg_handoff_recv": (c_int, [_P, c_size_t, _P, _P, c_int, c_int, c_int, c_int, c_size_t, c_int, _P]),
+    "fg_mailbox_slot": (_P, [_P, c_int, c_int, c_size_t, c_int, c_int]),
+    "fg_handoff_signal": (c_int, [_P, _P, c_int, c_int, c_int, c_size_t, _P]),
+    "fg_handoff_wait": (c_int, [_P, c_int, c_int, c_int, c_size_t, c_int, _P]),
 }
 
 

@@ -69,6 +69,54 @@ class QueueComm:
         return None
 
 
+class _PeerMailbox:
+    """One mailbox per rank in its own HBM (fg_mailbox_bytes geometry), mapped
+    by every peer through CUDA IPC (handles exchanged with all_gather_object)."""
+
+    def __init__(self, dist, group, rank: int, world: int, nslot: int, slot_bytes: int,
+                 device: torch.device) -> None:
+        from . import _lib
+
+        lib = _lib.lib()
+        nbytes = lib.fg_mailbox_bytes(world, nslot, slot_bytes)
+        assert nbytes > 0, f"bad mailbox geometry world={world} nslot={nslot} slot={slot_bytes}"
+        self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        torch.cuda.synchronize(device)
+        handle = ctypes.create_string_buffer(64)
+        off = ctypes.c_size_t(0)
+        _lib.call("fg_ipc_export", self.buf.data_ptr(), handle, ctypes.byref(off))
+        allh: list = [None] * world
+        dist.all_gather_object(allh, (rank, bytes(handle.raw), off.value), group=group)
+        self.peers: dict[int, tuple[int, int]] = {}
+        for r, h, o in allh:
+            if r == rank:
+                continue
+            ptr = ctypes.c_void_p()
+            _lib.call("fg_ipc_import", h, o, ctypes.byref(ptr))
+            self.peers[r] = (ptr.value, o)
+
+    @property
+    def ptr(self) -> int:
+        return self.buf.data_ptr()
+
+    def close(self) -> None:
+        from ._lib import call
+
+        for ptr, off in self.peers.values():
+            call("fg_ipc_close", ptr, off)
+        self.peers.clear()
+
+
+class _DeviceArray:
+    """A CUDA array interface over a raw device pointer (a peer's slot), so
+    torch can wrap it without copying."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], dtype: torch.dtype) -> None:
+        typestr = {torch.bfloat16: "<i2", torch.float16: "<f2", torch.float32: "<f4"}[dtype]  # bf16 as i2, viewed
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
 class P2PComm:
     """Comm backend over NVLink peer memory.
 
@@ -80,13 +128,17 @@ class P2PComm:
     device status) and copies the slot out. Both are ordinary launches on the
     current stream (CUDA-graph capturable). `tag` names an independent channel
     set (one per micro-batch in the ping-pong schedule).
+
+    direct=True adds a second, one-slot mailbox for zero-copy hand-offs of the
+    main path (direct_out / direct_signal on the sender, direct_wait /
+    direct_in on the receiver): the sender's producing kernel writes straight
+    into the peer's slot and the receiver's kernels read it in place
+    (fg_handoff_signal / fg_handoff_wait; the header states when that is safe).
     """
 
     def __init__(self, slot_bytes: int, *, nslot: int = 2, timeout_ms: int = 2000, group=None,
-                 tag: int = 0, device: torch.device | None = None) -> None:
+                 tag: int = 0, device: torch.device | None = None, direct: bool = False) -> None:
         import torch.distributed as dist
-
-        from . import _lib
 
         assert dist.is_available() and dist.is_initialized(), "P2PComm needs torch.distributed"
         self._dist = dist
@@ -98,23 +150,13 @@ class P2PComm:
         self.nslot = nslot
         self.timeout_ms = timeout_ms
         self.tag = tag
-        lib = _lib.lib()
-        nbytes = lib.fg_mailbox_bytes(self.world, nslot, self.slot_bytes)
-        self.mailbox = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
-        torch.cuda.synchronize(self.device)
-        handle = ctypes.create_string_buffer(64)
-        off = ctypes.c_size_t(0)
-        _lib.call("fg_ipc_export", self.mailbox.data_ptr(), handle, ctypes.byref(off))
-        mine = (self.rank, bytes(handle.raw), off.value)
-        allh: list = [None] * self.world
-        dist.all_gather_object(allh, mine, group=group)
-        self.peers: dict[int, tuple[int, int]] = {}
-        for r, h, o in allh:
-            if r == self.rank:
-                continue
-            ptr = ctypes.c_void_p()
-            _lib.call("fg_ipc_import", h, o, ctypes.byref(ptr))
-            self.peers[r] = (ptr.value, o)
+        self._mb = _PeerMailbox(dist, group, self.rank, self.world, nslot, self.slot_bytes, self.device)
+        self.mailbox = self._mb.buf
+        self.peers = self._mb.peers
+        self.direct = bool(direct)
+        self._dmb = (_PeerMailbox(dist, group, self.rank, self.world, 1, self.slot_bytes, self.device)
+                     if direct else None)
+        self._views: dict[tuple, torch.Tensor] = {}
         dist.barrier(group=group)
 
     def get_rank(self) -> int:
@@ -144,15 +186,54 @@ class P2PComm:
         call("fg_handoff_recv", out.data_ptr(), nbytes, self.mailbox.data_ptr(), self.peers[src][0],
              self.world, self.rank, src, self.nslot, self.slot_bytes, self.timeout_ms, self._stream())
 
+    # -- direct (zero-copy) main-path hand-off --------------------------------
+    def _slot_view(self, mailbox_ptr: int, src: int, shape: tuple[int, ...], dtype: torch.dtype) -> torch.Tensor:
+        from . import _lib
+
+        key = (mailbox_ptr, src, tuple(shape), dtype)
+        v = self._views.get(key)
+        if v is None:
+            nbytes = torch.Size(shape).numel() * torch.empty((), dtype=dtype).element_size()
+            assert nbytes <= self.slot_bytes, f"{nbytes} bytes do not fit the {self.slot_bytes}-byte slot"
+            ptr = _lib.lib().fg_mailbox_slot(mailbox_ptr, self.world, 1, self.slot_bytes, src, 0)
+            assert ptr, "fg_mailbox_slot failed"
+            v = torch.as_tensor(_DeviceArray(ptr, shape, dtype), device=self.device)
+            if dtype == torch.bfloat16:
+                v = v.view(torch.bfloat16)
+            self._views[key] = v
+        return v
+
+    def direct_out(self, dst: int, shape: tuple[int, ...], dtype: torch.dtype) -> torch.Tensor:
+        """This rank's slot in dst's direct mailbox (peer memory): write the
+        message there, then direct_signal(dst)."""
+        assert self.direct, "P2PComm(direct=True) is required"
+        return self._slot_view(self._dmb.peers[dst][0], self.rank, shape, dtype)
+
+    def direct_signal(self, dst: int) -> None:
+        from ._lib import call
+
+        call("fg_handoff_signal", self._dmb.ptr, self._dmb.peers[dst][0], self.world, self.rank, dst,
+             self.slot_bytes, self._stream())
+
+    def direct_wait(self, src: int) -> None:
+        from ._lib import call
+
+        call("fg_handoff_wait", self._dmb.ptr, self.world, self.rank, src, self.slot_bytes, self.timeout_ms,
+             self._stream())
+
+    def direct_in(self, src: int, shape: tuple[int, ...], dtype: torch.dtype) -> torch.Tensor:
+        """src's slot in this rank's direct mailbox (read after direct_wait)."""
+        assert self.direct, "P2PComm(direct=True) is required"
+        return self._slot_view(self._dmb.ptr, src, shape, dtype)
+
     def broadcast_tensor(self, t: torch.Tensor, src: int = 0) -> None:
         # src is a rank of this comm's group
         g = src if self.group is None else self._dist.get_global_rank(self.group, src)
         self._dist.broadcast(t, src=g, group=self.group)
 
     def close(self) -> None:
-        from ._lib import call
-
         torch.cuda.synchronize(self.device)
-        for ptr, off in self.peers.values():
-            call("fg_ipc_close", ptr, off)
-        self.peers.clear()
+        self._views.clear()
+        self._mb.close()
+        if self._dmb is not None:
+            self._dmb.close()

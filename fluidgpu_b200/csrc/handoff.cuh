@@ -175,6 +175,35 @@ __global__ void __launch_bounds__(256) recv_kernel(const RecvArgs a) {
   }
 }
 
+// Direct (zero-copy) hand-off on a one-slot mailbox: the producer's own
+// kernel stores its output straight into the peer's slot (a peer pointer from
+// fg_mailbox_slot), then signal_kernel publishes it; the consumer's
+// wait_kernel spins until the flag arrives and later kernels read the slot in
+// place. No slot acks: the channel is only used where the next message from
+// the same sender depends on data the receiver produced after its last read
+// of the slot (strict alternation between two ranks on the main path).
+__global__ void signal_kernel(uint32_t* peer_flag, uint32_t* my_send_seq) {
+  griddep_wait();  // the producer kernel's peer stores are complete
+  griddep_launch_dependents();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const uint32_t seq = *((volatile uint32_t*)my_send_seq) + 1u;
+    *((volatile uint32_t*)my_send_seq) = seq;
+    st_release_sys(peer_flag, seq);
+  }
+}
+
+__global__ void wait_kernel(const uint32_t* my_flag, uint32_t* my_recv_seq, uint64_t timeout_ns) {
+  griddep_wait();
+  griddep_launch_dependents();
+  if (threadIdx.x == 0) {
+    const uint32_t seq = *((volatile uint32_t*)my_recv_seq) + 1u;
+    wait_at_least(my_flag, seq, timeout_ns, 0x403);
+    *((volatile uint32_t*)my_recv_seq) = seq;
+    __threadfence();
+  }
+}
+
 // One CTA per 32 KiB, at most 128: small messages stay on a few SMs (only
 // thread 0 of each CTA spins, so a waiting receive parks little on the SMs),
 // large ones keep enough stores in flight to fill a peer link (~770 GB/s per
@@ -303,6 +332,44 @@ int fg_handoff_recv(void* out, size_t nbytes, void* my_mailbox, void* peer_mailb
   a.timeout_ns = (uint64_t)(timeout_ms > 0 ? timeout_ms : 2000) * 1000000ull;
   return fg::launch_k("fg_handoff_recv", recv_kernel, dim3(copy_grid(a.n16)), dim3(256), 0,
                       (cudaStream_t)stream, a);
+}
+
+void* fg_mailbox_slot(void* mailbox, int world, int nslot, size_t slot_bytes, int src, int slot) {
+  if (!mailbox || world <= 0 || nslot <= 0 || src < 0 || src >= world || slot < 0 || slot >= nslot ||
+      slot_bytes == 0 || slot_bytes % 16)
+    return nullptr;
+  const fg::handoff::Geometry g(world, nslot, slot_bytes);
+  return static_cast<uint8_t*>(mailbox) + g.data + ((size_t)src * nslot + slot) * slot_bytes;
+}
+
+int fg_handoff_signal(void* my_mailbox, void* peer_mailbox, int world, int me, int dst, size_t slot_bytes,
+                      fg_stream_t stream) {
+  using namespace fg::handoff;
+  FG_REQUIRE(my_mailbox && peer_mailbox, "fg_handoff_signal: null pointer");
+  FG_REQUIRE(world > 0 && me >= 0 && me < world && dst >= 0 && dst < world && dst != me,
+             "fg_handoff_signal: bad ranks me=%d dst=%d world=%d", me, dst, world);
+  const Geometry g(world, 1, slot_bytes);
+  uint32_t* peer_flag = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(peer_mailbox) + g.flags) +
+                        (size_t)me * kWordStride;
+  uint32_t* my_send_seq = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(my_mailbox) + g.send_seq) +
+                          (size_t)dst * kWordStride;
+  return fg::launch_k("fg_handoff_signal", signal_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream,
+                      peer_flag, my_send_seq);
+}
+
+int fg_handoff_wait(void* my_mailbox, int world, int me, int src, size_t slot_bytes, int timeout_ms,
+                    fg_stream_t stream) {
+  using namespace fg::handoff;
+  FG_REQUIRE(my_mailbox, "fg_handoff_wait: null pointer");
+  FG_REQUIRE(world > 0 && me >= 0 && me < world && src >= 0 && src < world && src != me,
+             "fg_handoff_wait: bad ranks me=%d src=%d world=%d", me, src, world);
+  const Geometry g(world, 1, slot_bytes);
+  uint8_t* mine = static_cast<uint8_t*>(my_mailbox);
+  const uint32_t* my_flag = reinterpret_cast<const uint32_t*>(mine + g.flags) + (size_t)src * kWordStride;
+  uint32_t* my_recv_seq = reinterpret_cast<uint32_t*>(mine + g.recv_seq) + (size_t)src * kWordStride;
+  const uint64_t timeout_ns = (uint64_t)(timeout_ms > 0 ? timeout_ms : 2000) * 1000000ull;
+  return fg::launch_k("fg_handoff_wait", wait_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream, my_flag,
+                      my_recv_seq, timeout_ns);
 }
 
 }  // extern "C"

@@ -45,6 +45,11 @@ class LayerExecutor:
         self._prefill_buf: torch.Tensor | None = None
         self._wide_bufs: dict[tuple, torch.Tensor] = {}
         self._partial_bufs: dict[tuple, tuple[torch.Tensor, torch.Tensor]] = {}
+        # zero-copy main path (P2PComm(direct=True)): only for plans whose main
+        # path alternates strictly between ranks at coarse task boundaries, so
+        # a received slot is never read after this rank has sent the value on
+        self._direct = bool(getattr(comm_backend, "direct", False)) and _direct_safe(profile)
+        self._accepts_out: dict[Any, bool] = {}
         if cfg.preallocate_recv_buffers:
             self._decode_bufs[cfg.max_batch] = torch.empty(
                 (cfg.max_batch, 1, profile.hidden_size), dtype=cfg.dtype, device=self.device)
@@ -98,12 +103,30 @@ class LayerExecutor:
             value = self._recv_partials(prev.shard_ranks, mode=mode, batch=b,
                                         seq_len=self._seq_len(value, seq_len))
         elif prev is not None and prev.rank_for(mode) != self.my_rank:
-            value = self._recv(mode=mode, batch=b, seq_len=self._seq_len(value, seq_len),
-                               src=prev.rank_for(mode), width=recv_width)
+            sl = self._seq_len(value, seq_len)
+            if self._direct and mode == "decode" and recv_width is None:
+                # zero-copy: wait for the sender's flag and read its slot in place
+                src = prev.rank_for(mode)
+                self._comm.direct_wait(src)
+                value = self._comm.direct_in(src, (b, sl, self.profile.hidden_size), self.cfg.dtype)
+            else:
+                value = self._recv(mode=mode, batch=b, seq_len=sl, src=prev.rank_for(mode), width=recv_width)
         assert value is not None, f"rank {self.my_rank} entered {task_name} without input"
+        nxt = self.tasks[idx + 1] if idx < len(self.tasks) - 1 else None
+        direct_dst = None
+        if (self._direct and mode == "decode" and nxt is not None and nxt.shard_ranks is None
+                and nxt.rank_for(mode) != self.my_rank):
+            assert self._takes_out(fn), f"{task_name}: a direct hand-off needs a kernel group that takes out="
+            # zero-copy: the group's last kernel writes straight into the peer's slot
+            direct_dst = nxt.rank_for(mode)
+            kwargs["out"] = self._comm.direct_out(direct_dst, (b, self._seq_len(value, seq_len),
+                                                               self.profile.hidden_size), self.cfg.dtype)
         with trace_region(kind="compute", name=task_name, device=self.device, mode=mode):
             out = _first_tensor(fn(value, **kwargs))
-        nxt = self.tasks[idx + 1] if idx < len(self.tasks) - 1 else None
+        if direct_dst is not None:
+            assert out.data_ptr() == kwargs["out"].data_ptr(), f"{task_name} did not write its output in place"
+            self._comm.direct_signal(direct_dst)
+            return out
         if nxt is not None:
             if not out.is_contiguous():
                 out = out.contiguous()
@@ -113,6 +136,19 @@ class LayerExecutor:
             elif nxt.rank_for(mode) != self.my_rank:
                 self._comm.send_tensor(out, dst=nxt.rank_for(mode))
         return out
+
+    def _takes_out(self, fn: Callable[..., Any]) -> bool:
+        key = getattr(fn, "__func__", fn)
+        ok = self._accepts_out.get(key)
+        if ok is None:
+            import inspect
+
+            try:
+                ok = "out" in inspect.signature(fn).parameters
+            except (TypeError, ValueError):
+                ok = False
+            self._accepts_out[key] = ok
+        return ok
 
     def _recv(self, *, mode: str, batch: int, seq_len: int, src: int, width: int | None = None) -> torch.Tensor:
         buf = self._recv_buffer(mode=mode, batch=batch, seq_len=seq_len, width=width)
@@ -170,6 +206,29 @@ class LayerExecutor:
             return int(value.shape[1])
         assert seq_len is not None, "seq_len is required when receiving into an empty value"
         return seq_len
+
+
+def _direct_safe(profile: RuntimeProfile) -> bool:
+    """The zero-copy hand-off needs a main path that alternates between ranks
+    only at coarse attention / FFN boundaries, with no fine-grained split (aux
+    tensors), no sharded group and no phase-dependent rank; MoE groups must
+    share a rank."""
+    from .profile import parse_layer_task
+
+    for t in profile.tasks:
+        if t.shard_ranks is not None or t.decode_rank is not None:
+            return False
+        p = parse_layer_task(t.name)
+        if p is not None and p[1] not in ("attn", "mlp", "moe_router", "moe_experts", "moe_combine"):
+            return False
+    by_name = profile.task_by_name
+    for t in profile.tasks:
+        p = parse_layer_task(t.name)
+        if p is not None and p[1] == "moe_router":
+            ranks = {by_name[f"layer_{p[0]}_{s}"].rank for s in ("moe_router", "moe_experts", "moe_combine")}
+            if len(ranks) != 1:
+                return False
+    return True
 
 
 def _first_tensor(value: Any) -> torch.Tensor:

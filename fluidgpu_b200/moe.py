@@ -229,8 +229,9 @@ def experts_forward(x: torch.Tensor, idx: torch.Tensor, weights: torch.Tensor, W
     return out
 
 
-def residual_add(residual: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
-    out = torch.empty_like(residual)
+def residual_add(residual: torch.Tensor, y: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty_like(residual)
     call("fg_add_bf16", residual.data_ptr(), y.data_ptr(), out.data_ptr(), residual.numel(),
          kernels._stream(residual.device))
     return out

@@ -177,11 +177,16 @@ class FluidRunner:
         return hidden
 
     # -- kernel groups (override points of the reference runner) ---------------
-    def _embed(self, tokens: torch.Tensor) -> torch.Tensor:
+    # `out`: where the group's result must land (the next rank's slot of a
+    # zero-copy hand-off); the group's last kernel writes there directly
+    def _embed(self, tokens: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         B = tokens.shape[0]
-        return kernels.embed(tokens.reshape(-1).contiguous(), self.weights.embed).view(B, 1, -1)
+        o = kernels.embed(tokens.reshape(-1).contiguous(), self.weights.embed,
+                          out=None if out is None else out.view(B, -1))
+        return o.view(B, 1, -1) if out is None else out
 
-    def _run_attn(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+    def _run_attn(self, hidden: torch.Tensor, *, layer: int, out: torch.Tensor | None = None,
+                  **_: Any) -> torch.Tensor:
         s = self.spec
         W = self.weights.layers[layer]
         kv = self.kv_cache
@@ -196,9 +201,9 @@ class FluidRunner:
         a = kernels.paged_decode_attn(q, kp, vp, bt, kv.seq_lens[:B], kv.plan_len(),
                                       window=s.window(layer), sinks=W.get("sinks"),
                                       slot=self.slot + ".attn")
-        out = kernels.gemm(a, W["wo"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h, bias=W.get("bo"),
-                           slot=self.slot + ".gemm")
-        return out.view(B, 1, s.hidden)
+        o = kernels.gemm(a, W["wo"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h, bias=W.get("bo"),
+                         out=None if out is None else out.view(B, s.hidden), slot=self.slot + ".gemm")
+        return o.view(B, 1, s.hidden) if out is None else out
 
     # fine attention groups (runner.py:256-347)
     def _run_attn_qkv(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
@@ -265,7 +270,7 @@ class FluidRunner:
         return st
 
     def _run_mlp(self, hidden: torch.Tensor, *, layer: int, shard: tuple[int, int] | None = None,
-                 **_: Any) -> torch.Tensor:
+                 out: torch.Tensor | None = None, **_: Any) -> torch.Tensor:
         s = self.spec
         W = self.weights.layers[layer]
         B = hidden.shape[0]
@@ -280,9 +285,9 @@ class FluidRunner:
             out = kernels.gemm(act, W["w_down"], epilogue=_lib.FG_EPI_F32,
                                residual=h if shard[0] == 0 else None, slot=self.slot + ".gemm")
             return out.view(B, 1, s.hidden)
-        out = kernels.gemm(act, W["w_down"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h,
-                           slot=self.slot + ".gemm")
-        return out.view(B, 1, s.hidden)
+        o = kernels.gemm(act, W["w_down"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h,
+                         out=None if out is None else out.view(B, s.hidden), slot=self.slot + ".gemm")
+        return o.view(B, 1, s.hidden) if out is None else out
 
     # fine dense FFN groups (runner.py:416-430)
     def _run_mlp_gate_up(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
@@ -356,23 +361,29 @@ class FluidRunner:
             st["residual"] = self._recv_aux((B, s.hidden), torch.bfloat16, src)
             if self.record_routing:
                 self.last_routing[layer] = st["indices"]
-        # the combine group's residual add is fused when it runs here too
-        fuse = self._rank_of(layer, "moe_combine") == self.executor.my_rank
+        # the combine group's residual add is fused when it runs here too (not
+        # under zero-copy hand-offs, where the combine writes the peer's slot)
+        fuse = (self._rank_of(layer, "moe_combine") == self.executor.my_rank
+                and not getattr(self.executor, "_direct", False))
         y = moe.experts_forward(hidden.reshape(B, s.hidden), st["indices"], st["weights"],
                                 self.weights.layers[layer], s,
                                 residual=st["residual"] if fuse else None)
         st["fused"] = fuse
         return y.view(B, 1, s.hidden)
 
-    def _run_moe_combine(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+    def _run_moe_combine(self, hidden: torch.Tensor, *, layer: int, out: torch.Tensor | None = None,
+                         **_: Any) -> torch.Tensor:
         from . import moe
 
         B = hidden.shape[0]
         self._ensure_residual(self._moe_states, layer, B, src=self._rank_of(layer, "moe_experts"))
         st = self._moe_states.pop(layer)
         if st.get("fused"):
+            assert out is None, "a fused combine has no output of its own to place"
             return hidden
-        return moe.residual_add(st["residual"], hidden.reshape(B, -1)).view(B, 1, -1)
+        o = moe.residual_add(st["residual"], hidden.reshape(B, -1),
+                             out=None if out is None else out.view(B, -1))
+        return o.view(B, 1, -1) if out is None else out
 
     def _after_moe_router(self, layer: int) -> None:
         shards = self._shards_of(layer, "moe_experts")

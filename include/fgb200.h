@@ -285,6 +285,23 @@ int fg_handoff_put(const void* src, size_t nbytes, void* my_mailbox, void* peer_
 int fg_handoff_recv(void* out, size_t nbytes, void* my_mailbox, void* peer_mailbox, int world,
                     int me, int src, int nslot, size_t slot_bytes, int timeout_ms, fg_stream_t stream);
 
+/* Direct (zero-copy) hand-off on a mailbox made with nslot = 1. The sender
+ * stores its tensor straight into its slot in the receiver's mailbox (the
+ * address fg_mailbox_slot gives for the peer's mailbox, src = sender) from
+ * its own producing kernel, then fg_handoff_signal publishes it (sequence
+ * number, system-scope release); the receiver's fg_handoff_wait spins
+ * (bounded by timeout_ms, device status 2 on expiry) until it arrives, and
+ * the receiver's kernels then read the slot in place. No acks: valid only
+ * where the sender's next message on the channel depends on data the
+ * receiver produced after its last read of the slot (strict alternation of
+ * the main path between two ranks). No counterpart in the reference (its
+ * send/recv copy through NCCL buffers). */
+void* fg_mailbox_slot(void* mailbox, int world, int nslot, size_t slot_bytes, int src, int slot);
+int fg_handoff_signal(void* my_mailbox, void* peer_mailbox, int world, int me, int dst, size_t slot_bytes,
+                      fg_stream_t stream);
+int fg_handoff_wait(void* my_mailbox, int world, int me, int src, size_t slot_bytes, int timeout_ms,
+                    fg_stream_t stream);
+
 /* positions[b] += 1 and seq_lens[b] += 1 after a decode step
  * (LayerKVCache.advance, kv_cache.py:140-144). Either pointer may be NULL. */
 int fg_advance(int32_t* positions, int32_t* seq_lens, int B, fg_stream_t stream);

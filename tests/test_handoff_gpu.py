@@ -203,8 +203,56 @@ def _sharded(rank, comm):
         out = ref.runner.decode_step(logits[s].argmax(-1).cuda())
 
 
+def _direct_graphed(rank, comm):
+    """Zero-copy hand-offs (the o_proj / down GEMM writes the peer's slot, the
+    peer reads it in place), replayed from per-rank CUDA graphs: greedy tokens
+    and logits equal a co-located run bit for bit."""
+    from transformers.models.llama import LlamaConfig, LlamaForCausalLM
+
+    from fluidgpu_b200.config import EngineConfig
+    from fluidgpu_b200.engine import DecodeEngine
+    from fluidgpu_b200.model import ModelWeights
+    from fluidgpu_b200.profile import profile_from_dict
+
+    assert comm.direct
+    torch.manual_seed(0)
+    cfg = LlamaConfig(num_hidden_layers=3, vocab_size=2048, hidden_size=512, intermediate_size=1024,
+                      num_attention_heads=8, num_key_value_heads=2, max_position_embeddings=256)
+    model = LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+    B, prompt, steps = 4, 10, 8
+    ecfg = EngineConfig(model_name="disagg", max_seq_len=64, world_size=2, device=f"cuda:{rank}",
+                        max_batch=B, cuda_graph_decode=True)
+    eng = DecodeEngine(ModelWeights.from_hf(model, f"cuda:{rank}"), ecfg, profile=profile_from_dict(_attn_ffn_plan()),
+                       comm=comm)
+    assert eng.executor._direct
+    g = torch.Generator().manual_seed(1)
+    prompts = torch.randint(0, 2048, (B, prompt), generator=g)
+    eng.start(B, reserve_tokens=prompt + steps + 2)
+    out = eng.runner.prefill(prompts.cuda())  # eager steps through the direct channel
+    tok = out.reshape(B, -1).float().argmax(-1).cpu() if rank == 0 else torch.zeros(B, dtype=torch.int64)
+    toks = []
+    for _ in range(steps):  # graphed steps
+        nxt = eng.step(tok)
+        if rank == 0:
+            toks.append(nxt)
+            tok = nxt
+    torch.cuda.synchronize()
+    if rank != 0:
+        return
+    ref = DecodeEngine(ModelWeights.from_hf(model, "cuda:0"),
+                       EngineConfig(model_name="colo", max_seq_len=64, world_size=1, device="cuda:0",
+                                    max_batch=B, cuda_graph_decode=True))
+    ref.start(B, reserve_tokens=prompt + steps + 2)
+    out = ref.runner.prefill(prompts.cuda())
+    tok = out.reshape(B, -1).float().argmax(-1).cpu()
+    for s in range(steps):
+        tok = ref.step(tok)
+        assert torch.equal(tok, toks[s]), f"step {s}: direct hand-off tokens differ"
+
+
 CASES = {"roundtrip": _roundtrip, "graphed": _graphed, "disaggregated": _disaggregated,
-         "fine_split": lambda rank, comm: _disaggregated(rank, comm, _fine_plan), "sharded": _sharded}
+         "fine_split": lambda rank, comm: _disaggregated(rank, comm, _fine_plan), "sharded": _sharded,
+         "direct": _disaggregated, "direct_graphed": _direct_graphed}
 
 
 def _worker(rank, world, port, case, q):
@@ -219,7 +267,7 @@ def _worker(rank, world, port, case, q):
         from fluidgpu_b200.comm import P2PComm
 
         build.build()
-        comm = P2PComm(slot_bytes=1 << 20, nslot=2, timeout_ms=5000)
+        comm = P2PComm(slot_bytes=1 << 20, nslot=2, timeout_ms=5000, direct=case.startswith("direct"))
         CASES[case](rank, comm)
         torch.cuda.synchronize()
         kernels.check_device(f"{case} rank {rank}")
