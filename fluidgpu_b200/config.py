@@ -39,6 +39,9 @@ class EngineConfig:
     nccl_ib_gid_index: int | None = None
     max_batch: int = 1
     block_size: int = 16
+    # paged-KV block allocation: "vllm" (vLLM BlockPool order, blocks added as
+    # sequences grow) or "reserve" (each sequence's expected length up front)
+    kv_allocation: str = "vllm"
 
     def __post_init__(self) -> None:
         assert self.dtype is torch.bfloat16, f"dtype must be torch.bfloat16, got {self.dtype}"
@@ -50,6 +53,7 @@ class EngineConfig:
         )
         assert self.max_batch >= 1, f"max_batch must be >= 1, got {self.max_batch}"
         assert self.block_size == 16, f"block_size must be 16, got {self.block_size}"
+        assert self.kv_allocation in ("vllm", "reserve"), f"bad kv_allocation {self.kv_allocation}"
         if self.rank_override is not None:
             assert 0 <= self.rank_override < self.world_size, (
                 f"rank_override must be in [0, {self.world_size}), got {self.rank_override}"

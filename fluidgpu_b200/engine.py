@@ -105,6 +105,7 @@ class DecodeEngine:
     def replay(self) -> torch.Tensor:
         """One graphed decode step from the static token buffer; returns the
         static next-token buffer (also the next replay's input)."""
+        self.kv_cache.prepare_step(1)  # block-table entries the step needs (before any capture)
         g = self.capture(self.bucket(self.kv_cache.max_attended()))
         g.replay()
         self.kv_cache.host_advance(1)

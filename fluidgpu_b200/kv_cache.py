@@ -14,9 +14,16 @@ Device-side per-sequence counters:
 Both advance on the device (fg_advance), so a decode step needs no host
 round trip; a host mirror tracks the same counts for planning.
 
-Blocks come from a FIFO free list (lowest id first, freed blocks return to
-the tail), and a sequence reserves the pages for its whole expected length
-up front, so the block table is written only when requests join.
+Block allocation (allocation="vllm", the default) follows vLLM's BlockPool
+(vllm/v1/core/block_pool.py, the allocator behind the reference's vLLM
+integration): block 0 is the reserved null block, free blocks form a FIFO
+queue (lowest id first), a sequence gets the blocks its prompt needs when the
+batch starts and one more block whenever a step would run past its last one
+(prepare_step, sequences in batch order), and a finished sequence returns its
+blocks tail-first. The block tables therefore equal vLLM's for the same
+requests (tests/test_block_table_vllm.py runs vLLM's own BlockPool beside
+it). allocation="reserve" instead reserves each sequence's whole expected
+length up front (lowest ids first, no null block).
 """
 from __future__ import annotations
 
@@ -31,11 +38,12 @@ BLOCK = 16
 
 
 class BlockAllocator:
-    """FIFO free-list of physical block ids (deterministic)."""
+    """FIFO free-list of physical block ids (deterministic). With null_block,
+    block 0 is never handed out (vLLM's placeholder block)."""
 
-    def __init__(self, num_blocks: int) -> None:
+    def __init__(self, num_blocks: int, null_block: bool = False) -> None:
         self.num_blocks = num_blocks
-        self._free = collections.deque(range(num_blocks))
+        self._free = collections.deque(range(1 if null_block else 0, num_blocks))
 
     @property
     def num_free(self) -> int:
@@ -53,8 +61,10 @@ class PagedKVCache:
     def __init__(self, num_layers: int, owned_layer_ids: list[int] | tuple[int, ...],
                  max_seq_len: int, num_kv_heads: int, head_dim: int, dtype: torch.dtype,
                  device: torch.device | str, *, max_batch: int = 1,
-                 num_blocks: int | None = None) -> None:
+                 num_blocks: int | None = None, allocation: str = "vllm") -> None:
         assert dtype is torch.bfloat16, "the paged cache holds bf16"
+        assert allocation in ("vllm", "reserve"), f"unknown allocation policy {allocation}"
+        self.allocation = allocation
         self.num_layers = num_layers
         self.owned = set(owned_layer_ids)
         self.max_seq_len = max_seq_len
@@ -64,7 +74,8 @@ class PagedKVCache:
         self.device = torch.device(device)
         self.max_batch = max_batch
         self.max_blocks = (max_seq_len + BLOCK - 1) // BLOCK
-        self.num_blocks = num_blocks if num_blocks is not None else max_batch * self.max_blocks
+        null = allocation == "vllm"
+        self.num_blocks = num_blocks if num_blocks is not None else max_batch * self.max_blocks + int(null)
         self.static_mode = False
         self._slot = {lid: i for i, lid in enumerate(sorted(self.owned))}
         n_owned = len(self._slot)
@@ -72,9 +83,15 @@ class PagedKVCache:
                                 dtype=dtype, device=self.device) if n_owned else None
         self.block_table = torch.full((max_batch, self.max_blocks), -1, dtype=torch.int32,
                                       device=self.device)
+        # host mirror of the block table (pinned), copied to the device in one
+        # asynchronous copy when a step adds blocks; entries only grow until
+        # the next batch, so a copy that runs late still holds every entry
+        # the kernels before it read
+        self._bt_host = torch.full((max_batch, self.max_blocks), -1, dtype=torch.int32,
+                                   pin_memory=self.device.type == "cuda")
         self.positions = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
         self.seq_lens = torch.ones(max_batch, dtype=torch.int32, device=self.device)
-        self.allocator = BlockAllocator(self.num_blocks)
+        self.allocator = BlockAllocator(self.num_blocks, null_block=null)
         self._blocks: list[list[int]] = [[] for _ in range(max_batch)]
         self._host_pos = [0] * max_batch
         self.batch = 0
@@ -103,9 +120,12 @@ class PagedKVCache:
         for b in range(B):
             total = max(res[b], lengths[b] + 1)
             assert total <= self.max_seq_len, f"exceed max_seq_len: {total} > {self.max_seq_len}"
+            if self.allocation == "vllm":
+                total = lengths[b]  # the prompt's blocks; the rest come step by step
             nb = (total + BLOCK - 1) // BLOCK
             self._blocks[b] = self.allocator.allocate(nb)
             table[b, :nb] = torch.tensor(self._blocks[b], dtype=torch.int32)
+        self._bt_host.copy_(table)
         self.block_table.copy_(table)
         pos = torch.zeros(self.max_batch, dtype=torch.int32)
         pos[:B] = torch.tensor(lengths, dtype=torch.int32)
@@ -113,6 +133,27 @@ class PagedKVCache:
         self.seq_lens.copy_(pos + 1)
         self._host_pos = list(lengths) + [0] * (self.max_batch - B)
         self.batch = B
+
+    def prepare_step(self, n: int = 1) -> None:
+        """Give every sequence the blocks its next n tokens need (vLLM order:
+        sequences in batch order, one FIFO allocation each), writing the new
+        block-table entries on the current stream. Not while a CUDA graph is
+        being captured (the graph must not hold these host copies)."""
+        if self.allocation != "vllm" or (self.block_table.is_cuda and torch.cuda.is_current_stream_capturing()):
+            return
+        dirty = False
+        for b in range(self.batch):
+            need = (self._host_pos[b] + n + BLOCK - 1) // BLOCK
+            have = len(self._blocks[b])
+            if need > have:
+                assert need <= self.max_blocks, f"exceed max_seq_len: {self._host_pos[b] + n}"
+                new = self.allocator.allocate(need - have)
+                self._blocks[b].extend(new)
+                for j, blk in enumerate(new):
+                    self._bt_host[b, have + j] = blk
+                dirty = True
+        if dirty:
+            self.block_table.copy_(self._bt_host, non_blocking=True)
 
     # -- LayerKVCache surface --------------------------------------------------
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
@@ -127,6 +168,7 @@ class PagedKVCache:
         assert hd == self.head_dim, f"head_dim mismatch: got {hd}, expected {self.head_dim}"
         if B > self.batch:
             self.start_batch([0] * B, self.max_seq_len)
+        self.prepare_step(S)
         cp = None if cache_kwargs is None else cache_kwargs.get("cache_position")
         if cp is not None and B == 1:
             pos = cp.flatten().to(device=self.device, dtype=torch.int32)
@@ -205,10 +247,14 @@ class PagedKVCache:
     def reset(self) -> None:
         for b in range(self.max_batch):
             if self._blocks[b]:
-                self.allocator.free(self._blocks[b])
+                # vLLM frees a finished request's blocks tail-first
+                self.allocator.free(self._blocks[b][::-1] if self.allocation == "vllm" else self._blocks[b])
                 self._blocks[b] = []
         self._host_pos = [0] * self.max_batch
         self.batch = 0
+        if self.block_table.is_cuda:  # a pending table copy may still read the host mirror
+            torch.cuda.current_stream(self.device).synchronize()
+        self._bt_host.fill_(-1)
         if self.positions.is_cuda:
             self.positions.zero_()
             self.seq_lens.fill_(1)

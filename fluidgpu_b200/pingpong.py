@@ -49,6 +49,7 @@ class PingPongEngine:
         (ranks capture before any of them replays, so no receive waits on a
         peer that is still capturing)."""
         for eng in self.engines:
+            eng.kv_cache.prepare_step(1)
             eng.capture(eng.bucket(eng.kv_cache.max_attended()))
 
     @property

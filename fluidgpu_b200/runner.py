@@ -71,7 +71,8 @@ class FluidRunner:
         self.kv_cache = PagedKVCache(
             num_layers=self.spec.num_layers, owned_layer_ids=owned_layer_ids,
             max_seq_len=cfg.max_seq_len, num_kv_heads=self.spec.n_kv, head_dim=self.spec.head_dim,
-            dtype=cfg.dtype, device=self.device, max_batch=cfg.max_batch, num_blocks=num_blocks)
+            dtype=cfg.dtype, device=self.device, max_batch=cfg.max_batch, num_blocks=num_blocks,
+            allocation=cfg.kv_allocation)
         self._moe_states: dict[int, dict[str, torch.Tensor]] = {}
         self._attn_states: dict[int, dict[str, torch.Tensor]] = {}
         self._mlp_states: dict[int, dict[str, torch.Tensor]] = {}
@@ -120,6 +121,7 @@ class FluidRunner:
     def _step(self, tokens: torch.Tensor, *, want_logits: bool) -> torch.Tensor | None:
         B = tokens.shape[0]
         ex = self.executor
+        self.kv_cache.prepare_step(1)  # blocks for this step's token (no-op inside a graph capture)
         hidden = ex.run_stage("embed", self._embed, tokens, mode="decode", seq_len=1, batch=B)
         for i in self.layers:
             hidden = self._run_attention_tasks(i, hidden, B)
