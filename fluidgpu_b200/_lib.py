@@ -51,6 +51,15 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [_P, _P, _P, c_float, _P, c_int, c_int, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P],
     ),
+    "fg_rope_kv_append_tokens": (
+        c_int,
+        [_P, _P, _P, _P, c_float, _P, c_int, c_int, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P],
+    ),
+    "fg_prefill_attn": (
+        c_int,
+        [_P, _P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+         c_float, _P],
+    ),
     "fg_kv_append": (
         c_int, [_P, _P, _P, _P, _P, c_int, c_int, _P, _P, c_int, c_int, c_int, c_int, _P],
     ),

@@ -438,6 +438,240 @@ int launch(const Params& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaSt
                   st, p, HD);
 }
 
+// ---------------------------------------------------------------------------
+// Prefill (many query positions per sequence), causal, from the paged cache.
+//
+// Queries: q [B*S][nq][hd] for S consecutive positions per sequence starting
+// at p0[b] (tokens of one sequence contiguous); their K/V are already in the
+// pages (fg_rope_kv_append_tokens), together with any context cached before
+// p0[b]. CTA = (block of 64/G positions, kv head g, sequence b); its 64 MMA
+// rows are (position j, head g*G + h) pairs, 16 per consumer warp. The
+// producer streams the pages the block can see (causal, window) through the
+// same TMA ring as decode; every consumer warp reads every page (its own
+// rows), so a page's K/V feed all G heads and all the block's positions.
+// Row r attends key k iff k <= pos(r) and (window == 0 or k > pos(r) - window);
+// sinks join each head's denominator. Output o [B*S][nq][hd] bf16.
+struct PrefillParams {
+  const __nv_bfloat16* q;
+  const int32_t* block_table;
+  const int32_t* p0;        // [B] position of each sequence's first query
+  const float* sinks;       // [nq] or null
+  __nv_bfloat16* out;
+  int B, S, nq, nkv, G, QP; // QP = 64 / G positions per CTA
+  int max_blocks, num_blocks;
+  int window;
+  float scale_log2;
+};
+
+template <int HD, int STAGES>
+__global__ void __launch_bounds__(kThreads) prefill_attn_kernel(
+    const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+    const PrefillParams p) {
+  using L = Layout<HD, STAGES>;
+  constexpr int KT = HD / 16;
+  constexpr int ND = HD / 8;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int G = p.G, QP = p.QP;
+  griddep_wait();  // q and the pages come from earlier kernels
+  if (threadIdx.x == 0) griddep_launch_dependents();
+
+  const int base = p.p0[b];
+  const int j0 = qb * QP;                       // first position offset of the block
+  const int jn = min(QP, p.S - j0);             // positions in this block
+  if (jn <= 0) return;
+  const int qlo = base + j0, qhi = base + j0 + jn - 1;  // query positions
+  const int klo = p.window > 0 ? max(0, qlo - p.window + 1) : 0;
+  const int pbeg = klo / kBlock, pend = qhi / kBlock + 1;
+  const int npages = pend - pbeg;
+
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar_full = sbase + L::BAR_OFFSET;
+  const uint32_t bar_empty = bar_full + STAGES * 8;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, kConsumers);  // every consumer warp reads every page
+    }
+    fence_mbar_init();
+    prefetch_tensormap(&tm_k);
+    prefetch_tensormap(&tm_v);
+  }
+  __syncthreads();
+
+  if (warp == kConsumers) {
+    if (lane == 0) {
+      const int32_t* bt = p.block_table + (int64_t)b * p.max_blocks;
+      const uint64_t pol = l2_policy_evict_last();  // pages are re-read by the other query blocks
+      int issued = 0;
+      for (int i = 0; i < npages; ++i) {
+        const int s = i % STAGES;
+        if (!mbar_wait(bar_empty + 8 * s, ((uint32_t)(i / STAGES) & 1u) ^ 1u, 0x211)) break;
+        const int page = pbeg + i;
+        int blk = page < p.max_blocks ? bt[page] : -1;
+        if (blk < 0 || blk >= p.num_blocks) {
+          record_device_error(DEV_BAD_INDEX, 0x212);
+          blk = 0;
+        }
+        const int row = (blk * p.nkv + g) * kBlock;
+        const uint32_t st = sbase + s * L::STAGE_BYTES;
+        mbar_arrive_expect_tx(bar_full + 8 * s, L::STAGE_BYTES);
+#pragma unroll
+        for (int bx = 0; bx < L::BOXES; ++bx) {
+          tma_load_2d_hint(st + bx * 2048, &tm_k, bar_full + 8 * s, bx * 64, row, pol);
+          tma_load_2d_hint(st + L::TILE_BYTES + bx * 2048, &tm_v, bar_full + 8 * s, bx * 64, row, pol);
+        }
+        ++issued;
+      }
+      if (issued < npages) {
+        for (int s = 0; s < STAGES && s < issued; ++s) {
+          const int last = s + ((issued - 1 - s) / STAGES) * STAGES;
+          mbar_wait(bar_full + 8 * s, (uint32_t)(last / STAGES) & 1u, 0x214);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers: warp w owns rows 16w .. 16w+15 ----------------
+  const int r0 = warp * 16 + (lane >> 2), r1 = r0 + 8;
+  const int jr0 = r0 / G, jr1 = r1 / G;           // position offsets within the block
+  const int hr0 = g * G + r0 % G, hr1 = g * G + r1 % G;
+  const bool ok0 = jr0 < jn, ok1 = jr1 < jn;
+  const int pos0 = qlo + jr0, pos1 = qlo + jr1;
+  uint32_t qf[KT][4];
+  {
+    const int c = (lane & 3) * 2;
+    const uint32_t* q0 = reinterpret_cast<const uint32_t*>(
+        p.q + (((int64_t)b * p.S + j0 + jr0) * p.nq + hr0) * HD);
+    const uint32_t* q1 = reinterpret_cast<const uint32_t*>(
+        p.q + (((int64_t)b * p.S + j0 + jr1) * p.nq + hr1) * HD);
+#pragma unroll
+    for (int kt = 0; kt < KT; ++kt) {
+      qf[kt][0] = ok0 ? q0[(kt * 16 + c) >> 1] : 0u;
+      qf[kt][1] = ok1 ? q1[(kt * 16 + c) >> 1] : 0u;
+      qf[kt][2] = ok0 ? q0[(kt * 16 + 8 + c) >> 1] : 0u;
+      qf[kt][3] = ok1 ? q1[(kt * 16 + 8 + c) >> 1] : 0u;
+    }
+  }
+  float o[ND][4];
+#pragma unroll
+  for (int i = 0; i < ND; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = kNegBig, m1 = kNegBig, l0 = 0.f, l1 = 0.f;
+  const int k_tok = ((lane >> 4) << 3) + (lane & 7);
+  const int k_sub = (lane >> 3) & 1;
+  const int v_tok = (((lane >> 3) & 1) << 3) + (lane & 7);
+  const int v_sub = lane >> 4;
+  const int lo0 = p.window > 0 ? pos0 - p.window + 1 : 0, lo1 = p.window > 0 ? pos1 - p.window + 1 : 0;
+
+  for (int i = 0; i < npages; ++i) {
+    const int s = i % STAGES;
+    if (!__all_sync(0xffffffffu, mbar_wait(bar_full + 8 * s, (uint32_t)(i / STAGES) & 1u, 0x213))) break;
+    const uint32_t kbase = sbase + s * L::STAGE_BYTES;
+    const uint32_t vbase = kbase + L::TILE_BYTES;
+    float sc[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+    for (int kt = 0; kt < KT; ++kt) {
+      uint32_t kb[4];
+      ldsm_x4(kb, tile_addr(kbase, k_tok, kt * 2 + k_sub));
+      mma_bf16(sc[0], qf[kt], kb[0], kb[1]);
+      mma_bf16(sc[1], qf[kt], kb[2], kb[3]);
+    }
+    const int tok0 = (pbeg + i) * kBlock + (lane & 3) * 2;
+    float mx0 = kNegBig, mx1 = kNegBig;
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = tok0 + n * 8 + (e & 1);
+        const bool valid = e < 2 ? (ok0 && t <= pos0 && t >= lo0) : (ok1 && t <= pos1 && t >= lo1);
+        sc[n][e] = valid ? sc[n][e] * p.scale_log2 : kNegBig;
+      }
+      mx0 = fmaxf(mx0, fmaxf(sc[n][0], sc[n][1]));
+      mx1 = fmaxf(mx1, fmaxf(sc[n][2], sc[n][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float a0 = exp2f(m0 - mn0), a1 = exp2f(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    // masked keys contribute nothing, also while a row has no valid key yet
+    // (a sliding window starts later for the block's later positions)
+    float ps[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      ps[n][0] = sc[n][0] > 0.5f * kNegBig ? exp2f(sc[n][0] - mn0) : 0.f;
+      ps[n][1] = sc[n][1] > 0.5f * kNegBig ? exp2f(sc[n][1] - mn0) : 0.f;
+      ps[n][2] = sc[n][2] > 0.5f * kNegBig ? exp2f(sc[n][2] - mn1) : 0.f;
+      ps[n][3] = sc[n][3] > 0.5f * kNegBig ? exp2f(sc[n][3] - mn1) : 0.f;
+    }
+    l0 = l0 * a0 + ps[0][0] + ps[0][1] + ps[1][0] + ps[1][1];
+    l1 = l1 * a1 + ps[0][2] + ps[0][3] + ps[1][2] + ps[1][3];
+#pragma unroll
+    for (int nd = 0; nd < ND; ++nd) {
+      o[nd][0] *= a0;
+      o[nd][1] *= a0;
+      o[nd][2] *= a1;
+      o[nd][3] *= a1;
+    }
+    uint32_t pa[4];
+    pa[0] = pack_bf16x2(ps[0][0], ps[0][1]);
+    pa[1] = pack_bf16x2(ps[0][2], ps[0][3]);
+    pa[2] = pack_bf16x2(ps[1][0], ps[1][1]);
+    pa[3] = pack_bf16x2(ps[1][2], ps[1][3]);
+#pragma unroll
+    for (int c2 = 0; c2 < KT; ++c2) {
+      uint32_t vb[4];
+      ldsm_x4_t(vb, tile_addr(vbase, v_tok, c2 * 2 + v_sub));
+      mma_bf16(o[2 * c2], pa, vb[0], vb[1]);
+      mma_bf16(o[2 * c2 + 1], pa, vb[2], vb[3]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_empty + 8 * s);
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float s0 = p.sinks ? exp2f(p.sinks[hr0] * kLog2e - m0) : 0.f;
+  const float s1 = p.sinks ? exp2f(p.sinks[hr1] * kLog2e - m1) : 0.f;
+  const float inv0 = 1.f / (l0 + s0), inv1 = 1.f / (l1 + s1);
+  const int c = (lane & 3) * 2;
+  __nv_bfloat16* out0 = p.out + (((int64_t)b * p.S + j0 + jr0) * p.nq + hr0) * HD;
+  __nv_bfloat16* out1 = p.out + (((int64_t)b * p.S + j0 + jr1) * p.nq + hr1) * HD;
+#pragma unroll
+  for (int nd = 0; nd < ND; ++nd) {
+    if (ok0) *reinterpret_cast<uint32_t*>(out0 + nd * 8 + c) = pack_bf16x2(o[nd][0] * inv0, o[nd][1] * inv0);
+    if (ok1) *reinterpret_cast<uint32_t*>(out1 + nd * 8 + c) = pack_bf16x2(o[nd][2] * inv1, o[nd][3] * inv1);
+  }
+}
+
+template <int HD, int STAGES>
+int launch_prefill(const PrefillParams& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t st) {
+  using L = Layout<HD, STAGES>;
+  auto kern = prefill_attn_kernel<HD, STAGES>;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev & 63]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN_SMEM) != cudaSuccess) {
+      set_last_error("fg_prefill_attn: cannot set the kernel's shared-memory limit");
+      return FG_ERR_CUDA;
+    }
+    attr_done[dev & 63] = true;
+  }
+  return launch_k("fg_prefill_attn", kern, dim3((p.S + p.QP - 1) / p.QP, p.nkv, p.B), dim3(kThreads),
+                  L::DYN_SMEM, st, tk, tv, p);
+}
+
 }  // namespace attn
 }  // namespace fg
 
@@ -513,6 +747,47 @@ int fg_paged_decode_attn(const fg_bf16* q, const fg_bf16* k_cache, const fg_bf16
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (hd == 128) return launch<128, 8>(p, tk, tv, st);
   return launch<64, 8>(p, tk, tv, st);
+}
+
+int fg_prefill_attn(const fg_bf16* q, const fg_bf16* k_cache, const fg_bf16* v_cache,
+                    const int32_t* block_table, const int32_t* first_pos, const float* sinks, fg_bf16* out,
+                    int B, int S, int nq, int nkv, int hd, int block_size, int num_blocks, int max_blocks,
+                    int window, float scale, fg_stream_t stream) {
+  using namespace fg::attn;
+  FG_REQUIRE(q && k_cache && v_cache && block_table && first_pos && out, "fg_prefill_attn: null pointer");
+  FG_REQUIRE(hd == 64 || hd == 128, "fg_prefill_attn: hd must be 64 or 128, got %d", hd);
+  FG_REQUIRE(block_size == kBlock, "fg_prefill_attn: block_size must be 16, got %d", block_size);
+  FG_REQUIRE(nkv > 0 && nq % nkv == 0 && nq / nkv <= 16 && 64 % (nq / nkv) == 0,
+             "fg_prefill_attn: nq/nkv must divide 64 (nq=%d nkv=%d)", nq, nkv);
+  FG_REQUIRE(B >= 0 && S >= 0 && num_blocks > 0 && max_blocks > 0 && window >= 0, "fg_prefill_attn: bad sizes");
+  FG_REQUIRE((((uintptr_t)q | (uintptr_t)k_cache | (uintptr_t)v_cache | (uintptr_t)out) & 15) == 0,
+             "fg_prefill_attn: q/k/v/out must be 16-byte aligned");
+  if (B == 0 || S == 0) return FG_OK;
+  PrefillParams p;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  p.block_table = block_table;
+  p.p0 = first_pos;
+  p.sinks = sinks;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.B = B;
+  p.S = S;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.G = nq / nkv;
+  p.QP = 64 / p.G;
+  p.max_blocks = max_blocks;
+  p.num_blocks = num_blocks;
+  p.window = window;
+  p.scale_log2 = scale * kLog2e;
+  const uint64_t rows = (uint64_t)num_blocks * nkv * kBlock;
+  CUtensorMap tk, tv;
+  int rc = fg::make_tmap_2d_bf16(&tk, k_cache, hd, rows, (uint64_t)hd * 2, 64, kBlock, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = fg::make_tmap_2d_bf16(&tv, v_cache, hd, rows, (uint64_t)hd * 2, 64, kBlock, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (hd == 128) return launch_prefill<128, 8>(p, tk, tv, st);
+  return launch_prefill<64, 8>(p, tk, tv, st);
 }
 
 }  // extern "C"

@@ -96,7 +96,10 @@ __global__ void __launch_bounds__(THREADS) rmsnorm_kernel(const uint4* __restric
 // RoPE (rotate-half) + paged KV append, one decode token per sequence
 // ---------------------------------------------------------------------------
 // grid (B, nq + 2*nkv), block hd/2: thread i rotates the pair (i, i + hd/2).
+// token b of qkv belongs to sequence seq_ids[b] (seq_ids null: sequence b,
+// one token per sequence as in decode) at position positions[b]
 __global__ void rope_kv_append_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                      const int32_t* __restrict__ seq_ids,
                                       const int32_t* __restrict__ positions,
                                       const float* __restrict__ inv_freq, float attn_scaling,
                                       const int32_t* __restrict__ block_table, int max_blocks,
@@ -131,8 +134,9 @@ __global__ void rope_kv_append_kernel(const __nv_bfloat16* __restrict__ qkv,
     dst[i + half] = f2bf(o2);
     return;
   }
+  const int seq = seq_ids ? seq_ids[b] : b;
   const int page = pos / block_size;
-  int blk = (pos >= 0 && page < max_blocks) ? block_table[(int64_t)b * max_blocks + page] : -1;
+  int blk = (pos >= 0 && page < max_blocks) ? block_table[(int64_t)seq * max_blocks + page] : -1;
   if (blk < 0 || blk >= num_blocks) {
     if (i == 0) record_device_error(DEV_BAD_INDEX, 2);
     return;
@@ -311,23 +315,42 @@ int fg_rmsnorm(const fg_bf16* x, const fg_bf16* weight, fg_bf16* out, int T, int
                       weight_mode);
 }
 
-int fg_rope_kv_append(const fg_bf16* qkv, const int32_t* positions, const float* inv_freq,
-                      float attention_scaling, const int32_t* block_table, int max_blocks,
-                      int num_blocks, fg_bf16* q_out, fg_bf16* k_cache, fg_bf16* v_cache, int B,
-                      int nq, int nkv, int hd, int block_size, fg_stream_t stream) {
+static int rope_kv_append_launch(const fg_bf16* qkv, const int32_t* seq_ids, const int32_t* positions,
+                                 const float* inv_freq, float attention_scaling, const int32_t* block_table,
+                                 int max_blocks, int num_blocks, fg_bf16* q_out, fg_bf16* k_cache,
+                                 fg_bf16* v_cache, int T, int nq, int nkv, int hd, int block_size,
+                                 fg_stream_t stream) {
   FG_REQUIRE(qkv && positions && inv_freq && block_table && q_out && k_cache && v_cache,
              "fg_rope_kv_append: null pointer");
-  FG_REQUIRE(B >= 0 && nq > 0 && nkv > 0 && nq % nkv == 0, "fg_rope_kv_append: bad heads");
+  FG_REQUIRE(T >= 0 && nq > 0 && nkv > 0 && nq % nkv == 0, "fg_rope_kv_append: bad heads");
   FG_REQUIRE(hd % 2 == 0 && hd <= 256 && block_size > 0 && max_blocks > 0 && num_blocks > 0,
              "fg_rope_kv_append: bad hd=%d / block_size=%d", hd, block_size);
-  if (B == 0) return FG_OK;
-  return fg::launch_k("fg_rope_kv_append", fg::rope_kv_append_kernel, dim3(B, nq + 2 * nkv),
+  if (T == 0) return FG_OK;
+  return fg::launch_k("fg_rope_kv_append", fg::rope_kv_append_kernel, dim3(T, nq + 2 * nkv),
                       dim3(hd / 2), 0, (cudaStream_t)stream,
-                      reinterpret_cast<const __nv_bfloat16*>(qkv), positions, inv_freq,
+                      reinterpret_cast<const __nv_bfloat16*>(qkv), seq_ids, positions, inv_freq,
                       attention_scaling, block_table, max_blocks, num_blocks,
                       reinterpret_cast<__nv_bfloat16*>(q_out),
                       reinterpret_cast<__nv_bfloat16*>(k_cache),
                       reinterpret_cast<__nv_bfloat16*>(v_cache), nq, nkv, hd, block_size);
+}
+
+int fg_rope_kv_append(const fg_bf16* qkv, const int32_t* positions, const float* inv_freq,
+                      float attention_scaling, const int32_t* block_table, int max_blocks,
+                      int num_blocks, fg_bf16* q_out, fg_bf16* k_cache, fg_bf16* v_cache, int B,
+                      int nq, int nkv, int hd, int block_size, fg_stream_t stream) {
+  return rope_kv_append_launch(qkv, nullptr, positions, inv_freq, attention_scaling, block_table, max_blocks,
+                               num_blocks, q_out, k_cache, v_cache, B, nq, nkv, hd, block_size, stream);
+}
+
+int fg_rope_kv_append_tokens(const fg_bf16* qkv, const int32_t* seq_ids, const int32_t* positions,
+                             const float* inv_freq, float attention_scaling, const int32_t* block_table,
+                             int max_blocks, int num_blocks, fg_bf16* q_out, fg_bf16* k_cache,
+                             fg_bf16* v_cache, int T, int nq, int nkv, int hd, int block_size,
+                             fg_stream_t stream) {
+  FG_REQUIRE(seq_ids, "fg_rope_kv_append_tokens: null seq_ids");
+  return rope_kv_append_launch(qkv, seq_ids, positions, inv_freq, attention_scaling, block_table, max_blocks,
+                               num_blocks, q_out, k_cache, v_cache, T, nq, nkv, hd, block_size, stream);
 }
 
 int fg_kv_append(const fg_bf16* k, const fg_bf16* v, const int32_t* seq_ids,

@@ -71,6 +71,12 @@ class LayerExecutor:
                          **kwargs: Any) -> torch.Tensor | None:
         return self._run(task_name, fn, hidden, mode=mode, seq_len=seq_len, **kwargs)
 
+    def message_capacity(self) -> int | None:
+        """Largest tensor (bytes) the comm backend carries in one hand-off;
+        None when it has no fixed slot size."""
+        cap = getattr(self._comm, "slot_bytes", None)
+        return None if cap is None else int(cap)
+
     def send_aux_tensor(self, tensor: torch.Tensor, *, dst: int) -> None:
         self._comm.send_tensor(tensor, dst=dst)
 

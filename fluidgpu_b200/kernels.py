@@ -238,6 +238,48 @@ def rope_kv_append(qkv: torch.Tensor, positions: torch.Tensor, inv_freq: torch.T
     return q_out
 
 
+def rope_kv_append_tokens(qkv: torch.Tensor, seq_ids: torch.Tensor, positions: torch.Tensor,
+                          inv_freq: torch.Tensor, attention_scaling: float, block_table: torch.Tensor,
+                          k_cache: torch.Tensor, v_cache: torch.Tensor, nq: int, nkv: int, hd: int,
+                          q_out: torch.Tensor | None = None) -> torch.Tensor:
+    """rope_kv_append for T tokens: token t of sequence seq_ids[t] at positions[t]."""
+    _check(qkv, "qkv", _BF16)
+    _check(seq_ids, "seq_ids", torch.int32)
+    _check(positions, "positions", torch.int32)
+    _check(inv_freq, "inv_freq", torch.float32)
+    _check(block_table, "block_table", torch.int32)
+    T = positions.numel()
+    assert seq_ids.numel() == T and qkv.numel() == T * (nq + 2 * nkv) * hd, "qkv / token shape mismatch"
+    num_blocks, _, block_size, _ = k_cache.shape
+    if q_out is None:
+        q_out = torch.empty((T, nq, hd), dtype=_BF16, device=qkv.device)
+    call("fg_rope_kv_append_tokens", _ptr(qkv), _ptr(seq_ids), _ptr(positions), _ptr(inv_freq),
+         float(attention_scaling), _ptr(block_table), block_table.shape[1], num_blocks, _ptr(q_out),
+         _ptr(k_cache), _ptr(v_cache), T, nq, nkv, hd, block_size, _stream(qkv.device))
+    return q_out
+
+
+def prefill_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                 first_pos: torch.Tensor, S: int, *, window: int = 0, sinks: torch.Tensor | None = None,
+                 scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal attention of S query positions per sequence (q [B*S, nq, hd],
+    sequence b's queries at first_pos[b] ..) over the paged cache."""
+    _check(q, "q", _BF16)
+    _check(first_pos, "first_pos", torch.int32)
+    T, nq, hd = q.shape
+    B = first_pos.numel()
+    assert T == B * S, f"prefill q has {T} rows, expected {B} x {S}"
+    num_blocks, nkv, block_size, _ = k_cache.shape
+    if out is None:
+        out = torch.empty((T, nq, hd), dtype=_BF16, device=q.device)
+    if sinks is not None:
+        _check(sinks, "sinks", torch.float32)
+    call("fg_prefill_attn", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(block_table), _ptr(first_pos),
+         _ptr(sinks), _ptr(out), B, S, nq, nkv, hd, block_size, num_blocks, block_table.shape[1], window,
+         float(scale if scale is not None else hd ** -0.5), _stream(q.device))
+    return out
+
+
 def kv_append(k: torch.Tensor, v: torch.Tensor, seq_ids: torch.Tensor, positions: torch.Tensor,
               block_table: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor) -> None:
     """Write rotated k / raw v [T, nkv, hd] into their paged slots."""

@@ -209,8 +209,11 @@ class PagedKVCache:
             assert nxt <= self.max_seq_len, f"exceed max_seq_len: {nxt} > {self.max_seq_len}"
             assert nxt < len(self._blocks[b]) * BLOCK + 1, "sequence ran past its reserved pages"
             self._host_pos[b] = nxt
-        for _ in range(seq_len):
+        if seq_len == 1:
             kernels.advance(self.positions, self.seq_lens)
+        else:  # a prefill chunk: one counter update on the device
+            self.positions[: self.batch] += seq_len
+            self.seq_lens[: self.batch] += seq_len
 
     def max_attended(self) -> int:
         """Longest attention span of the coming step (host mirror)."""

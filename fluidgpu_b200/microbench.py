@@ -4,6 +4,8 @@
   python -m fluidgpu_b200.microbench gemm  [--T T] [--N N] [--K K] [--epilogue store|residual|swiglu]
   python -m fluidgpu_b200.microbench sweep-attn      # B in {1,32,256} x ctx in {512,4096,32768}
   python -m fluidgpu_b200.microbench moe   [--T T]  # gpt-oss MXFP4 expert GEMMs, 32 experts top-4
+  python -m fluidgpu_b200.microbench prefill-attn [--batch B] [--S S] [--context L]  # causal prefill attention
+  python -m fluidgpu_b200.microbench prefill [--model M] [--batch B] [--S S] [--chunk C]  # whole-model prefill
   torchrun --nproc-per-node 2 -m fluidgpu_b200.microbench handoff
       # [T,H] bf16 hand-off GPU0 -> GPU1, T in {1,8,64,256,1024,8192}, H in {2880,4096}:
       # NVLink mailbox put/recv (P2PComm) against NCCL send/recv, one-way time
@@ -269,9 +271,69 @@ def bench_handoff(iters: int = 50, warmup: int = 10) -> None:
     dist.destroy_process_group()
 
 
+def bench_prefill_attn(B: int, S: int, ctx: int = 0, nq: int = 32, nkv: int = 8, hd: int = 128,
+                       window: int = 0, iters: int = 10, warmup: int = 3, seed: int = 4) -> dict:
+    """fg_prefill_attn: S causal query positions per sequence after `ctx`
+    cached ones. FLOPs = 4 * hd * nq * (attended keys summed over queries)."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    L = ctx + S
+    pages = (L + 15) // 16
+    num_blocks = B * pages
+    kc = torch.empty((num_blocks, nkv, 16, hd), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
+    vc = torch.empty_like(kc).normal_(generator=g)
+    table = torch.randperm(num_blocks, generator=g, device="cuda").to(torch.int32).view(B, pages).contiguous()
+    q = torch.empty((B * S, nq, hd), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
+    first = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+    out = torch.empty_like(q)
+    fn = lambda: kernels.prefill_attn(q, kc, vc, table, first, S, window=window, out=out)  # noqa: E731
+    ms = _time(fn, iters, warmup)
+    keys = sum(min(ctx + j + 1, window) if window else ctx + j + 1 for j in range(S))
+    flops = 4.0 * hd * nq * B * keys
+    nbytes = 2.0 * (2 * B * S * nq * hd + 2 * B * nkv * hd * L)
+    kernels.check_device("prefill attn microbench")
+    return {"kernel": "fg_prefill_attn", "B": B, "S": S, "context": ctx, "nq": nq, "nkv": nkv, "hd": hd,
+            "window": window, "ms": ms, "TFLOPs": flops / (ms * 1e-3) / 1e12,
+            "GBps": nbytes / (ms * 1e-3) / 1e9, "timing": "graph" if GRAPH else "eager"}
+
+
+def bench_prefill(model: str, B: int, S: int, chunk: int, iters: int = 3, warmup: int = 1) -> dict:
+    """Whole-model prefill throughput (random weights): FluidRunner.prefill of
+    B prompts of S tokens in chunks of `chunk` positions, eager launches,
+    CUDA events around each prefill."""
+    from .config import EngineConfig
+    from .engine import DecodeEngine
+    from .model import SPECS, ModelWeights
+
+    spec = SPECS[model]
+    w = ModelWeights.random(spec, seed=0, device=torch.device("cuda:0"))
+    eng = DecodeEngine(w, EngineConfig(model_name=spec.name, max_seq_len=S + 8, world_size=1,
+                                       device="cuda:0", max_batch=B))
+    ids = torch.randint(0, spec.vocab, (B, S), device="cuda")
+    ts = []
+    for i in range(warmup + iters):
+        eng.start(B, reserve_tokens=S + 2)
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        eng.runner.prefill(ids, chunk=chunk)
+        b.record()
+        torch.cuda.synchronize()
+        if i >= warmup:
+            ts.append(a.elapsed_time(b))
+    ms = statistics.median(ts)
+    kernels.check_device("prefill microbench")
+    return {"bench": "prefill", "model": model, "B": B, "S": S, "chunk": chunk, "ms": ms,
+            "tokens_per_s": B * S / (ms * 1e-3), "timing": "eager, events around the prefill"}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["attn", "gemm", "sweep-attn", "llama-gemms", "handoff", "moe"])
+    ap.add_argument("what", choices=["attn", "gemm", "sweep-attn", "llama-gemms", "handoff", "moe",
+                                     "prefill-attn", "prefill"])
+    ap.add_argument("--model", default="llama-3-8b")
+    ap.add_argument("--S", type=int, default=2048)
+    ap.add_argument("--chunk", type=int, default=512)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--window", type=int, default=0)
@@ -300,6 +362,11 @@ def main() -> None:
     elif a.what == "gemm":
         print(json.dumps(bench_gemm(a.T, a.N, a.K, a.epilogue, a.iters, a.warmup, splits=a.splits,
                                     packed=not a.rowmajor)))
+    elif a.what == "prefill-attn":
+        print(json.dumps(bench_prefill_attn(a.batch, a.S, a.context, a.nq, a.nkv, a.hd, a.window,
+                                            a.iters, a.warmup)))
+    elif a.what == "prefill":
+        print(json.dumps(bench_prefill(a.model, a.batch, a.S, a.chunk)))
     elif a.what == "moe":
         for line in bench_moe(a.T, iters=a.iters, warmup=a.warmup):
             print(json.dumps(line), flush=True)

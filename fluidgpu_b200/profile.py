@@ -252,6 +252,14 @@ def ffn_shard_of(profile: RuntimeProfile, rank: int) -> tuple[int, int] | None:
     return found
 
 
+def has_fine_groups(profile: RuntimeProfile) -> bool:
+    """True when a layer's attention or dense FFN is split into sub-groups
+    (qkv / sdpa / o_proj, mlp_gate_up / mlp_down_proj). Such plans prefill
+    one position per pass through the decode kernels; the others prefill
+    chunks of positions."""
+    return any(n.endswith(("_qkv", "_mlp_gate_up")) for n in profile.task_index_by_name)
+
+
 def kv_layer_ids(profile: RuntimeProfile, rank: int) -> list[int]:
     """Layers whose paged KV lives on `rank`: where the attention reads it
     (attn, or sdpa in a split plan). Equal to owned_layer_ids except when

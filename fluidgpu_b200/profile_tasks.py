@@ -11,9 +11,10 @@ Differences from the reference's table, each forced by what is measured:
   * batch > 1 decodes together (the reference's runner is batch 1), and the
     KV pages hold `--context` tokens of synthetic values, so decode_us is the
     cost at that batch and context;
-  * prefill runs the prompt through the decode kernels one position at a
-    time (no batched prefill kernel yet): prefill_us is the sum over the
-    `--prefill-len` positions of a batch-1 prompt;
+  * prefill_us is one batched prefill pass of a batch-1 prompt of
+    `--prefill-len` positions (token-wise RoPE/KV append, causal prefill
+    attention over the pages, GEMMs over every position), as the
+    reference's whole-prompt HF forward;
   * for MoE models the groups are layer_i_moe_router / _moe_experts /
     _moe_combine; a layer_i_mlp row (their sum) is added for planners that
     expect the coarse attn / mlp split.

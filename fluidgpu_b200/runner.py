@@ -54,6 +54,7 @@ from .config import EngineConfig
 from .executor import LayerExecutor
 from .kv_cache import PagedKVCache
 from .model import ModelWeights
+from .profile import has_fine_groups
 
 
 class FluidRunner:
@@ -73,14 +74,20 @@ class FluidRunner:
             max_seq_len=cfg.max_seq_len, num_kv_heads=self.spec.n_kv, head_dim=self.spec.head_dim,
             dtype=cfg.dtype, device=self.device, max_batch=cfg.max_batch, num_blocks=num_blocks,
             allocation=cfg.kv_allocation)
+        self._mode, self._n = "decode", 1
         self._moe_states: dict[int, dict[str, torch.Tensor]] = {}
         self._attn_states: dict[int, dict[str, torch.Tensor]] = {}
         self._mlp_states: dict[int, dict[str, torch.Tensor]] = {}
         # scratch slots of this runner (runners on other streams use their own)
         self.slot = f"runner{id(self):x}"
+        # positions per sequence in one prefill pass (bounded by activation memory)
+        self.prefill_chunk = 512
         # MoE routing of the last step per layer (tests compare it with the oracle)
         self.record_routing = False
         self.last_routing: dict[int, torch.Tensor] = {}
+        # with record_routing: every pass's (layer, positions per sequence,
+        # indices [B * n, k]) in order, when this is a list
+        self.routing_log: list[tuple[int, int, torch.Tensor]] | None = None
 
     # -- sequence admission ---------------------------------------------------
     def start(self, batch: int, prompt_lens: list[int] | None = None,
@@ -93,17 +100,30 @@ class FluidRunner:
 
     # -- reference entry points -----------------------------------------------
     @torch.inference_mode()
-    def prefill(self, input_ids: torch.Tensor) -> torch.Tensor | None:
-        """Prompts [B, S] (equal lengths) -> logits of the last position [B, 1, V]."""
+    def prefill(self, input_ids: torch.Tensor, chunk: int | None = None) -> torch.Tensor | None:
+        """Prompts [B, S] (equal lengths) -> logits of the last position [B, 1, V].
+
+        The prompt runs in chunks of `chunk` positions (default prefill_chunk),
+        each chunk one pass of every kernel group over its B*chunk tokens:
+        token-wise RoPE + KV append, causal attention over the pages
+        (fg_prefill_attn, earlier chunks included), GEMMs over all the tokens.
+        Plans with fine-grained attention / FFN splits feed the prompt one
+        position at a time through the decode path instead."""
         assert input_ids.ndim == 2, "input_ids must be [batch, seq]"
         B, S = input_ids.shape
         assert S <= self.cfg.max_seq_len, f"prompt length {S} exceeds max_seq_len {self.cfg.max_seq_len}"
         if self.kv_cache.batch != B or self.kv_cache.get_seq_length() != 0:
             self.start(B)
         ids = input_ids.to(self.device)
+        step = 1 if has_fine_groups(self.executor.profile) else max(1, chunk or self.prefill_chunk)
+        cap = self.executor.message_capacity()
+        if cap is not None and self.executor.profile.rank_count > 1:
+            # every hand-off of a chunk must fit one mailbox slot
+            step = max(1, min(step, cap // self.max_message_bytes(B)))
         out = None
-        for t in range(S):
-            out = self._step(ids[:, t : t + 1], want_logits=(t == S - 1))
+        for t in range(0, S, step):
+            n = min(step, S - t)
+            out = self._step(ids[:, t : t + n], want_logits=(t + n == S))
         return out
 
     @torch.inference_mode()
@@ -119,31 +139,34 @@ class FluidRunner:
 
     # -- step -------------------------------------------------------------------
     def _step(self, tokens: torch.Tensor, *, want_logits: bool) -> torch.Tensor | None:
-        B = tokens.shape[0]
+        """tokens [B, n]: one decode step (n == 1) or one prefill chunk."""
+        B, n = tokens.shape
+        mode = "decode" if n == 1 else "prefill"
+        self._mode, self._n = mode, n  # the kernel groups of this pass run in this mode
         ex = self.executor
-        self.kv_cache.prepare_step(1)  # blocks for this step's token (no-op inside a graph capture)
-        hidden = ex.run_stage("embed", self._embed, tokens, mode="decode", seq_len=1, batch=B)
+        self.kv_cache.prepare_step(n)  # blocks for these tokens (no-op inside a graph capture)
+        hidden = ex.run_stage("embed", self._embed, tokens, mode=mode, seq_len=n, batch=B)
         for i in self.layers:
             hidden = self._run_attention_tasks(i, hidden, B)
             hidden = self._run_feed_forward_tasks(i, hidden, B)
-        self.kv_cache.advance(1)
+        self.kv_cache.advance(n)
         head = self._norm_head if want_logits else self._skip_head
-        return ex.run_stage("norm_lm_head", head, hidden, mode="decode", seq_len=1, batch=B)
+        return ex.run_stage("norm_lm_head", head, hidden, mode=mode, seq_len=n, batch=B)
 
     def _has_task(self, name: str) -> bool:
         return name in self.executor.task_index_by_name
 
     def _run_attention_tasks(self, i: int, hidden: torch.Tensor | None, B: int) -> torch.Tensor | None:
         if not self._has_task(f"layer_{i}_qkv"):
-            out = self.executor.run_kernel_group(f"layer_{i}_attn", self._run_attn, hidden, mode="decode",
-                                                 seq_len=1, batch=B, layer=i)
+            out = self.executor.run_kernel_group(f"layer_{i}_attn", self._run_attn, hidden, mode=self._mode,
+                                                 seq_len=self._n, batch=B, layer=i)
             return out if out is not None else hidden
         s = self.spec
         for suffix, fn in (("qkv", self._run_attn_qkv), ("sdpa", self._run_attn_sdpa),
                            ("o_proj", self._run_attn_o_proj)):
             kw = {"recv_width": s.n_q * s.head_dim} if suffix == "o_proj" else {}
-            out = self.executor.run_kernel_group(f"layer_{i}_{suffix}", fn, hidden, mode="decode",
-                                                 seq_len=1, batch=B, layer=i, **kw)
+            out = self.executor.run_kernel_group(f"layer_{i}_{suffix}", fn, hidden, mode=self._mode,
+                                                 seq_len=self._n, batch=B, layer=i, **kw)
             if out is not None:
                 hidden = out
                 if suffix == "qkv":
@@ -155,8 +178,8 @@ class FluidRunner:
     def _run_feed_forward_tasks(self, i: int, hidden: torch.Tensor | None, B: int) -> torch.Tensor | None:
         if self._has_task(f"layer_{i}_mlp_gate_up"):
             for suffix, fn in (("mlp_gate_up", self._run_mlp_gate_up), ("mlp_down_proj", self._run_mlp_down_proj)):
-                out = self.executor.run_kernel_group(f"layer_{i}_{suffix}", fn, hidden, mode="decode",
-                                                     seq_len=1, batch=B, layer=i)
+                out = self.executor.run_kernel_group(f"layer_{i}_{suffix}", fn, hidden, mode=self._mode,
+                                                     seq_len=self._n, batch=B, layer=i)
                 if out is not None:
                     hidden = out
                     if suffix == "mlp_gate_up":
@@ -164,12 +187,12 @@ class FluidRunner:
             return hidden
         if self._has_task(f"layer_{i}_mlp"):
             out = self.executor.run_kernel_group(f"layer_{i}_mlp", self._run_mlp, hidden,
-                                                 mode="decode", seq_len=1, batch=B, layer=i)
+                                                 mode=self._mode, seq_len=self._n, batch=B, layer=i)
             return out if out is not None else hidden
         for suffix, fn in (("moe_router", self._run_moe_router), ("moe_experts", self._run_moe_experts),
                            ("moe_combine", self._run_moe_combine)):
-            out = self.executor.run_kernel_group(f"layer_{i}_{suffix}", fn, hidden, mode="decode",
-                                                 seq_len=1, batch=B, layer=i)
+            out = self.executor.run_kernel_group(f"layer_{i}_{suffix}", fn, hidden, mode=self._mode,
+                                                 seq_len=self._n, batch=B, layer=i)
             if out is not None:
                 hidden = out
                 if suffix == "moe_router":
@@ -182,30 +205,47 @@ class FluidRunner:
     # `out`: where the group's result must land (the next rank's slot of a
     # zero-copy hand-off); the group's last kernel writes there directly
     def _embed(self, tokens: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        B = tokens.shape[0]
+        B, n = tokens.shape
         o = kernels.embed(tokens.reshape(-1).contiguous(), self.weights.embed,
-                          out=None if out is None else out.view(B, -1))
-        return o.view(B, 1, -1) if out is None else out
+                          out=None if out is None else out.view(B * n, -1))
+        return o.view(B, n, -1) if out is None else out
 
     def _run_attn(self, hidden: torch.Tensor, *, layer: int, out: torch.Tensor | None = None,
                   **_: Any) -> torch.Tensor:
         s = self.spec
         W = self.weights.layers[layer]
         kv = self.kv_cache
-        B = hidden.shape[0]
-        h = hidden.reshape(B, s.hidden)
+        B, n = hidden.shape[0], hidden.shape[1]
+        T = B * n
+        h = hidden.reshape(T, s.hidden)
         x = kernels.rmsnorm(h, W["ln1"], s.eps, s.norm_mode)
         qkv = kernels.gemm(x, W["wqkv"], bias=W.get("bqkv"), slot=self.slot + ".gemm")
         kp, vp = kv.layer_pages(layer)
         bt = kv.block_table[:B]
-        q = kernels.rope_kv_append(qkv, kv.positions[:B], self.weights.inv_freq,
-                                   self.weights.rope_scaling, bt, kp, vp, s.n_q, s.n_kv, s.head_dim)
-        a = kernels.paged_decode_attn(q, kp, vp, bt, kv.seq_lens[:B], kv.plan_len(),
-                                      window=s.window(layer), sinks=W.get("sinks"),
-                                      slot=self.slot + ".attn")
+        if n == 1:
+            q = kernels.rope_kv_append(qkv, kv.positions[:B], self.weights.inv_freq,
+                                       self.weights.rope_scaling, bt, kp, vp, s.n_q, s.n_kv, s.head_dim)
+            a = kernels.paged_decode_attn(q, kp, vp, bt, kv.seq_lens[:B], kv.plan_len(),
+                                          window=s.window(layer), sinks=W.get("sinks"),
+                                          slot=self.slot + ".attn")
+        else:
+            seq_ids, pos = self._chunk_tokens(B, n)
+            q = kernels.rope_kv_append_tokens(qkv, seq_ids, pos, self.weights.inv_freq,
+                                              self.weights.rope_scaling, kv.block_table, kp, vp,
+                                              s.n_q, s.n_kv, s.head_dim)
+            a = kernels.prefill_attn(q, kp, vp, kv.block_table, kv.positions[:B], n,
+                                     window=s.window(layer), sinks=W.get("sinks")).view(T, -1)
         o = kernels.gemm(a, W["wo"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h, bias=W.get("bo"),
-                         out=None if out is None else out.view(B, s.hidden), slot=self.slot + ".gemm")
-        return o.view(B, 1, s.hidden) if out is None else out
+                         out=None if out is None else out.view(T, s.hidden), slot=self.slot + ".gemm")
+        return o.view(B, n, s.hidden) if out is None else out
+
+    def _chunk_tokens(self, B: int, n: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """(sequence id, position) of every token of a prefill chunk of n
+        positions per sequence, from the device position counters."""
+        seq = torch.arange(B, device=self.device, dtype=torch.int32).repeat_interleave(n)
+        pos = (self.kv_cache.positions[:B, None]
+               + torch.arange(n, device=self.device, dtype=torch.int32)[None, :]).reshape(-1)
+        return seq, pos.to(torch.int32).contiguous()
 
     # fine attention groups (runner.py:256-347)
     def _run_attn_qkv(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
@@ -275,7 +315,8 @@ class FluidRunner:
                  out: torch.Tensor | None = None, **_: Any) -> torch.Tensor:
         s = self.spec
         W = self.weights.layers[layer]
-        B = hidden.shape[0]
+        B0, n = hidden.shape[0], hidden.shape[1]
+        B = B0 * n  # token rows
         h = hidden.reshape(B, s.hidden)
         x = kernels.rmsnorm(h, W["ln2"], s.eps, s.norm_mode)
         act = kernels.gemm(x, W["w_gate_up"], epilogue=_lib.FG_EPI_SWIGLU, slot=self.slot + ".gemm")
@@ -286,10 +327,10 @@ class FluidRunner:
                 f"layer {layer}: plan shard {shard} != weights shard {self.weights.ffn_shard}")
             out = kernels.gemm(act, W["w_down"], epilogue=_lib.FG_EPI_F32,
                                residual=h if shard[0] == 0 else None, slot=self.slot + ".gemm")
-            return out.view(B, 1, s.hidden)
+            return out.view(B0, n, s.hidden)
         o = kernels.gemm(act, W["w_down"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h,
                          out=None if out is None else out.view(B, s.hidden), slot=self.slot + ".gemm")
-        return o.view(B, 1, s.hidden) if out is None else out
+        return o.view(B0, n, s.hidden) if out is None else out
 
     # fine dense FFN groups (runner.py:416-430)
     def _run_mlp_gate_up(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
@@ -329,21 +370,23 @@ class FluidRunner:
 
         s = self.spec
         W = self.weights.layers[layer]
-        B = hidden.shape[0]
+        B0, n = hidden.shape[0], hidden.shape[1]
+        B = B0 * n  # token rows
         h = hidden.reshape(B, s.hidden)
         x = kernels.rmsnorm(h, W["ln2"], s.eps, s.norm_mode)
         weights, idx = moe.router_topk(x, W["router_w"], W.get("router_b"), s.top_k)
         self._moe_states[layer] = {"residual": h, "weights": weights, "indices": idx}
         if self.record_routing:
-            self.last_routing[layer] = idx
-        return x.view(B, 1, s.hidden)
+            self._record_routing(layer, idx)
+        return x.view(B0, n, s.hidden)
 
     def _run_moe_experts(self, hidden: torch.Tensor, *, layer: int, shard: tuple[int, int] | None = None,
                          **_: Any) -> torch.Tensor:
         from . import moe
 
         s = self.spec
-        B = hidden.shape[0]
+        B0, n = hidden.shape[0], hidden.shape[1]
+        B = B0 * n  # token rows
         if shard is not None:
             # expert-parallel shard: fp32 partial over this rank's experts
             assert self.weights.ffn_shard == shard, (
@@ -352,9 +395,9 @@ class FluidRunner:
             wts = self._recv_aux((B, s.top_k), torch.bfloat16, src)
             idx = self._recv_aux((B, s.top_k), torch.int32, src)
             if self.record_routing:
-                self.last_routing[layer] = idx
+                self._record_routing(layer, idx)
             y = moe.experts_forward(hidden.reshape(B, s.hidden), idx, wts, self.weights.layers[layer], s)
-            return y.view(B, 1, s.hidden)
+            return y.view(B0, n, s.hidden)
         st = self._moe_states.setdefault(layer, {})
         if "indices" not in st:
             src = self._rank_of(layer, "moe_router")
@@ -362,7 +405,7 @@ class FluidRunner:
             st["indices"] = self._recv_aux((B, s.top_k), torch.int32, src)
             st["residual"] = self._recv_aux((B, s.hidden), torch.bfloat16, src)
             if self.record_routing:
-                self.last_routing[layer] = st["indices"]
+                self._record_routing(layer, st["indices"])
         # the combine group's residual add is fused when it runs here too (not
         # under zero-copy hand-offs, where the combine writes the peer's slot)
         fuse = (self._rank_of(layer, "moe_combine") == self.executor.my_rank
@@ -371,13 +414,19 @@ class FluidRunner:
                                 self.weights.layers[layer], s,
                                 residual=st["residual"] if fuse else None)
         st["fused"] = fuse
-        return y.view(B, 1, s.hidden)
+        return y.view(B0, n, s.hidden)
+
+    def _record_routing(self, layer: int, idx: torch.Tensor) -> None:
+        self.last_routing[layer] = idx
+        if self.routing_log is not None:
+            self.routing_log.append((layer, self._n, idx.clone()))
 
     def _run_moe_combine(self, hidden: torch.Tensor, *, layer: int, out: torch.Tensor | None = None,
                          **_: Any) -> torch.Tensor:
         from . import moe
 
-        B = hidden.shape[0]
+        B0, n = hidden.shape[0], hidden.shape[1]
+        B = B0 * n  # token rows
         self._ensure_residual(self._moe_states, layer, B, src=self._rank_of(layer, "moe_experts"))
         st = self._moe_states.pop(layer)
         if st.get("fused"):
@@ -385,7 +434,7 @@ class FluidRunner:
             return hidden
         o = moe.residual_add(st["residual"], hidden.reshape(B, -1),
                              out=None if out is None else out.view(B, -1))
-        return o.view(B, 1, -1) if out is None else out
+        return o.view(B0, n, -1) if out is None else out
 
     def _after_moe_router(self, layer: int) -> None:
         shards = self._shards_of(layer, "moe_experts")
@@ -443,6 +492,8 @@ class FluidRunner:
     def _norm_head(self, hidden: torch.Tensor) -> torch.Tensor:
         s = self.spec
         B = hidden.shape[0]
+        if hidden.dim() == 3 and hidden.shape[1] > 1:  # a prefill chunk: the last position only
+            hidden = hidden[:, -1].contiguous()
         x = kernels.rmsnorm(hidden.reshape(B, s.hidden), self.weights.final_norm, s.eps, s.norm_mode)
         return kernels.gemm(x, self.weights.lm_head, slot=self.slot + ".gemm").view(B, 1, s.vocab)
 
@@ -451,7 +502,8 @@ class FluidRunner:
 
     def max_message_bytes(self, batch: int) -> int:
         """Largest tensor this plan sends between two ranks in a decode step of
-        `batch` sequences (the P2PComm slot must hold it)."""
+        `batch` sequences (the P2PComm slot must hold it); a prefill chunk of
+        n positions sends n times as much."""
         s = self.spec
         names = self.executor.task_index_by_name
         sizes = [batch * s.hidden * 2]

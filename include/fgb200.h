@@ -132,6 +132,14 @@ int fg_rope_kv_append(const fg_bf16* qkv, const int32_t* positions, const float*
                       float attention_scaling, const int32_t* block_table, int max_blocks,
                       int num_blocks, fg_bf16* q_out, fg_bf16* k_cache, fg_bf16* v_cache, int B,
                       int nq, int nkv, int hd, int block_size, fg_stream_t stream);
+/* fg_rope_kv_append for T tokens of any sequences: token t (row t of qkv and
+ * q_out) belongs to sequence seq_ids[t] at position positions[t] (a prefill
+ * chunk: S consecutive positions per sequence). */
+int fg_rope_kv_append_tokens(const fg_bf16* qkv, const int32_t* seq_ids, const int32_t* positions,
+                             const float* inv_freq, float attention_scaling, const int32_t* block_table,
+                             int max_blocks, int num_blocks, fg_bf16* q_out, fg_bf16* k_cache,
+                             fg_bf16* v_cache, int T, int nq, int nkv, int hd, int block_size,
+                             fg_stream_t stream);
 
 /* Paged KV append of already-rotated keys: token t (k,v:[T, nkv, hd]) of
  * sequence seq_ids[t] at position positions[t] goes to its page slot. The
@@ -165,6 +173,18 @@ int fg_paged_decode_attn(const fg_bf16* q, const fg_bf16* k_cache, const fg_bf16
 int fg_attn_splits(int B, int nkv, int hd, int max_seq_len, int window);
 /* Workspace bytes fg_paged_decode_attn needs for these sizes (0 if none). */
 size_t fg_attn_workspace_bytes(int B, int nq, int nkv, int hd, int max_seq_len, int window);
+
+/* Causal prefill attention over the paged cache: q [B*S][nq][hd] holds S
+ * consecutive query positions per sequence starting at first_pos[b] (their
+ * K/V already appended, earlier context cached before them); query at
+ * position p attends keys k <= p (and k > p - window when window > 0), sinks
+ * as in fg_paged_decode_attn. out [B*S][nq][hd] bf16. nq/nkv must divide 64.
+ * Replaces the reference's prefill attention over the whole prompt
+ * (runner.py:66-116 with the masks of :713-823). */
+int fg_prefill_attn(const fg_bf16* q, const fg_bf16* k_cache, const fg_bf16* v_cache,
+                    const int32_t* block_table, const int32_t* first_pos, const float* sinks, fg_bf16* out,
+                    int B, int S, int nq, int nkv, int hd, int block_size, int num_blocks, int max_blocks,
+                    int window, float scale, fg_stream_t stream);
 
 /* Paged decode attention for callers that cannot allocate device memory (a
  * runtime that owns all device memory through its own pool and refuses

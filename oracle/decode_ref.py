@@ -257,6 +257,9 @@ class OracleModel:
         self.v_cache: list[list[torch.Tensor]] = []
         self.lengths: list[int] = []
         self.router_indices: list[torch.Tensor] = []  # per layer, last step
+        # per layer, last step: each token's gap between its k-th and (k+1)-th
+        # router logit (a small gap is a near tie that rounding may flip)
+        self.router_margins: list[torch.Tensor] = []
 
     def reset(self, batch: int) -> None:
         L = self.spec.num_layers
@@ -307,6 +310,9 @@ class OracleModel:
         scores = torch.softmax(top_v, dim=-1, dtype=top_v.dtype) if self.dtype != torch.float32 \
             else torch.softmax(top_v, dim=-1)
         self.router_indices.append(top_i.clone())
+        if s.top_k < s.num_experts:
+            kk = torch.topk(logits.float(), s.top_k + 1, dim=-1).values
+            self.router_margins.append(kk[:, s.top_k - 1] - kk[:, s.top_k])
         out = torch.zeros_like(x)
         wgu = self.w[f"{i}.w_gate_up"]
         bgu = self.w[f"{i}.b_gate_up"]
@@ -331,6 +337,7 @@ class OracleModel:
         positions = torch.tensor(self.lengths, dtype=torch.long)
         h = self.w["embed"][tokens.reshape(-1)]
         self.router_indices = []
+        self.router_margins = []
         for i in range(s.num_layers):
             h = self._attention(i, h, positions)
             h = self._moe_ffn(i, h) if s.moe else self._dense_ffn(i, h)

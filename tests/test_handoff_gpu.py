@@ -119,7 +119,7 @@ def _disaggregated(rank, comm, plan=_attn_ffn_plan):
     from fluidgpu_b200.config import EngineConfig
     from fluidgpu_b200.engine import DecodeEngine
     from fluidgpu_b200.model import ModelWeights
-    from fluidgpu_b200.profile import profile_from_dict
+    from fluidgpu_b200.profile import has_fine_groups, profile_from_dict
 
     torch.manual_seed(0)
     cfg = LlamaConfig(num_hidden_layers=3, vocab_size=2048, hidden_size=512, intermediate_size=1024,
@@ -150,7 +150,7 @@ def _disaggregated(rank, comm, plan=_attn_ffn_plan):
                        EngineConfig(model_name="colo", max_seq_len=64, world_size=1, device="cuda:0",
                                     max_batch=B))
     ref.start(B, reserve_tokens=prompt + steps + 2)
-    out = ref.runner.prefill(prompts.cuda())
+    out = ref.runner.prefill(prompts.cuda(), chunk=1 if has_fine_groups(prof) else None)
     for s in range(steps):
         lg = out.reshape(B, -1).float().cpu()
         assert torch.equal(lg, logits[s]), f"step {s}: disaggregated logits differ"

@@ -298,3 +298,64 @@ def test_advance():
     kernels.advance(pos, lens)
     assert pos.cpu().tolist() == [1, 2, 3, 4, 5]
     assert lens.cpu().tolist() == [2, 3, 4, 5, 6]
+
+
+@pytest.mark.parametrize(
+    "B,nq,nkv,hd,S,ctx,window,sinks",
+    [
+        (2, 32, 8, 128, 37, [0, 20], 0, False),     # Llama-style GQA 4, context before the chunk
+        (3, 16, 4, 64, 64, [0, 0, 5], 0, False),
+        (2, 64, 8, 64, 50, [0, 100], 16, True),     # gpt-oss-style GQA 8, window, sinks
+        (1, 8, 8, 128, 130, [3], 0, False),         # MHA (64 positions per CTA)
+        (2, 32, 2, 64, 33, [0, 0], 0, True),        # GQA 16
+    ],
+)
+def test_prefill_attention(B, nq, nkv, hd, S, ctx, window, sinks):
+    """Causal prefill attention over the pages: query j of sequence b sits at
+    position ctx[b] + j and attends keys 0 .. ctx[b] + j (and the window)."""
+    from fluidgpu_b200 import kernels
+
+    g = _gen(9)
+    lens = [c + S for c in ctx]
+    num_blocks = sum((l + 15) // 16 for l in lens) + 5
+    table, kc, vc = _paged_setup(B, nkv, hd, lens, num_blocks, g)
+    q = _randn((B * S, nq, hd), g)
+    sk = (torch.randn(nq, generator=g) * 2.0) if sinks else None
+    first = torch.tensor(ctx, dtype=torch.int32)
+    out = kernels.prefill_attn(q.to(DEV), kc.to(DEV), vc.to(DEV), table.to(DEV), first.to(DEV), S,
+                               window=window, sinks=None if sk is None else sk.to(DEV)).cpu()
+    scale = 1.0 / math.sqrt(hd)
+    worst = 0.0
+    for b in range(B):
+        k = _gather(kc, table, b, lens[b])
+        v = _gather(vc, table, b, lens[b])
+        for j in range(S):
+            L = ctx[b] + j + 1
+            exp = ref.attention_one(q[b * S + j], k[:L], v[:L], scale, window, sk)
+            worst = max(worst, (out[b * S + j].float() - exp.reshape(nq, hd)).abs().max().item())
+    assert worst <= 2e-2, worst
+
+
+def test_rope_kv_append_tokens_matches_per_sequence():
+    """The token-wise form equals the per-sequence one bit for bit."""
+    from fluidgpu_b200 import kernels
+
+    g = _gen(10)
+    B, S, nq, nkv, hd = 3, 5, 8, 2, 64
+    num_blocks = 12
+    table = torch.randperm(num_blocks, generator=g)[: B * 4].view(B, 4).to(torch.int32)
+    qkv = _randn((B * S, (nq + 2 * nkv) * hd), g)
+    inv_freq = ref.default_inv_freq(hd, 10000.0).to(DEV)
+    seq = torch.arange(B, dtype=torch.int32).repeat_interleave(S)
+    start = torch.tensor([0, 14, 30], dtype=torch.int32)
+    pos = (start[:, None] + torch.arange(S, dtype=torch.int32)[None, :]).reshape(-1)
+    kc1 = torch.zeros((num_blocks, nkv, 16, hd), dtype=torch.bfloat16, device=DEV)
+    vc1, kc2, vc2 = kc1.clone(), kc1.clone(), kc1.clone()
+    qkvd, td = qkv.to(DEV), table.to(DEV)
+    q1 = kernels.rope_kv_append_tokens(qkvd, seq.to(DEV), pos.to(DEV), inv_freq, 1.0, td, kc1, vc1, nq, nkv, hd)
+    q2 = torch.empty_like(q1)
+    for j in range(S):  # one position of every sequence at a time, as decode does
+        rows = torch.arange(B) * S + j
+        x = qkvd[rows.to(DEV)].contiguous()
+        q2[rows.to(DEV)] = kernels.rope_kv_append(x, (start + j).to(DEV), inv_freq, 1.0, td, kc2, vc2, nq, nkv, hd)
+    assert torch.equal(q1, q2) and torch.equal(kc1, kc2) and torch.equal(vc1, vc2)

@@ -1,0 +1,215 @@
+"""Batched chunked prefill (FluidRunner.prefill: token-wise RoPE/KV append,
+causal attention over the pages, GEMMs over every token of a chunk) against
+the CPU oracle's position-by-position prefill on the same HF weights.
+
+The reference runs a prompt as one forward over all its positions
+(runner.py:160-184, HF attention with a causal mask); the oracle restates
+that position by position, which is the same math. Tolerances are the decode
+tests' (north star, bf16): |logit - oracle| <= 2e-2 + 1e-2 |oracle|, or no
+worse than the reference's own bf16 arithmetic. After the prompt, a few
+teacher-forced decode steps check that the KV pages the prefill wrote are
+the ones decode reads (positions, RoPE, block tables).
+
+Chunk sizes cover one chunk for the whole prompt, chunks that do not divide
+the prompt (a ragged last chunk), chunks shorter than the sliding window and
+chunks that cross page boundaries (block size 16)."""
+import pytest
+import torch
+
+from oracle import decode_ref as ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+ATOL, RTOL = 2e-2, 1e-2
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    from fluidgpu_b200 import build
+
+    build.build()
+    yield
+    from fluidgpu_b200 import kernels
+
+    kernels.check_device("prefill tests")
+
+
+def _tiny_llama():
+    from transformers.models.llama import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(0)
+    cfg = LlamaConfig(num_hidden_layers=3, vocab_size=4096, hidden_size=1024, intermediate_size=2816,
+                      num_attention_heads=16, num_key_value_heads=4, max_position_embeddings=4096,
+                      rope_theta=500000.0)
+    return LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+
+
+def _tiny_gptoss():
+    from transformers.models.gpt_oss import GptOssConfig, GptOssForCausalLM
+
+    from fluidgpu_b200 import moe
+
+    torch.manual_seed(0)
+    cfg = GptOssConfig(num_hidden_layers=2, num_local_experts=8, vocab_size=1024, hidden_size=512,
+                       intermediate_size=256, head_dim=64, num_attention_heads=8, num_key_value_heads=2,
+                       sliding_window=16, num_experts_per_tok=2,
+                       layer_types=["sliding_attention", "full_attention"], max_position_embeddings=4096)
+    cfg._attn_implementation = "eager"
+    model = GptOssForCausalLM(cfg).to(torch.bfloat16).eval()
+    with torch.no_grad():
+        for layer in model.model.layers:
+            ex = layer.mlp.experts
+            for name in ("gate_up_proj", "down_proj"):  # MXFP4-exact experts, as a real checkpoint
+                p = getattr(ex, name)
+                v, s = moe.quantize_mxfp4(p.data.transpose(1, 2).float())
+                p.data.copy_(moe.dequantize_mxfp4(v, s).transpose(1, 2).to(p.dtype))
+            layer.mlp.router.weight.data.normal_(0, 0.2)
+            layer.self_attn.sinks.data.normal_(0, 1.0)
+    return model
+
+
+def _engine(model, batch, max_seq_len):
+    from fluidgpu_b200.config import EngineConfig
+    from fluidgpu_b200.engine import DecodeEngine
+    from fluidgpu_b200.model import ModelWeights
+
+    w = ModelWeights.from_hf(model, DEV)
+    return DecodeEngine(w, EngineConfig(model_name="tiny", max_seq_len=max_seq_len, world_size=1,
+                                        device=DEV, max_batch=batch))
+
+
+class _Judge:
+    """Per step, on the rows being compared: greedy tokens equal wherever the
+    exact model's top-2 margin clears twice the tolerance, and every logit
+    within atol/rtol of the fp32 oracle or of the reference's own bf16
+    arithmetic (the bf16 oracle), or the worst deviation no more than 1.25x
+    that bf16 arithmetic's own. Dense models also keep 1 - cosine <= 1e-4.
+
+    MoE rows: the GPU's expert choice for every token of every pass (prefill
+    chunks included) is compared with the exact model's. A differing choice
+    must be a near tie (the exact model's k-th and (k+1)-th router logits
+    within FLIP_MARGIN; the bf16 oracle itself flips choices up to ~0.16
+    apart on these random models), and its sequence leaves the logit
+    comparison from that position on. Most rows must stay."""
+
+    FLIP_MARGIN = 0.25
+
+    def __init__(self, moe, batch):
+        self.moe = moe
+        self.rows = torch.ones(batch, dtype=torch.bool)
+        self.flips = 0
+
+    def observe(self, oracle, gpu_choice):
+        """gpu_choice[layer]: the GPU's expert ids [B, k] for this position."""
+        if not self.moe:
+            return
+        for layer, (want, margin) in enumerate(zip(oracle.router_indices, oracle.router_margins)):
+            got = gpu_choice[layer].long()
+            diff = (torch.sort(got, -1).values != torch.sort(want, -1).values).any(-1) & self.rows
+            if diff.any():
+                assert (margin[diff] < self.FLIP_MARGIN).all(), (
+                    f"layer {layer}: expert choice differs at router margin {margin[diff].tolist()}")
+                self.flips += int(diff.sum())
+                self.rows &= ~diff
+
+    def check(self, got, truth, bf16, what):
+        r = self.rows
+        got, truth, bf16 = got.float().cpu()[r], truth.float()[r], bf16.float()[r]
+        err = (got - truth).abs()
+        near_truth = (err <= ATOL + RTOL * truth.abs()).all()
+        near_bf16 = ((got - bf16).abs() <= ATOL + RTOL * bf16.abs()).all()
+        ref_err = (bf16 - truth).abs().max().item() if r.any() else 0.0
+        assert near_truth or near_bf16 or err.max().item() <= 1.25 * ref_err + 1e-3, (
+            f"{what}: max-abs {err.max().item():.4f} vs reference-bf16 {ref_err:.4f}")
+        if not self.moe:
+            cos = torch.nn.functional.cosine_similarity(got, truth, dim=-1).min().item()
+            assert cos >= 0.9999, f"{what}: cosine {cos}"
+        top2 = truth.topk(2, dim=-1).values
+        decided = (top2[:, 0] - top2[:, 1]) > 2 * (ATOL + RTOL * top2[:, 0].abs())
+        assert torch.equal(ref.argmax_lowest(got)[decided], ref.argmax_lowest(truth)[decided]), (
+            f"{what}: greedy token mismatch")
+
+
+def _gpu_choices(log, batch, k):
+    """The runner's routing log -> {(layer, position): expert ids [B, k]}."""
+    out, nxt = {}, {}
+    for layer, n, idx in log:
+        idx = idx.cpu().view(batch, n, k)
+        p0 = nxt.get(layer, 0)
+        for j in range(n):
+            out[(layer, p0 + j)] = idx[:, j]
+        nxt[layer] = p0 + n
+    log.clear()
+    return out
+
+
+def _run(model, batch, prompt, chunk, steps=4, seed=0):
+    spec = ref.spec_from_hf(model.config)
+    w = ref.weights_from_hf(model)
+    truth = ref.OracleModel(spec, {k: v.float() for k, v in w.items()}, torch.float32)
+    bf16 = ref.OracleModel(spec, w, torch.bfloat16)
+    eng = _engine(model, batch, prompt + steps + 2)
+    g = torch.Generator().manual_seed(seed)
+    prompts = torch.randint(0, model.config.vocab_size, (batch, prompt), generator=g)
+    eng.start(batch, reserve_tokens=prompt + steps + 2)
+    eng.runner.record_routing = spec.moe
+    log = eng.runner.routing_log = []
+    judge = _Judge(spec.moe, batch)
+    got = eng.runner.prefill(prompts.to(DEV), chunk=chunk).reshape(batch, -1)
+    choices = _gpu_choices(log, batch, spec.top_k) if spec.moe else {}
+    truth.reset(batch)
+    for t in range(prompt):  # position by position, checking every expert choice
+        lt = truth.step(prompts[:, t])
+        judge.observe(truth, [choices.get((layer, t)) for layer in range(spec.num_layers)])
+    lb = bf16.prefill_stepwise(prompts)
+    judge.check(got, lt, lb, f"prefill chunk={chunk}")
+    for s in range(steps):
+        tok = ref.argmax_lowest(lt.float())
+        got = eng.runner.decode_step(tok.to(DEV)).reshape(batch, -1)
+        lt, lb = truth.step(tok), bf16.step(tok)
+        if spec.moe:
+            choices = _gpu_choices(log, batch, spec.top_k)
+            judge.observe(truth, [choices[(layer, 0)] for layer in range(spec.num_layers)])
+        judge.check(got, lt, lb, f"decode {s} after chunk={chunk}")
+    assert judge.rows.sum() * 2 >= batch, f"only {int(judge.rows.sum())} of {batch} rows clear of router ties"
+    assert int(eng.kv_cache.get_seq_length()) == prompt + steps
+
+
+@pytest.mark.parametrize("batch,prompt,chunk", [(4, 40, None), (4, 40, 16), (3, 37, 5), (2, 70, 32), (1, 9, 1)])
+def test_llama_prefill_matches_oracle(batch, prompt, chunk):
+    _run(_tiny_llama(), batch, prompt, chunk)
+
+
+@pytest.mark.parametrize("batch,prompt,chunk", [(4, 40, None), (3, 45, 12), (2, 33, 7)])
+def test_gpt_oss_prefill_matches_oracle(batch, prompt, chunk):
+    """Sliding-window layers (window 16 < prompt) with sinks, MoE over B*chunk tokens."""
+    _run(_tiny_gptoss(), batch, prompt, chunk)
+
+
+def test_prefill_chunking_is_consistent():
+    """One chunk vs many: the same KV pages and the same last-position logits
+    up to summation order (different GEMM row counts, same reductions per row)."""
+    model = _tiny_llama()
+    B, S = 3, 48
+    prompts = torch.randint(0, model.config.vocab_size, (B, S), generator=torch.Generator().manual_seed(3))
+    outs, pages = [], []
+    from fluidgpu_b200.kv_cache import BLOCK
+
+    for chunk in (None, 16, 1):
+        eng = _engine(model, B, S + 2)
+        eng.start(B, reserve_tokens=S + 2)
+        outs.append(eng.runner.prefill(prompts.to(DEV), chunk=chunk).reshape(B, -1).float().cpu())
+        kv = eng.kv_cache
+        kp, vp = kv.layer_pages(0)
+        bt = kv.block_table[:B].long().cpu()
+        # layer 0's K/V depend only on the embeddings: equal whatever the
+        # chunking, up to the QKV GEMM's summation order at a different row count
+        k = torch.stack([kp[bt[b, : S // BLOCK]].float().cpu() for b in range(B)])
+        v = torch.stack([vp[bt[b, : S // BLOCK]].float().cpu() for b in range(B)])
+        pages.append((k, v))
+    for o in outs[1:]:
+        err = (o - outs[0]).abs()
+        assert (err <= ATOL + RTOL * outs[0].abs()).all(), f"max |delta| {err.max().item():.4f}"
+    for k, v in pages[1:]:
+        torch.testing.assert_close(k, pages[0][0], atol=2e-2, rtol=1.6e-2)
+        torch.testing.assert_close(v, pages[0][1], atol=2e-2, rtol=1.6e-2)

@@ -65,7 +65,7 @@ def _tiny_gptoss():
     return model
 
 
-def _decode(weights, prof, comm, B, prompts, steps, rank, out, feed=None):
+def _decode(weights, prof, comm, B, prompts, steps, rank, out, feed=None, chunk=None):
     from fluidgpu_b200.config import EngineConfig
     from fluidgpu_b200.engine import DecodeEngine
 
@@ -74,7 +74,7 @@ def _decode(weights, prof, comm, B, prompts, steps, rank, out, feed=None):
                        profile=prof, comm=comm)
     eng.start(B, reserve_tokens=prompts.shape[1] + steps + 2)
     logits = []
-    o = eng.runner.prefill(prompts.to(DEV))
+    o = eng.runner.prefill(prompts.to(DEV), chunk=chunk)
     for s in range(steps):
         if o is not None:
             logits.append(o.reshape(B, -1).float().cpu())
@@ -89,7 +89,8 @@ def _decode(weights, prof, comm, B, prompts, steps, rank, out, feed=None):
 def _run_split(model, assignments, B=4, prompt=9, steps=5):
     from fluidgpu_b200.comm import QueueComm
     from fluidgpu_b200.model import ModelWeights
-    from fluidgpu_b200.profile import colocated_profile, make_ranked_task_profile, profile_from_dict
+    from fluidgpu_b200.profile import (colocated_profile, has_fine_groups, make_ranked_task_profile,
+                                       profile_from_dict)
 
     weights = ModelWeights.from_hf(model, DEV)
     s = weights.spec
@@ -122,7 +123,9 @@ def _run_split(model, assignments, B=4, prompt=9, steps=5):
     ref = {}
     from fluidgpu_b200.comm import LocalComm
 
-    _decode(weights, colo, LocalComm(), B, prompts, steps, 0, ref)
+    # a plan with sub-groups prefills position by position: the co-located
+    # run does the same, so every kernel sees the same rows
+    _decode(weights, colo, LocalComm(), B, prompts, steps, 0, ref, chunk=1 if has_fine_groups(prof) else None)
     for step, (a, b) in enumerate(zip(results[0], ref[0])):
         assert torch.equal(a, b), f"step {step}: split logits differ from co-located"
 
