@@ -77,6 +77,7 @@ SIGNATURES: dict[str, tuple] = {
     "fg_attn_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
     "fg_argmax": (c_int, [_P, _P, c_int, c_int, _P]),
     "fg_moe_router_topk": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P, _P, _P]),
+    "fg_moe_topk_softmax": (c_int, [_P, c_int, c_int, c_int, _P, _P, _P]),
     "fg_moe_tile_tokens": (c_int, [c_int, c_int, c_int]),
     "fg_moe_max_items": (c_int, [c_int, c_int, c_int, c_int]),
     "fg_moe_permute": (c_int, [_P, c_int, c_int, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P, _P]),

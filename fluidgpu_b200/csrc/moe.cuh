@@ -40,6 +40,49 @@ constexpr int kMaxE = 64;
 // One CTA of 32 warps per token: warp w computes the logits of experts w,
 // w+32 (one dot product each, its loads all in flight together), then warp 0
 // selects the top-k.
+// Top-k of the E <= 64 logits a warp holds (lane e has experts e and e+32),
+// by value with the lower expert id first on ties, then the softmax over
+// the k selected (fp32, rounded to bf16). Lane 0 writes the k pairs.
+__device__ __forceinline__ void warp_topk_softmax(float v0, float v1, int lane, int E, int k,
+                                                  __nv_bfloat16* __restrict__ out_w,
+                                                  int32_t* __restrict__ out_idx) {
+  float sel_v[8];
+  int sel_i[8];
+  for (int j = 0; j < k; ++j) {
+    float bv = v0;
+    int bi = lane;
+    if (v1 > bv) {
+      bv = v1;
+      bi = lane + 32;
+    }
+    if (bi >= E) bi = 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    sel_v[j] = bv;
+    sel_i[j] = bi;
+    if (bi == lane) v0 = -INFINITY;
+    if (bi == lane + 32) v1 = -INFINITY;
+  }
+  if (lane == 0) {
+    float m = sel_v[0], s = 0.f, p[8];
+    for (int j = 0; j < k; ++j) {
+      p[j] = __expf(sel_v[j] - m);
+      s += p[j];
+    }
+    for (int j = 0; j < k; ++j) {
+      out_idx[j] = sel_i[j];
+      out_w[j] = f2bf(p[j] / s);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(1024) router_topk_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
     const __nv_bfloat16* __restrict__ bias, int H, int E, int k, __nv_bfloat16* __restrict__ out_w,
@@ -73,46 +116,24 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(
     }
   }
   __syncthreads();
-  if (warp == 0) {
-    // each lane holds up to two experts
-    float v0 = lane < E ? logit[lane] : -INFINITY;
-    float v1 = lane + 32 < E ? logit[lane + 32] : -INFINITY;
-    float sel_v[8];
-    int sel_i[8];
-    for (int j = 0; j < k; ++j) {
-      float bv = v0;
-      int bi = lane;
-      if (v1 > bv) {
-        bv = v1;
-        bi = lane + 32;
-      }
-      if (bi >= E) bi = 0x7fffffff;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      sel_v[j] = bv;
-      sel_i[j] = bi;
-      if (bi == lane) v0 = -INFINITY;
-      if (bi == lane + 32) v1 = -INFINITY;
-    }
-    if (lane == 0) {
-      float m = sel_v[0], s = 0.f, p[8];
-      for (int j = 0; j < k; ++j) {
-        p[j] = __expf(sel_v[j] - m);
-        s += p[j];
-      }
-      for (int j = 0; j < k; ++j) {
-        out_idx[(int64_t)t * k + j] = sel_i[j];
-        out_w[(int64_t)t * k + j] = f2bf(p[j] / s);
-      }
-    }
-  }
+  if (warp == 0)
+    warp_topk_softmax(lane < E ? logit[lane] : -INFINITY, lane + 32 < E ? logit[lane + 32] : -INFINITY,
+                      lane, E, k, out_w + (int64_t)t * k, out_idx + (int64_t)t * k);
+}
+
+// Top-k and softmax of router logits that are already computed (the vLLM
+// MoE runner receives them from the gate linear): one warp per token.
+__global__ void __launch_bounds__(256) topk_softmax_kernel(const __nv_bfloat16* __restrict__ logits, int T,
+                                                           int E, int k, __nv_bfloat16* __restrict__ out_w,
+                                                           int32_t* __restrict__ out_idx) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const __nv_bfloat16* row = logits + (int64_t)t * E;
+  warp_topk_softmax(lane < E ? bf2f(row[lane]) : -INFINITY, lane + 32 < E ? bf2f(row[lane + 32]) : -INFINITY,
+                    lane, E, k, out_w + (int64_t)t * k, out_idx + (int64_t)t * k);
 }
 
 // ---------------------------------------------------------------------------
@@ -851,6 +872,17 @@ int fg_moe_router_topk(const fg_bf16* x, const fg_bf16* w, const fg_bf16* bias, 
                       reinterpret_cast<const __nv_bfloat16*>(bias), H, E, k,
                       reinterpret_cast<__nv_bfloat16*>(weights), indices,
                       reinterpret_cast<__nv_bfloat16*>(logits));
+}
+
+int fg_moe_topk_softmax(const fg_bf16* logits, int T, int E, int k, fg_bf16* weights, int32_t* indices,
+                        fg_stream_t stream) {
+  FG_REQUIRE(logits && weights && indices, "fg_moe_topk_softmax: null pointer");
+  FG_REQUIRE(T >= 0 && E > 0 && E <= fg::moe::kMaxE && k > 0 && k <= 8 && k <= E,
+             "fg_moe_topk_softmax: bad sizes (E <= 64, k <= 8)");
+  if (T == 0) return FG_OK;
+  return fg::launch_k("fg_moe_topk_softmax", fg::moe::topk_softmax_kernel, dim3((T + 7) / 8), dim3(256), 0,
+                      (cudaStream_t)stream, reinterpret_cast<const __nv_bfloat16*>(logits), T, E, k,
+                      reinterpret_cast<__nv_bfloat16*>(weights), indices);
 }
 
 int fg_moe_max_items(int T, int k, int E, int BN) {

@@ -6,6 +6,7 @@
   python -m fluidgpu_b200.microbench moe   [--T T]  # gpt-oss MXFP4 expert GEMMs, 32 experts top-4
   python -m fluidgpu_b200.microbench prefill-attn [--batch B] [--S S] [--context L]  # causal prefill attention
   python -m fluidgpu_b200.microbench prefill [--model M] [--batch B] [--S S] [--chunk C]  # whole-model prefill
+  python -m fluidgpu_b200.microbench vllm-moe [--expert-device cuda:1]  # vLLM MoE forward_impl, gpt-oss-20b layer
   torchrun --nproc-per-node 2 -m fluidgpu_b200.microbench handoff
       # [T,H] bf16 hand-off GPU0 -> GPU1, T in {1,8,64,256,1024,8192}, H in {2880,4096}:
       # NVLink mailbox put/recv (P2PComm) against NCCL send/recv, one-way time
@@ -327,10 +328,46 @@ def bench_prefill(model: str, B: int, S: int, chunk: int, iters: int = 3, warmup
             "tokens_per_s": B * S / (ms * 1e-3), "timing": "eager, events around the prefill"}
 
 
+def bench_vllm_moe(T: int, expert_device: str = "cuda:0", E: int = 32, H: int = 2880, I: int = 2880, k: int = 4,
+                   iters: int = 20, warmup: int = 5, seed: int = 6) -> dict:
+    """The vLLM MoE forward_impl (vllm_ops.make_forward_impl) at gpt-oss-20b
+    layer shapes: router logits in, experts on expert_device, the result in
+    the home GPU's graph-stable buffer; random MXFP4 codes and scales in the
+    checkpoint's format. Eager calls bracketed by events on the home stream
+    (the cross-device copies order the expert device's work into it)."""
+    from .vllm_ops import ExpertsOnDevice, StableOutput, make_forward_impl
+
+    g = torch.Generator(device="cuda:0").manual_seed(seed)
+    gu_b = torch.randint(0, 256, (E, 2 * I, H // 32, 16), generator=g, device="cuda:0", dtype=torch.uint8)
+    gu_s = torch.randint(119, 123, (E, 2 * I, H // 32), generator=g, device="cuda:0", dtype=torch.uint8)
+    d_b = torch.randint(0, 256, (E, H, I // 32, 16), generator=g, device="cuda:0", dtype=torch.uint8)
+    d_s = torch.randint(119, 123, (E, H, I // 32), generator=g, device="cuda:0", dtype=torch.uint8)
+    gu_bias = torch.empty(E, 2 * I, device="cuda:0").normal_(0, 0.02, generator=g).to(torch.bfloat16)
+    d_bias = torch.empty(E, H, device="cuda:0").normal_(0, 0.02, generator=g).to(torch.bfloat16)
+    remote = ExpertsOnDevice(gu_b, gu_s, gu_bias, d_b, d_s, d_bias, expert_device, top_k=k)
+    stable = StableOutput(max(T, 1), H, torch.bfloat16, "cuda:0")
+    impl = make_forward_impl(remote, "cuda:0", stable)
+    x = torch.empty(T, H, device="cuda:0").normal_(generator=g).to(torch.bfloat16)
+    lg = torch.empty(T, E, device="cuda:0").normal_(0, 2, generator=g).to(torch.bfloat16)
+    global GRAPH
+    graph, GRAPH = GRAPH, False
+    try:
+        ms = _time(lambda: impl(None, x, lg, None), iters, warmup)
+    finally:
+        GRAPH = graph
+    touched = int(torch.unique(torch.topk(lg.float(), k, dim=-1).indices).numel())
+    nbytes = touched * 3 * H * I * (0.5 + 1 / 32) + 2.0 * T * H * 2
+    kernels.check_device("vllm moe microbench")
+    return {"op": "vllm forward_impl (MoE)", "T": T, "E": E, "H": H, "I": I, "k": k,
+            "expert_device": expert_device, "experts_touched": touched, "ms": ms,
+            "weight_GBps": nbytes / (ms * 1e-3) / 1e9, "timing": "eager, events on the home stream"}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["attn", "gemm", "sweep-attn", "llama-gemms", "handoff", "moe",
-                                     "prefill-attn", "prefill"])
+                                     "prefill-attn", "prefill", "vllm-moe"])
+    ap.add_argument("--expert-device", default="cuda:0")
     ap.add_argument("--model", default="llama-3-8b")
     ap.add_argument("--S", type=int, default=2048)
     ap.add_argument("--chunk", type=int, default=512)
@@ -367,6 +404,9 @@ def main() -> None:
                                             a.iters, a.warmup)))
     elif a.what == "prefill":
         print(json.dumps(bench_prefill(a.model, a.batch, a.S, a.chunk)))
+    elif a.what == "vllm-moe":
+        for T in ([a.T] if a.T != 64 else [1, 64, 128, 512, 2048]):
+            print(json.dumps(bench_vllm_moe(T, a.expert_device, iters=a.iters, warmup=a.warmup)), flush=True)
     elif a.what == "moe":
         for line in bench_moe(a.T, iters=a.iters, warmup=a.warmup):
             print(json.dumps(line), flush=True)

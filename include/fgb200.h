@@ -216,6 +216,12 @@ int fg_argmax(const fg_bf16* logits, int64_t* out, int T, int V, fg_stream_t str
 int fg_moe_router_topk(const fg_bf16* x, const fg_bf16* w, const fg_bf16* bias, int T, int H, int E,
                        int k, fg_bf16* weights, int32_t* indices, fg_bf16* logits,
                        fg_stream_t stream);
+/* Top-k + softmax of given router logits [T,E] (the vLLM MoE runner's input,
+ * vllm_integration.py:452-464: topk over the logits, softmax over the
+ * selected): ties to the lower expert id, weights = bf16(softmax in fp32).
+ * weights,indices:[T,k]. E <= 64, k <= 8. */
+int fg_moe_topk_softmax(const fg_bf16* logits, int T, int E, int k, fg_bf16* weights, int32_t* indices,
+                        fg_stream_t stream);
 /* Token tile (16/32/64) the expert GEMMs use for T tokens, and the bound on
  * (expert, token tile) work items fg_moe_permute emits. */
 int fg_moe_tile_tokens(int T, int k, int E);

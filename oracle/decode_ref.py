@@ -203,6 +203,45 @@ def mxfp4_dequantize(packed: torch.Tensor, scales: torch.Tensor, dtype=torch.bfl
 
 
 # ---------------------------------------------------------------------------
+# vLLM op boundary (fluidgpu_torch/vllm_integration.py)
+# ---------------------------------------------------------------------------
+def vllm_moe_experts(x: torch.Tensor, router_logits: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor,
+                     w2: torch.Tensor, b2: torch.Tensor, top_k: int,
+                     expert_range: tuple[int, int] | None = None) -> torch.Tensor:
+    """The expert computation behind the reference's vLLM MoE forward_impl
+    (MarlinExpertsOnDevice.forward_on_device, vllm_integration.py:452-485):
+    top-k of the router logits (lowest expert id first on ties), softmax over
+    the k selected in fp32, per selected expert gu = x W1^T + b1 with gate =
+    gu[:, 0::2], up = gu[:, 1::2] (the checkpoint's interleaved rows),
+    SwiGLU-OAI, y = act W2^T + b2, weighted sum over the k. fp32 throughout.
+    w1 [E, 2I, H], b1 [E, 2I], w2 [E, H, I], b2 [E, H]. With expert_range
+    only experts in [lo, hi) contribute (expert_map, :371-390), so two ranges
+    that cover all experts add up to the full result (:1052-1093)."""
+    x = x.float()
+    top_v, top_i = topk_lowest(router_logits.float(), top_k)
+    wts = torch.softmax(top_v, dim=-1)
+    lo, hi = expert_range if expert_range is not None else (0, w1.shape[0])
+    out = torch.zeros(x.shape[0], w2.shape[1], dtype=torch.float32)
+    for e in range(lo, hi):
+        tok, slot = torch.where(top_i == e)
+        if tok.numel() == 0:
+            continue
+        gu = x[tok] @ w1[e].float().T + b1[e].float()
+        act = swiglu_oai(gu[:, 0::2], gu[:, 1::2])
+        y = act @ w2[e].float().T + b2[e].float()
+        out.index_add_(0, tok, y * wts[tok, slot, None])
+    return out
+
+
+def vllm_dense_mlp(x: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    """RemoteDenseMLP._mlp (vllm_integration.py:1305-1311): w_gate_up is the
+    merged [gate; up] weight [2I, H]; down(SiLU(gate) * up) in fp32."""
+    gu = x.float() @ w_gate_up.float().T
+    gate, up = gu.chunk(2, dim=-1)
+    return (F.silu(gate) * up) @ w_down.float().T
+
+
+# ---------------------------------------------------------------------------
 # model
 # ---------------------------------------------------------------------------
 @dataclass
