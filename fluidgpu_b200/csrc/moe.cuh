@@ -422,9 +422,15 @@ __global__ void pack_mxfp4_kernel(const uint8_t* __restrict__ vals, const uint8_
 // tile) u = blockIdx.x + j * gridDim.x; a unit's K runs in steps of two
 // 64-wide records. 16 warps:
 //   warp 0       weight producer: one bulk copy per step into a deep ring
-//   warp 2       activation producer: the step's 2-D TMA tiles, own ring
+//   warp 2       activation producer: the step's 2-D TMA tiles into the
+//                activation stage paired with the step's A stage
 //   warp 1       TMEM owner and MMA issuer (8 x K16 per step into one of
-//                two accumulators, so the epilogue overlaps the next unit)
+//                two accumulators, so the epilogue overlaps the next unit);
+//                one barrier wait and one commit per step: the commit frees
+//                the A stage and its activation stage together, and the
+//                converters hold a_full until the activation tile landed.
+//                The issuing thread's serial latency per step is part of
+//                what bounds the kernel, so it is kept to that minimum.
 //   warps 4-11   two converter warpgroups taking alternate steps: a thread
 //                per weight row decodes its 128 values into a TMEM A stage
 //                (tcgen05.st); four A stages
@@ -458,15 +464,16 @@ constexpr int kLutBytes = 256 * 256;
 template <int BN>
 struct MLayout {
   static constexpr int WS = BN <= 16 ? 14 : (BN <= 32 ? 12 : 10);  // weight ring (steps)
-  static constexpr int XS = BN <= 32 ? 4 : 3;                      // activation ring (steps)
+  // activation ring: one stage per A stage, freed by the same MMA commit
+  static constexpr int XS = kAStages;
   static constexpr int X_TILE = BN * BK * 2;                       // [BN][64] f16, 128B swizzle
   static constexpr int X_STAGE = kKS * X_TILE;
   static constexpr int W_STAGE = kKS * kRecBytes;
   static constexpr int W_OFFSET = XS * X_STAGE;
   static constexpr int XCH_OFFSET = W_OFFSET + WS * W_STAGE;       // bf16 [BN][64]
   static constexpr int BAR_OFFSET = (XCH_OFFSET + BN * 64 * 2 + 7) / 8 * 8;
-  // w_full[WS] w_empty[WS] x_full[XS] x_empty[XS] a_full[A] a_empty[A] acc_full[2] acc_empty[2] mma_done
-  static constexpr int MISC_OFFSET = BAR_OFFSET + (2 * WS + 2 * XS + 2 * kAStages + 5) * 8;
+  // w_full[WS] w_empty[WS] x_full[XS] a_full[A] a_empty[A] acc_full[2] acc_empty[2] mma_done
+  static constexpr int MISC_OFFSET = BAR_OFFSET + (2 * WS + XS + 2 * kAStages + 5) * 8;
   static constexpr int TOTAL = MISC_OFFSET + 16;
   // the decode table sits at the start of dynamic shared memory, the
   // 1024-aligned region above starts after it
@@ -580,8 +587,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
   const uint32_t w_full = sbase + L::BAR_OFFSET;
   const uint32_t w_empty = w_full + WS * 8;
   const uint32_t x_full = w_empty + WS * 8;
-  const uint32_t x_empty = x_full + XS * 8;
-  const uint32_t a_full = x_empty + XS * 8;
+  const uint32_t a_full = x_full + XS * 8;
   const uint32_t a_empty = a_full + kAStages * 8;
   const uint32_t acc_full = a_empty + kAStages * 8;
   const uint32_t acc_empty = acc_full + 2 * 8;
@@ -597,7 +603,6 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     }
     for (int s = 0; s < XS; ++s) {
       mbar_init(x_full + 8 * s, 1);
-      mbar_init(x_empty + 8 * s, 1);  // MMA commit
     }
     for (int s = 0; s < kAStages; ++s) {
       mbar_init(a_full + 8 * s, 4);
@@ -669,7 +674,9 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
         const Unit w = unit_of(p, blockIdx.x + j * G, BN);
         for (int t = 0; t < nsteps; ++t, ++g) {
           const int s = g % XS;
-          if (!mbar_wait(x_empty + 8 * s, ((uint32_t)(g / XS) & 1u) ^ 1u, 0x322)) {
+          // stage s is free once the MMAs of step g - XS have completed (their
+          // commit releases A stage s and activation stage s together)
+          if (!mbar_wait(a_empty + 8 * s, ((uint32_t)(g / XS) & 1u) ^ 1u, 0x322)) {
             ok = false;
             break;
           }
@@ -695,8 +702,9 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
         const uint32_t d = tmem + kDCol0 + buf * BN;
         for (int t = 0; t < nsteps; ++t, ++g) {
           const int sa = g % kAStages, sx = g % XS;
-          if (!mbar_wait(a_full + 8 * sa, (uint32_t)(g / kAStages) & 1u, 0x324) ||
-              !mbar_wait(x_full + 8 * sx, (uint32_t)(g / XS) & 1u, 0x325)) {
+          // a_full also covers the step's activation tile: a converter saw
+          // x_full before arriving (one wait per step on this thread)
+          if (!mbar_wait(a_full + 8 * sa, (uint32_t)(g / kAStages) & 1u, 0x324)) {
             ok = false;
             break;
           }
@@ -710,7 +718,6 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
               tc_mma_ts(d, a + k16 * 8, bdesc + 2 * k16, idesc, (t > 0 || kk > 0 || k16 > 0) ? 1u : 0u);
           }
           gemm::tc_commit(a_empty + 8 * sa);
-          gemm::tc_commit(x_empty + 8 * sx);
         }
         if (ok) gemm::tc_commit(acc_full + 8 * buf);
       }
@@ -753,6 +760,12 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
       }
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       gemm::tc_fence_before();
+      // the step's activation tile must have landed before a_full releases the MMA
+      if (q == 0) {
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(x_full + 8 * sa, (uint32_t)(g / XS) & 1u, 0x325) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      }
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(a_full + 8 * sa);
