@@ -420,7 +420,7 @@ __global__ void pack_mxfp4_kernel(const uint8_t* __restrict__ vals, const uint8_
 //
 // Persistent: one CTA per SM walks the work units (permute item x 128-row
 // tile) u = blockIdx.x + j * gridDim.x; a unit's K runs in steps of two
-// 64-wide records. 16 warps:
+// 64-wide records (four per step for token tiles of 16 or 32, else two). 16 warps:
 //   warp 0       weight producer: one bulk copy per step into a deep ring
 //   warp 2       activation producer: the step's 2-D TMA tiles into the
 //                activation stage paired with the step's A stage
@@ -449,13 +449,10 @@ struct GemmParams {
   int e_base;                 // expert id of the first packed expert (expert-parallel shards)
 };
 
-constexpr int kKS = 2;            // records per step
 constexpr int kConvWarp0 = 4;
 constexpr int kEpiWarp0 = 12;
 constexpr int kMoeWarps = 16;
 constexpr int kMoeThreads = kMoeWarps * 32;
-constexpr int kAStages = 4;       // TMEM A stages of kKS * 32 columns
-constexpr int kDCol0 = kAStages * kKS * 32;  // two accumulators of BN columns follow the A stages
 // byte -> f16x2 decode table, one copy per lane: entry (byte b, lane l) at
 // b * 256 + l * 4, so a warp's 32 lookups hit 32 different banks and the
 // address is one byte permute of (b, 4l)
@@ -463,24 +460,29 @@ constexpr int kLutBytes = 256 * 256;
 
 template <int BN>
 struct MLayout {
-  static constexpr int WS = BN <= 16 ? 14 : (BN <= 32 ? 12 : 10);  // weight ring (steps)
+  // records per step: each step costs the MMA thread one barrier wait and one
+  // commit, so narrow token tiles (short MMAs) take longer steps
+  static constexpr int KS = BN <= 32 ? 4 : 2;
+  static constexpr int AST = BN <= 32 ? 3 : 4;                     // TMEM A stages of KS * 32 columns
+  static constexpr int DCOL0 = AST * KS * 32;                      // two accumulators of BN columns follow
+  static constexpr int WS = BN <= 32 ? 6 : 10;                     // weight ring (steps)
   // activation ring: one stage per A stage, freed by the same MMA commit
-  static constexpr int XS = kAStages;
+  static constexpr int XS = AST;
   static constexpr int X_TILE = BN * BK * 2;                       // [BN][64] f16, 128B swizzle
-  static constexpr int X_STAGE = kKS * X_TILE;
-  static constexpr int W_STAGE = kKS * kRecBytes;
+  static constexpr int X_STAGE = KS * X_TILE;
+  static constexpr int W_STAGE = KS * kRecBytes;
   static constexpr int W_OFFSET = XS * X_STAGE;
   static constexpr int XCH_OFFSET = W_OFFSET + WS * W_STAGE;       // bf16 [BN][64]
   static constexpr int BAR_OFFSET = (XCH_OFFSET + BN * 64 * 2 + 7) / 8 * 8;
   // w_full[WS] w_empty[WS] x_full[XS] a_full[A] a_empty[A] acc_full[2] acc_empty[2] mma_done
-  static constexpr int MISC_OFFSET = BAR_OFFSET + (2 * WS + XS + 2 * kAStages + 5) * 8;
+  static constexpr int MISC_OFFSET = BAR_OFFSET + (2 * WS + XS + 2 * AST + 5) * 8;
   static constexpr int TOTAL = MISC_OFFSET + 16;
   // the decode table sits at the start of dynamic shared memory, the
   // 1024-aligned region above starts after it
   static constexpr int DYN_SMEM = kLutBytes + TOTAL + 1024;
-  static constexpr uint32_t TMEM_COLS = 512;  // A stages 256 + two accumulators of BN <= 64
+  static constexpr uint32_t TMEM_COLS = 512;  // A stages (256 or 384 columns) + two accumulators of BN
   static_assert(X_TILE % 1024 == 0 && kRecBytes % 16 == 0, "stage alignment");
-  static_assert(kDCol0 + 2 * BN <= (int)TMEM_COLS, "tensor memory budget");
+  static_assert(DCOL0 + 2 * BN <= (int)TMEM_COLS, "tensor memory budget");
   static_assert(DYN_SMEM <= 232448, "shared memory budget");
 };
 
@@ -570,7 +572,7 @@ template <int BN>
 __global__ void __launch_bounds__(kMoeThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const GemmParams p) {
   using L = MLayout<BN>;
-  constexpr int WS = L::WS, XS = L::XS;
+  constexpr int WS = L::WS, XS = L::XS, kKS = L::KS, kAStages = L::AST, kDCol0 = L::DCOL0;
   extern __shared__ uint8_t smem_raw[];
   const uint8_t* lut = smem_raw;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw + kLutBytes) + 1023) &
