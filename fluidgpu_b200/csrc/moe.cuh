@@ -412,29 +412,35 @@ __global__ void pack_mxfp4_kernel(const uint8_t* __restrict__ vals, const uint8_
 
 // ---------------------------------------------------------------------------
 // MXFP4 x activation grouped GEMM (swap-AB). Weights are decoded (e2m1 ->
-// f16 by table lookup, times the block scale) straight into tensor memory
-// and used as the A operand of tcgen05.mma kind::f16 (A from TMEM, B = the
-// f16 activation tile from shared memory). Only the 4.25-bit records and
-// the activation tiles cross shared memory, so the kernel streams HBM
-// instead of saturating shared-memory bandwidth with expanded tiles.
+// f16 by the hardware conversion, times the block scale) straight into
+// tensor memory and used as the A operand of tcgen05.mma kind::f16 (A from
+// TMEM, B = the f16 activation tile from shared memory). Only the 4.25-bit
+// records and the activation tiles cross shared memory, so the kernel
+// streams HBM instead of saturating shared-memory bandwidth with expanded
+// tiles.
 //
-// Persistent: one CTA per SM walks the work units (permute item x 128-row
+// What bounds it at decode sizes is the MMA-issuing thread: a 128 x 16 MMA
+// covers only 1088 bytes of MXFP4, and the thread's serial path per step
+// (barrier wait, MMAs, commit, issue slots shared with the converters on
+// its sub-partition) costs more than the tensor pipe's ~52 cycles per MMA.
+// So the kernel is built for two resident CTAs per SM (two independent
+// issuing threads, half the tensor memory and shared memory each), and each
+// thread takes one barrier wait and one commit per step.
+//
+// Persistent: two CTAs per SM walk the work units (permute item x 128-row
 // tile) u = blockIdx.x + j * gridDim.x; a unit's K runs in steps of two
-// 64-wide records (four per step for token tiles of 16 or 32, else two). 16 warps:
-//   warp 0       weight producer: one bulk copy per step into a deep ring
+// 64-wide records. 12 warps:
+//   warp 0       weight producer: one bulk copy per step into a ring
 //   warp 2       activation producer: the step's 2-D TMA tiles into the
 //                activation stage paired with the step's A stage
 //   warp 1       TMEM owner and MMA issuer (8 x K16 per step into one of
 //                two accumulators, so the epilogue overlaps the next unit);
-//                one barrier wait and one commit per step: the commit frees
-//                the A stage and its activation stage together, and the
-//                converters hold a_full until the activation tile landed.
-//                The issuing thread's serial latency per step is part of
-//                what bounds the kernel, so it is kept to that minimum.
-//   warps 4-11   two converter warpgroups taking alternate steps: a thread
-//                per weight row decodes its 128 values into a TMEM A stage
-//                (tcgen05.st); four A stages
-//   warps 12-15  epilogue: accumulator x 2^(s_ref-127) + bias, SwiGLU-OAI
+//                the commit frees the A stage and its activation stage
+//                together, and the converters hold a_full until the
+//                activation tile has landed
+//   warps 4-7    converters: a thread per weight row decodes its 128 values
+//                of the step into a TMEM A stage (tcgen05.st)
+//   warps 8-11   epilogue: accumulator x 2^(s_ref-127) + bias, SwiGLU-OAI
 //                (gate rows 0-63 of a tile, up rows 64-127; f16 out) or
 //                store (bf16 out)
 // ---------------------------------------------------------------------------
@@ -450,22 +456,17 @@ struct GemmParams {
 };
 
 constexpr int kConvWarp0 = 4;
-constexpr int kEpiWarp0 = 12;
-constexpr int kMoeWarps = 16;
+constexpr int kEpiWarp0 = 8;
+constexpr int kMoeWarps = 12;
 constexpr int kMoeThreads = kMoeWarps * 32;
-// byte -> f16x2 decode table, one copy per lane: entry (byte b, lane l) at
-// b * 256 + l * 4, so a warp's 32 lookups hit 32 different banks and the
-// address is one byte permute of (b, 4l)
-constexpr int kLutBytes = 256 * 256;
+constexpr int kMoeCtasPerSm = 2;
 
 template <int BN>
 struct MLayout {
-  // records per step: each step costs the MMA thread one barrier wait and one
-  // commit, so narrow token tiles (short MMAs) take longer steps
-  static constexpr int KS = BN <= 32 ? 4 : 2;
-  static constexpr int AST = BN <= 32 ? 3 : 4;                     // TMEM A stages of KS * 32 columns
+  static constexpr int KS = 2;                                      // records per step
+  static constexpr int AST = BN <= 32 ? 3 : 2;                     // TMEM A stages of KS * 32 columns
   static constexpr int DCOL0 = AST * KS * 32;                      // two accumulators of BN columns follow
-  static constexpr int WS = BN <= 32 ? 6 : 10;                     // weight ring (steps)
+  static constexpr int WS = 8;                                     // weight ring (steps)
   // activation ring: one stage per A stage, freed by the same MMA commit
   static constexpr int XS = AST;
   static constexpr int X_TILE = BN * BK * 2;                       // [BN][64] f16, 128B swizzle
@@ -477,13 +478,11 @@ struct MLayout {
   // w_full[WS] w_empty[WS] x_full[XS] a_full[A] a_empty[A] acc_full[2] acc_empty[2] mma_done
   static constexpr int MISC_OFFSET = BAR_OFFSET + (2 * WS + XS + 2 * AST + 5) * 8;
   static constexpr int TOTAL = MISC_OFFSET + 16;
-  // the decode table sits at the start of dynamic shared memory, the
-  // 1024-aligned region above starts after it
-  static constexpr int DYN_SMEM = kLutBytes + TOTAL + 1024;
-  static constexpr uint32_t TMEM_COLS = 512;  // A stages (256 or 384 columns) + two accumulators of BN
+  static constexpr int DYN_SMEM = TOTAL + 1024;  // + slack for the 1024-byte alignment
+  static constexpr uint32_t TMEM_COLS = 256;     // half of the SM's: two CTAs per SM
   static_assert(X_TILE % 1024 == 0 && kRecBytes % 16 == 0, "stage alignment");
   static_assert(DCOL0 + 2 * BN <= (int)TMEM_COLS, "tensor memory budget");
-  static_assert(DYN_SMEM <= 232448, "shared memory budget");
+  static_assert(kMoeCtasPerSm * (DYN_SMEM + 1024) <= 233472, "shared memory budget (two CTAs per SM)");
 };
 
 // instruction descriptor for kind::f16 with f16 A/B, fp32 D, K-major
@@ -512,23 +511,16 @@ __device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&a)[32])
       : "memory");
 }
 
-// f16 bits of the e2m1 code n (sign, 2-bit exponent, 1-bit mantissa)
-__device__ __forceinline__ uint32_t e2m1_f16_bits(uint32_t n) {
-  const uint32_t mag = n & 7u;
-  // 0, 0.5, then 2^(e-1) * (1 + m/2): f16 exponent field e + 14, mantissa bit 9
-  const uint32_t bits = mag == 0u ? 0u : (mag == 1u ? 0x3800u : ((mag >> 1) + 14u) << 10 | (mag & 1u) << 9);
-  return bits | (n & 8u) << 12;
-}
-
-// four bytes of e2m1 pairs -> four f16x2 (low nibble in the low half) by
-// table lookup; the hardware e2m1 conversion issues on the narrow XU pipe
-// and would bound the kernel well below HBM speed
-__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t v, uint32_t lane4, const uint8_t* lut, uint32_t* o) {
-#pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    const uint32_t off = __byte_perm(v, lane4, 0x5504u | ((uint32_t)b << 4));  // byte b << 8 | 4*lane
-    o[b] = *reinterpret_cast<const uint32_t*>(lut + off);
-  }
+// eight e2m1 values (one 32-bit word, low nibble first) -> four f16x2 words
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t v, uint32_t* o) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(v));
 }
 
 // f16 bits of 2^(c-24), c in [0, 37], in both halves
@@ -569,22 +561,14 @@ __device__ __forceinline__ Unit unit_of(const GemmParams& p, int u, int BN) {
 }
 
 template <int BN>
-__global__ void __launch_bounds__(kMoeThreads, 1)
+__global__ void __launch_bounds__(kMoeThreads, kMoeCtasPerSm)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const GemmParams p) {
   using L = MLayout<BN>;
   constexpr int WS = L::WS, XS = L::XS, kKS = L::KS, kAStages = L::AST, kDCol0 = L::DCOL0;
   extern __shared__ uint8_t smem_raw[];
-  const uint8_t* lut = smem_raw;
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw + kLutBytes) + 1023) &
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  {
-    uint32_t* t = reinterpret_cast<uint32_t*>(smem_raw);
-    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
-      const uint32_t b = (uint32_t)i >> 5, l = (uint32_t)i & 31u;
-      t[b * 64 + l] = e2m1_f16_bits(b & 15u) | e2m1_f16_bits(b >> 4) << 16;
-    }
-  }
   const uint32_t sbase = smem_u32(smem);
   const uint32_t w_full = sbase + L::BAR_OFFSET;
   const uint32_t w_empty = w_full + WS * 8;
@@ -729,10 +713,9 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     }
   } else if (warp >= kConvWarp0 && warp < kEpiWarp0) {
     // ---------------- converters ----------------
-    const int wg = (warp - kConvWarp0) >> 2, q = warp & 3;
+    const int q = warp & 3;
     const int row = q * 32 + lane;  // weight row of this thread, also its TMEM lane
-    const uint32_t lane4 = (uint32_t)lane * 4u;
-    for (int g = wg; g < NS; g += 2) {
+    for (int g = 0; g < NS; ++g) {
       const int s = g % WS, sa = g % kAStages;
       if (!mbar_wait(w_full + 8 * s, (uint32_t)(g / WS) & 1u, 0x327)) break;
       if (!mbar_wait(a_empty + 8 * sa, ((uint32_t)(g / kAStages) & 1u) ^ 1u, 0x328)) break;
@@ -746,14 +729,14 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
         const uint32_t codes = *reinterpret_cast<const uint16_t*>(rec + kValBytes + 2 * row);
         const uint32_t m0 = pow2_f16x2(codes & 0xFFu), m1 = pow2_f16x2(codes >> 8);
         uint32_t a[32];
-        e2m1x8_to_f16x2(v0.x, lane4, lut, a + 0);
-        e2m1x8_to_f16x2(v0.y, lane4, lut, a + 4);
-        e2m1x8_to_f16x2(v0.z, lane4, lut, a + 8);
-        e2m1x8_to_f16x2(v0.w, lane4, lut, a + 12);
-        e2m1x8_to_f16x2(v1.x, lane4, lut, a + 16);
-        e2m1x8_to_f16x2(v1.y, lane4, lut, a + 20);
-        e2m1x8_to_f16x2(v1.z, lane4, lut, a + 24);
-        e2m1x8_to_f16x2(v1.w, lane4, lut, a + 28);
+        e2m1x8_to_f16x2(v0.x, a + 0);
+        e2m1x8_to_f16x2(v0.y, a + 4);
+        e2m1x8_to_f16x2(v0.z, a + 8);
+        e2m1x8_to_f16x2(v0.w, a + 12);
+        e2m1x8_to_f16x2(v1.x, a + 16);
+        e2m1x8_to_f16x2(v1.y, a + 20);
+        e2m1x8_to_f16x2(v1.z, a + 24);
+        e2m1x8_to_f16x2(v1.w, a + 28);
 #pragma unroll
         for (int c = 0; c < 16; ++c) a[c] = hmul2_bits(a[c], m0);
 #pragma unroll
@@ -1005,7 +988,7 @@ int fg_moe_gemm_mxfp4(const fg_f16* x, const void* w_packed, const fg_bf16* bias
                                  CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  const int grid = std::min(fg::num_sms(), max_items * p.n_tiles);
+  const int grid = std::min(kMoeCtasPerSm * fg::num_sms(), max_items * p.n_tiles);
   auto go = [&](auto kern, int smem) -> int {
     static bool done[3][64] = {{false}};
     int dev = 0;
