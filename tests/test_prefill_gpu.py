@@ -82,8 +82,11 @@ class _Judge:
     """Per step, on the rows being compared: greedy tokens equal wherever the
     exact model's top-2 margin clears twice the tolerance, and every logit
     within atol/rtol of the fp32 oracle or of the reference's own bf16
-    arithmetic (the bf16 oracle), or the worst deviation no more than 1.25x
-    that bf16 arithmetic's own. Dense models also keep 1 - cosine <= 1e-4.
+    arithmetic (the bf16 oracle); where a step is not, the run's worst
+    deviation must be no more than 1.25x the bf16 oracle's worst over the
+    same steps (one step's maximum is a noisy statistic, and the bf16 oracle
+    comes out slightly differently on hosts whose CPU matmul kernels differ).
+    Dense models also keep 1 - cosine <= 1e-4.
 
     MoE rows: the GPU's expert choice for every token of every pass (prefill
     chunks included) is compared with the exact model's. A differing choice
@@ -98,6 +101,7 @@ class _Judge:
         self.moe = moe
         self.rows = torch.ones(batch, dtype=torch.bool)
         self.flips = 0
+        self.err, self.ref_err, self.loose = 0.0, 0.0, []
 
     def observe(self, oracle, gpu_choice):
         """gpu_choice[layer]: the GPU's expert ids [B, k] for this position."""
@@ -116,11 +120,13 @@ class _Judge:
         r = self.rows
         got, truth, bf16 = got.float().cpu()[r], truth.float()[r], bf16.float()[r]
         err = (got - truth).abs()
-        near_truth = (err <= ATOL + RTOL * truth.abs()).all()
-        near_bf16 = ((got - bf16).abs() <= ATOL + RTOL * bf16.abs()).all()
-        ref_err = (bf16 - truth).abs().max().item() if r.any() else 0.0
-        assert near_truth or near_bf16 or err.max().item() <= 1.25 * ref_err + 1e-3, (
-            f"{what}: max-abs {err.max().item():.4f} vs reference-bf16 {ref_err:.4f}")
+        near_truth = bool((err <= ATOL + RTOL * truth.abs()).all())
+        near_bf16 = bool(((got - bf16).abs() <= ATOL + RTOL * bf16.abs()).all())
+        if r.any():
+            self.err = max(self.err, err.max().item())
+            self.ref_err = max(self.ref_err, (bf16 - truth).abs().max().item())
+        if not (near_truth or near_bf16):
+            self.loose.append(what)
         if not self.moe:
             cos = torch.nn.functional.cosine_similarity(got, truth, dim=-1).min().item()
             assert cos >= 0.9999, f"{what}: cosine {cos}"
@@ -128,6 +134,11 @@ class _Judge:
         decided = (top2[:, 0] - top2[:, 1]) > 2 * (ATOL + RTOL * top2[:, 0].abs())
         assert torch.equal(ref.argmax_lowest(got)[decided], ref.argmax_lowest(truth)[decided]), (
             f"{what}: greedy token mismatch")
+
+    def final(self):
+        assert not self.loose or self.err <= 1.25 * self.ref_err + 1e-3, (
+            f"{self.loose} outside atol/rtol; worst max-abs {self.err:.4f} vs reference-bf16 worst "
+            f"{self.ref_err:.4f}")
 
 
 def _gpu_choices(log, batch, k):
@@ -171,6 +182,7 @@ def _run(model, batch, prompt, chunk, steps=4, seed=0):
             choices = _gpu_choices(log, batch, spec.top_k)
             judge.observe(truth, [choices[(layer, 0)] for layer in range(spec.num_layers)])
         judge.check(got, lt, lb, f"decode {s} after chunk={chunk}")
+    judge.final()
     assert judge.rows.sum() * 2 >= batch, f"only {int(judge.rows.sum())} of {batch} rows clear of router ties"
     assert int(eng.kv_cache.get_seq_length()) == prompt + steps
 

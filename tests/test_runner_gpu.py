@@ -45,17 +45,24 @@ class Judge:
       truth : oracle in fp32 (the exact math the kernels approximate)
       bf16  : oracle rounding like the reference's bf16 modules
     The GPU must be as close to `truth` as the reference's own bf16
-    arithmetic is: elementwise within atol/rtol, or within 1.25x the bf16
-    oracle's own deviation (the north star's elementwise bound is at the
-    bf16 noise floor for these random-init models: the two CPU variants
-    already differ by ~0.03 max-abs after a few dozen positions)."""
+    arithmetic is: at every step elementwise within atol/rtol of `truth` or
+    of the bf16 oracle, or, over the run, a worst deviation no more than
+    1.25x the bf16 oracle's worst deviation (the north star's elementwise
+    bound is at the bf16 noise floor for these random-init models: the two
+    CPU variants already differ by ~0.03 max-abs after a few dozen
+    positions). The comparison with the bf16 oracle is made over the whole
+    run because one step's maximum over a vocabulary row is a noisy
+    statistic, and the bf16 oracle itself comes out slightly differently on
+    hosts whose CPU matmul kernels differ. Per step: cosine >= 0.9999 and
+    identical greedy tokens wherever the exact model's top-2 margin exceeds
+    twice the tolerance."""
 
     def __init__(self, model):
         spec = ref.spec_from_hf(model.config)
         w = ref.weights_from_hf(model)
         self.bf16 = ref.OracleModel(spec, w, torch.bfloat16)
         self.truth = ref.OracleModel(spec, {k: v.float() for k, v in w.items()}, torch.float32)
-        self.worst = 0.0
+        self.err, self.ref_err, self.loose = 0.0, 0.0, []
 
     def prefill(self, prompts):
         return self.truth.prefill_stepwise(prompts), self.bf16.prefill_stepwise(prompts)
@@ -66,17 +73,23 @@ class Judge:
     def check(self, got, truth, bf16, step):
         got, truth, bf16 = got.float().cpu(), truth.float(), bf16.float()
         err = (got - truth).abs()
-        ref_err = (bf16 - truth).abs().max().item()
-        excess = (err - (ATOL + RTOL * truth.abs())).max().item()
-        self.worst = max(self.worst, excess)
-        assert excess <= 0 or err.max().item() <= 1.25 * ref_err + 1e-3, (
-            f"step {step}: max-abs {err.max().item():.4f} vs reference-bf16 {ref_err:.4f}")
+        self.err = max(self.err, err.max().item())
+        self.ref_err = max(self.ref_err, (bf16 - truth).abs().max().item())
+        near_truth = bool((err <= ATOL + RTOL * truth.abs()).all())
+        near_bf16 = bool(((got - bf16).abs() <= ATOL + RTOL * bf16.abs()).all())
+        if not (near_truth or near_bf16):
+            self.loose.append(step)
         cos = torch.nn.functional.cosine_similarity(got, truth, dim=-1).min().item()
         assert cos >= 0.9999, f"step {step}: cosine {cos}"
         top2 = truth.topk(2, dim=-1).values
         decided = (top2[:, 0] - top2[:, 1]) > 2 * (ATOL + RTOL * top2[:, 0].abs())
         assert torch.equal(ref.argmax_lowest(got)[decided], ref.argmax_lowest(truth)[decided]), (
             f"step {step}: greedy token mismatch")
+
+    def final(self):
+        assert not self.loose or self.err <= 1.25 * self.ref_err + 1e-3, (
+            f"steps {self.loose} outside atol/rtol; worst max-abs {self.err:.4f} vs "
+            f"reference-bf16 worst {self.ref_err:.4f}")
 
 
 @pytest.mark.parametrize("batch,prompt,steps", [(8, 24, 32), (3, 5, 8)])
@@ -97,6 +110,7 @@ def test_llama_decode_matches_oracle(batch, prompt, steps):
         got = eng.runner.decode_step(tok.cuda()).reshape(batch, -1)
         truth, bf16 = judge.step(tok)
         judge.check(got, truth, bf16, s)
+    judge.final()
     kernels.check_device("llama decode")
 
 
