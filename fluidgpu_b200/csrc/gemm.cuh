@@ -151,13 +151,20 @@ __device__ __forceinline__ int cta_of_unit(long long U, int G, long long u) {
   return c;
 }
 
+// Tile t covers weight rows n_tile * 128.. and tokens t_tile * BN..; token
+// tiles vary fastest, so the CTAs resident at one time share few weight
+// tiles and a large-T GEMM (prefill) reads each weight tile from HBM once,
+// its other token tiles hitting L2. With one token tile (decode) t = n_tile.
+__device__ __forceinline__ int tile_n(const Params& p, int tile) { return tile / p.t_tiles; }
+__device__ __forceinline__ int tile_t(const Params& p, int tile) { return tile - (tile / p.t_tiles) * p.t_tiles; }
+
 // Epilogue of one 128 x BN tile from a value source load16(j0, v[16]) giving
 // columns j0..j0+15 of accumulator row `row` (= 32*q + lane).
 template <int BN, class Load>
 __device__ __forceinline__ void apply_epilogue(const Params& p, int tile, int q, int lane,
                                                __nv_bfloat16* xch, Load&& load16) {
-  const int n_tile = tile % p.n_tiles;
-  const int t_tile = tile / p.n_tiles;
+  const int n_tile = tile_n(p, tile);
+  const int t_tile = tile_t(p, tile);
   const int row = q * 32 + lane;
   if (p.epilogue == FG_EPI_SWIGLU) {
     // rows [0,64) hold gate features n_tile*64 + row, rows [64,128) the matching up
@@ -282,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto load_w = [&](long long u, int s) {
         const int tile = (int)(u / p.nkb);
         const int kb = (int)(u - (long long)tile * p.nkb);
-        const int n_tile = tile % p.n_tiles;
+        const int n_tile = tile_n(p, tile);
         const uint32_t dst = sbase + s * L::STAGE_BYTES;
         if (PACKED) {
           const uint8_t* src = p.w_packed + ((size_t)n_tile * p.nkb + kb) * kTileBytes;
@@ -294,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto load_x = [&](long long u, int s) {
         const int tile = (int)(u / p.nkb);
         const int kb = (int)(u - (long long)tile * p.nkb);
-        const int t_tile = tile / p.n_tiles;
+        const int t_tile = tile_t(p, tile);
         tma_load_2d_hint(sbase + s * L::STAGE_BYTES + L::A_BYTES, &tm_x, bar_full + 8 * s, kb * BK,
                          t_tile * BN, pol_x);
       };
@@ -491,8 +498,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kb0 = (p.nkb * r) / S;
   const int kb1 = (p.nkb * (r + 1)) / S;
   const int n = kb1 - kb0;
-  const int n_tile = tile % p.n_tiles;
-  const int t_tile = tile / p.n_tiles;
+  const int n_tile = tile_n(p, tile);
+  const int t_tile = tile_t(p, tile);
 
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar_full = sbase + L::BAR_OFFSET;
