@@ -161,10 +161,8 @@ __device__ __forceinline__ int tile_t(const Params& p, int tile) { return tile -
 // Epilogue of one 128 x BN tile from a value source load16(j0, v[16]) giving
 // columns j0..j0+15 of accumulator row `row` (= 32*q + lane).
 template <int BN, class Load>
-__device__ __forceinline__ void apply_epilogue(const Params& p, int tile, int q, int lane,
+__device__ __forceinline__ void apply_epilogue(const Params& p, int n_tile, int t_tile, int q, int lane,
                                                __nv_bfloat16* xch, Load&& load16) {
-  const int n_tile = tile_n(p, tile);
-  const int t_tile = tile_t(p, tile);
   const int row = q * 32 + lane;
   if (p.epilogue == FG_EPI_SWIGLU) {
     // rows [0,64) hold gate features n_tile*64 + row, rows [64,128) the matching up
@@ -390,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       if (whole) {
-        apply_epilogue<BN>(p, tile, q, lane, xch, from_tmem);
+        apply_epilogue<BN>(p, tile_n(p, tile), tile_t(p, tile), q, lane, xch, from_tmem);
       } else {
         const long long first = (long long)tile * p.nkb;
         const int c_first = cta_of_unit(U, G, first);
@@ -447,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           };
-          apply_epilogue<BN>(p, tile, q, lane, xch, from_partials);
+          apply_epilogue<BN>(p, tile_n(p, tile), tile_t(p, tile), q, lane, xch, from_partials);
           if (threadIdx.x == 64) p.tickets[tile] = 0u;  // rearm for the next call
         }
         u += nseg;
@@ -608,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
     if (S == 1) {
-      apply_epilogue<BN>(p, tile, q, lane, xch, from_tmem);
+      apply_epilogue<BN>(p, n_tile, t_tile, q, lane, xch, from_tmem);
     } else {
       // park the partial tile in this CTA's shared memory (the ring is idle:
       // every stage was consumed before the accumulator completed)
@@ -766,6 +764,18 @@ inline Plan make_plan(int T, int N, int K, int splits) {
   pl.streamk = false;
   pl.split = 1;
   pl.max_contrib = 1;
+  if (splits == 0 && pl.t_tiles >= 2 && tiles >= 2 * slots) {
+    // many tokens (prefill): a persistent grid walking whole tiles, so each
+    // CTA's epilogue overlaps its next tile's MMAs (two accumulators) and the
+    // per-tile prologue is paid once per CTA; the grid divides the tiles
+    // exactly, so no tile is split and no workspace is needed
+    for (long long g = slots; g >= slots / 2; --g) {
+      if (tiles % g == 0) {
+        splits = (int)-g;
+        break;
+      }
+    }
+  }
   if (splits < 0) {
     pl.streamk = true;
     pl.grid = (int)(-splits < pl.units ? -splits : pl.units);

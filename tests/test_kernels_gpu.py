@@ -144,6 +144,43 @@ def test_gemm_swiglu(T, I, K, splits):
     assert err <= 2e-2 * exp.abs().max().item() + 1e-4, err
 
 
+@pytest.mark.parametrize("T,N,K,epi", [(512, 36864, 128, 0),   # 576 tiles: 144 persistent CTAs x 4
+                                        (520, 25600, 192, 1),   # residual + bias, ragged last token tile
+                                        (512, 19200, 128, 2)])  # SwiGLU, 300 tiles: 100 CTAs x 3
+@pytest.mark.parametrize("packed", [True, False])
+def test_gemm_many_tokens_persistent(T, N, K, epi, packed):
+    """Many tokens (prefill): the automatic plan takes the persistent kernel
+    over whole tiles (a grid dividing the tile count, no workspace); per tile
+    its MMAs run over K in the same order as the one-tile-per-CTA kernel
+    (splits=1), so both give the same bits, and both match fp32."""
+    from fluidgpu_b200 import _lib, kernels
+
+    g = _gen(9)
+    x = _randn((T, K), g)
+    w = _randn((N, K), g, 0.05)
+    b = _randn((N,), g, 0.1) if epi == 1 else None
+    r = _randn((T, N), g) if epi == 1 else None
+    wd = kernels.PackedWeight(w.to(DEV)) if packed else w.to(DEV)
+    kw = dict(epilogue=epi, residual=None if r is None else r.to(DEV), bias=None if b is None else b.to(DEV))
+    lib = _lib.lib()
+    tiles = (N + 127) // 128 * ((T + 255) // 256)
+    grid = lib.fg_gemm_grid(T, N, K, 0)
+    assert grid <= 148 and tiles % grid == 0 and lib.fg_gemm_workspace_bytes(T, N, K, 0) == 0, (grid, tiles)
+    many = kernels.gemm(x.to(DEV), wd, splits=0, **kw).cpu()
+    one = kernels.gemm(x.to(DEV), wd, splits=1, **kw).cpu()
+    assert torch.equal(many, one)
+    acc = _gemm_ref(x, w, b)
+    if epi == 0:
+        exp = acc
+    elif epi == 1:
+        exp = r.float() + acc.to(torch.bfloat16).float()
+    else:
+        gu = acc.to(torch.bfloat16).view(T, N // 128, 2, 64)
+        exp = ref.silu_mul(gu[:, :, 0].reshape(T, -1), gu[:, :, 1].reshape(T, -1)).float()
+    err = (many.float() - exp).abs().max().item()
+    assert err <= 2e-2 * exp.abs().max().item() + 1e-3, err
+
+
 def test_pack_weight_layout():
     """Packed tile (nt, kb): 16-byte chunk c of row r sits at chunk c ^ (r % 8)."""
     from fluidgpu_b200 import kernels
