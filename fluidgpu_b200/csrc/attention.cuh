@@ -91,7 +91,10 @@ struct Layout {
 };
 
 template <int HD, int STAGES>
-__global__ void __launch_bounds__(kThreads, 3) paged_attn_kernel(
+// four resident CTAs per SM at hd 64 (96 registers): a 2 KB page per K or V
+// tile leaves a CTA with half the bytes per page step of hd 128, so more CTAs
+// keep the same bytes in flight; hd 128 fits three (128 registers)
+__global__ void __launch_bounds__(kThreads, HD == 64 ? 4 : 3) paged_attn_kernel(
     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
     const Params p) {
   using L = Layout<HD, STAGES>;
