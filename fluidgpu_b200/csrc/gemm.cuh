@@ -764,12 +764,14 @@ inline Plan make_plan(int T, int N, int K, int splits) {
   pl.streamk = false;
   pl.split = 1;
   pl.max_contrib = 1;
-  if (splits == 0 && pl.t_tiles >= 2 && tiles >= 2 * slots) {
+  if (splits == 0 && pl.t_tiles >= 2 && tiles >= slots) {
     // many tokens (prefill): a persistent grid walking whole tiles, so each
     // CTA's epilogue overlaps its next tile's MMAs (two accumulators) and the
     // per-tile prologue is paid once per CTA; the grid divides the tiles
-    // exactly, so no tile is split and no workspace is needed
-    for (long long g = slots; g >= slots / 2; --g) {
+    // exactly, so no tile is split and no workspace is needed. Below two
+    // waves of tiles the grid must still cover most SMs.
+    const long long g_min = tiles >= 2 * slots ? slots / 2 : (slots * 4) / 5;
+    for (long long g = slots; g >= g_min; --g) {
       if (tiles % g == 0) {
         splits = (int)-g;
         break;

@@ -81,7 +81,7 @@ class FluidRunner:
         # scratch slots of this runner (runners on other streams use their own)
         self.slot = f"runner{id(self):x}"
         # positions per sequence in one prefill pass (bounded by activation memory)
-        self.prefill_chunk = 512
+        self.prefill_chunk = 1024
         # MoE routing of the last step per layer (tests compare it with the oracle)
         self.record_routing = False
         self.last_routing: dict[int, torch.Tensor] = {}
