@@ -281,6 +281,10 @@ def make_forward_impl(remote: ExpertsOnDevice, home: str | torch.device, stable_
     if local is not None:
         assert local.partial and remote.partial and local.expert_range[1] == remote.expert_range[0], (
             "a split needs local experts [0, n) and remote experts [n, E)")
+        assert local.expert_range[0] == 0 and remote.expert_range[1] == remote.num_experts, (
+            "the two halves of a split must cover every expert")
+    else:
+        assert not remote.partial, "experts of a sub-range need the home half (local=) to make the full output"
 
     def forward_impl(layer: Any, hidden_states: torch.Tensor, router_logits: torch.Tensor,
                      shared_experts_input: torch.Tensor | None = None,
@@ -300,8 +304,6 @@ def make_forward_impl(remote: ExpertsOnDevice, home: str | torch.device, stable_
             with torch.cuda.device(home):
                 return _sum_partials([part_local, part_remote], home, dst)
         out = remote.forward_on_device(x, lg)
-        if remote.partial:  # a lone partial: the caller owns the other experts
-            return out
         if stable_out is None:
             return hop_tensor(out, home)
         return stable_out.stage(out, ub)
