@@ -21,7 +21,7 @@ operand is a K-major TMA source):
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass, field, replace
+from dataclasses import dataclass, field
 from typing import Any
 
 import torch
@@ -84,13 +84,6 @@ class ModelSpec:
             return rope_mod.llama3(self.head_dim, self.rope_theta, r["factor"], r["low_freq_factor"],
                                    r["high_freq_factor"], r["original_max_position_embeddings"])
         return rope_mod.default(self.head_dim, self.rope_theta)
-
-    def weight_bytes(self) -> int:
-        """bf16 bytes one decode step streams (dense), or the bf16 non-expert part."""
-        H, I = self.hidden, self.intermediate
-        attn = (self.qkv_width + self.n_q * self.head_dim) * H
-        ffn = 0 if self.moe else 3 * H * I
-        return 2 * (self.num_layers * (attn + ffn) + self.vocab * H)
 
 
 # Config 1 of the benchmark description (CPU-runnable reference case).
@@ -283,5 +276,3 @@ class ModelWeights:
         return out.finalize()
 
 
-def scaled_spec(spec: ModelSpec, **kw: Any) -> ModelSpec:
-    return replace(spec, **kw)

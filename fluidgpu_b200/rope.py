@@ -59,21 +59,3 @@ def yarn(head_dim: int, theta: float, factor: float, original_max: int, beta_fas
     inv = interpolated * (1 - keep_extrapolated) + extrapolated * keep_extrapolated
     scale = attention_factor if attention_factor is not None else 0.1 * math.log(factor) + 1.0
     return inv, float(scale)
-
-
-def from_hf_config(cfg) -> tuple[torch.Tensor, float]:
-    """inv_freq and attention scaling for a transformers config object."""
-    head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
-    params = getattr(cfg, "rope_parameters", None) or getattr(cfg, "rope_scaling", None) or {}
-    theta = params.get("rope_theta", getattr(cfg, "rope_theta", 10000.0))
-    kind = params.get("rope_type", params.get("type", "default")) or "default"
-    if kind == "default":
-        return default(head_dim, theta)
-    if kind == "llama3":
-        return llama3(head_dim, theta, params["factor"], params["low_freq_factor"],
-                      params["high_freq_factor"], params["original_max_position_embeddings"])
-    if kind == "yarn":
-        return yarn(head_dim, theta, params["factor"], params["original_max_position_embeddings"],
-                    params.get("beta_fast", 32.0) or 32.0, params.get("beta_slow", 1.0) or 1.0,
-                    params.get("truncate", True), params.get("attention_factor"))
-    raise AssertionError(f"unsupported rope_type {kind}")
