@@ -69,3 +69,31 @@ def test_no_cluster_multicast_anywhere():
     for p in list((ROOT / "fluidgpu_b200" / "csrc").rglob("*")) + [ROOT / "include" / "fgb200.h"]:
         if p.is_file():
             assert pat not in p.read_text(), p
+
+
+@pytest.mark.parametrize("T,N,K", [(64, 6144, 4096), (64, 4096, 4096), (64, 28672, 4096), (64, 4096, 14336),
+                                   (128, 5760, 2880), (1, 128256, 4096)])
+def test_gemm_plan_decode_sizes(lib_path, T, N, K):
+    """Decode sizes (one token tile): one CTA per tile or split-K clusters,
+    never a workspace (planning queries run without a GPU; 148 SMs assumed)."""
+    from fluidgpu_b200 import _lib
+
+    lib = _lib.lib()
+    tiles = (N + 127) // 128
+    assert lib.fg_gemm_grid(T, N, K, 0) == tiles
+    assert lib.fg_gemm_workspace_bytes(T, N, K, 0) == 0
+
+
+@pytest.mark.parametrize("T,N,K,grid", [(2048, 28672, 4096, 128), (4096, 4096, 14336, 128),
+                                        (512, 28672, 4096, 112), (2048, 4096, 4096, 128),
+                                        (512, 19200, 128, 100)])
+def test_gemm_plan_prefill_sizes(lib_path, T, N, K, grid):
+    """Many tokens: a persistent grid that divides the tile count (whole tiles
+    per CTA, no split tile, so no workspace)."""
+    from fluidgpu_b200 import _lib
+
+    lib = _lib.lib()
+    tiles = (N + 127) // 128 * ((T + 255) // 256)
+    g = lib.fg_gemm_grid(T, N, K, 0)
+    assert g == grid and tiles % g == 0
+    assert lib.fg_gemm_workspace_bytes(T, N, K, 0) == 0
