@@ -20,7 +20,6 @@ operand is a K-major TMA source):
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass, field
 from typing import Any
 

@@ -11,7 +11,6 @@
 - Three ranks: a tensor-parallel FFN over two ranks, partials added up on the
   attention rank, within the bf16 tolerance of a co-located run.
 Multi-GPU cases are skipped on a box with fewer GPUs."""
-import ctypes
 import os
 import socket
 import traceback

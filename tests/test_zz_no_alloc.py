@@ -7,7 +7,6 @@ while the split scratch lives in the library's built-in device array.
 Kept in a file of its own that pytest collects last, so a failure here cannot
 stop the rest of a `-x` run; it passes alone in a fresh process and after the
 other tests (the first call on the device resolves the array's address)."""
-import ctypes
 import math
 
 import pytest
