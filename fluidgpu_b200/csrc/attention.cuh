@@ -35,6 +35,9 @@ constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegBig = -1.0e30f;
 constexpr int kMinSlice = 8;   // fewest pages a split slice is given
+constexpr int kMaxSplits = 128;  // most slices plan_splits gives one (sequence, kv head)
+constexpr int kCombineThreads = 512;  // a multiple of every supported head dim
+constexpr int kSerialSplits = 8;      // up to this many, the combine walks splits in order
 
 struct Params {
   const __nv_bfloat16* q;   // [B][nq][hd]
@@ -348,24 +351,78 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 4 : 3) paged_attn_kernel(
   }
 }
 
-// merge split partials: grid (nq, B), block = hd threads
-__global__ void attn_combine_kernel(const Params p, int hd) {
+// block-wide max (kMax) or sum of one float per thread; every thread gets the
+// same value, combined in one fixed order
+template <bool kMax>
+__device__ __forceinline__ float block_reduce(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = kMax ? fmaxf(v, w) : v + w;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int i = 1; i < (int)(blockDim.x >> 5); ++i) r = kMax ? fmaxf(r, red[i]) : r + red[i];
+  __syncthreads();  // red is reused by the next call
+  return r;
+}
+
+// merge split partials: grid (nq, B), block a multiple of hd that covers every
+// split (at most kCombineThreads). Up to kSerialSplits splits, one group of hd
+// threads each walks the splits in order. Beyond that, thread s reads split s's
+// running max and denominator (two block reductions give the global max and
+// the rescaled denominator) and the weighted partial outputs are summed by
+// blockDim / hd groups of hd threads over interleaved splits, so no thread
+// walks all splits one dependent load at a time; the groups are added in index
+// order (the result does not depend on timing)
+__global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const Params p, int hd) {
+  __shared__ float s_f[kMaxSplits];
+  __shared__ float s_red[kCombineThreads / 32];
+  __shared__ float s_o[kCombineThreads];
   griddep_wait();
   griddep_launch_dependents();
-  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
-  const int64_t base = ((int64_t)b * p.nq + h) * p.splits;
-  float M = kNegBig;
-  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.part_ml[2 * (base + s)]);
-  float lsum = p.sinks ? exp2f(p.sinks[h] * kLog2e - M) : 0.f;
-  float osum = 0.f;
-  for (int s = 0; s < p.splits; ++s) {
-    const float m = p.part_ml[2 * (base + s)];
-    if (m <= kNegBig) continue;
-    const float f = exp2f(m - M);
-    lsum += p.part_ml[2 * (base + s) + 1] * f;
-    osum += p.part_o[(base + s) * hd + d] * f;
+  const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+  const int S = p.splits;
+  const int64_t base = ((int64_t)b * p.nq + h) * S;
+  const float* ml = p.part_ml + 2 * base;
+  if (S <= kSerialSplits) {
+    float M = kNegBig;
+    for (int s = 0; s < S; ++s) M = fmaxf(M, ml[2 * s]);
+    float lsum = p.sinks ? exp2f(p.sinks[h] * kLog2e - M) : 0.f;
+    float osum = 0.f;
+    for (int s = 0; s < S; ++s) {
+      const float m = ml[2 * s];
+      if (m <= kNegBig) continue;  // empty slice
+      const float f = exp2f(m - M);
+      lsum += ml[2 * s + 1] * f;
+      osum += p.part_o[(base + s) * hd + t] * f;
+    }
+    p.out[((int64_t)b * p.nq + h) * hd + t] = f2bf(lsum > 0.f ? osum / lsum : 0.f);
+    return;
   }
-  p.out[((int64_t)b * p.nq + h) * hd + d] = f2bf(lsum > 0.f ? osum / lsum : 0.f);
+  const float m = t < S ? ml[2 * t] : kNegBig;
+  const float l = t < S ? ml[2 * t + 1] : 0.f;
+  const float M = block_reduce<true>(m, s_red);
+  const float f = m <= kNegBig ? 0.f : exp2f(m - M);  // empty slices carry nothing
+  float lsum = block_reduce<false>(l * f, s_red);
+  if (p.sinks) lsum += exp2f(p.sinks[h] * kLog2e - M);
+  if (t < S) s_f[t] = f;
+  __syncthreads();
+  const int d = t % hd, grp = t / hd, ngrp = (int)blockDim.x / hd;
+  float o = 0.f;
+#pragma unroll 4
+  for (int s = grp; s < S; s += ngrp) {
+    const float fs = s_f[s];
+    if (fs != 0.f) o += p.part_o[(base + s) * hd + d] * fs;
+  }
+  s_o[t] = o;
+  __syncthreads();
+  if (grp == 0) {
+    float acc = 0.f;
+    for (int g2 = 0; g2 < ngrp; ++g2) acc += s_o[g2 * hd + d];
+    p.out[((int64_t)b * p.nq + h) * hd + d] = f2bf(lsum > 0.f ? acc / lsum : 0.f);
+  }
 }
 
 // resident CTAs per SM of the attention kernel for head dim `hd` (sets the
@@ -410,7 +467,7 @@ inline int plan_splits(int B, int nkv, int hd, int max_seq_len, int window) {
   const double slots = (double)(occ > 0 ? occ : 2) * num_sms();
   const double pairs = (double)B * nkv;
   int max_s = pages / kMinSlice;
-  if (max_s > 128) max_s = 128;
+  if (max_s > kMaxSplits) max_s = kMaxSplits;
   if (max_s < 1) max_s = 1;
   int best_s = 1;
   double best = -1.0;
@@ -437,8 +494,15 @@ int launch(const Params& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaSt
   int rc = launch_k("fg_paged_decode_attn", kern, dim3(p.splits, p.nkv, p.B), dim3(kThreads),
                     L::DYN_SMEM, st, tk, tv, p);
   if (rc || p.splits == 1) return rc;
-  return launch_k("fg_paged_decode_attn(combine)", attn_combine_kernel, dim3(p.nq, p.B), dim3(HD), 0,
-                  st, p, HD);
+  // one group of HD threads for a few splits; beyond that about eight splits
+  // per group, at least one thread per split, at most kCombineThreads threads
+  static_assert(kCombineThreads % HD == 0 && kMaxSplits <= kCombineThreads, "combine block shape");
+  static_assert(kSerialSplits <= HD, "the serial form has one group");
+  const int ngrp = p.splits <= kSerialSplits
+                       ? 1
+                       : min(kCombineThreads / HD, max((p.splits + HD - 1) / HD, (p.splits + 7) / 8));
+  return launch_k("fg_paged_decode_attn(combine)", attn_combine_kernel, dim3(p.nq, p.B),
+                  dim3(HD * ngrp), 0, st, p, HD);
 }
 
 // ---------------------------------------------------------------------------

@@ -252,6 +252,7 @@ def _gather(cache, table, b, L):
         (2, 64, 8, 64, [1000, 7], 0, True),
         (5, 32, 8, 128, [4096, 4000, 2048, 17, 4097], 0, False),
         (1, 32, 8, 128, [32768], 0, False),
+        (1, 64, 8, 64, [30000], 0, True),
         (8, 4, 2, 64, [20, 21, 22, 23, 24, 25, 26, 27], 2, False),
     ],
 )
