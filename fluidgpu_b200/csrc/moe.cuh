@@ -429,18 +429,23 @@ __global__ void pack_mxfp4_kernel(const uint8_t* __restrict__ vals, const uint8_
 //
 // Persistent: two CTAs per SM walk the work units (permute item x 128-row
 // tile) u = blockIdx.x + j * gridDim.x; a unit's K runs in steps of two
-// 64-wide records. 12 warps:
+// 64-wide records. 16 warps:
 //   warp 0       weight producer: one bulk copy per step into a ring
-//   warp 2       activation producer: the step's 2-D TMA tiles into the
-//                activation stage paired with the step's A stage
+//   warp 2       activation producer: the step's 2-D TMA tiles into an
+//                activation ring of its own, deeper than the A stages
+//                (XS > AST; measured faster than sharing their indices)
 //   warp 1       TMEM owner and MMA issuer (8 x K16 per step into one of
 //                two accumulators, so the epilogue overlaps the next unit);
-//                the commit frees the A stage and its activation stage
-//                together, and the converters hold a_full until the
-//                activation tile has landed
-//   warps 4-7    converters: a thread per weight row decodes its 128 values
-//                of the step into a TMEM A stage (tcgen05.st)
-//   warps 8-11   epilogue: accumulator x 2^(s_ref-127) + bias, SwiGLU-OAI
+//                one commit per step frees the A stage, and the converters
+//                hold a_full until the activation tile has landed
+//   warps 4-11   converters, two warpgroups taking alternate steps (one
+//                group's serial read -> store -> arrive chain per step was
+//                the bound with one): a thread per weight row decodes its
+//                128 values of the step into a TMEM A stage (tcgen05.st); the thread
+//                that sees an A stage freed also frees that step's
+//                activation stage (x_empty), so the MMA thread still takes
+//                one wait and one commit per step
+//   warps 12-15  epilogue: accumulator x 2^(s_ref-127) + bias, SwiGLU-OAI
 //                (gate rows 0-63 of a tile, up rows 64-127; f16 out) or
 //                store (bf16 out)
 // ---------------------------------------------------------------------------
@@ -456,8 +461,9 @@ struct GemmParams {
 };
 
 constexpr int kConvWarp0 = 4;
-constexpr int kEpiWarp0 = 8;
-constexpr int kMoeWarps = 12;
+constexpr int kConvGroups = 2;  // converter warpgroups, taking alternate steps
+constexpr int kEpiWarp0 = kConvWarp0 + 4 * kConvGroups;
+constexpr int kMoeWarps = kEpiWarp0 + 4;
 constexpr int kMoeThreads = kMoeWarps * 32;
 constexpr int kMoeCtasPerSm = 2;
 
@@ -466,21 +472,23 @@ struct MLayout {
   static constexpr int KS = 2;                                      // records per step
   static constexpr int AST = BN <= 32 ? 3 : 2;                     // TMEM A stages of KS * 32 columns
   static constexpr int DCOL0 = AST * KS * 32;                      // two accumulators of BN columns follow
-  static constexpr int WS = 8;                                     // weight ring (steps)
-  // activation ring: one stage per A stage, freed by the same MMA commit
-  static constexpr int XS = AST;
+  // weight ring (steps) and activation ring (steps, deeper than the A stages;
+  // shared memory for two CTAs per SM bounds the pair)
+  static constexpr int WS = BN == 16 ? 8 : 6;
+  static constexpr int XS = BN == 64 ? 3 : 6;
   static constexpr int X_TILE = BN * BK * 2;                       // [BN][64] f16, 128B swizzle
   static constexpr int X_STAGE = KS * X_TILE;
   static constexpr int W_STAGE = KS * kRecBytes;
   static constexpr int W_OFFSET = XS * X_STAGE;
   static constexpr int XCH_OFFSET = W_OFFSET + WS * W_STAGE;       // bf16 [BN][64]
   static constexpr int BAR_OFFSET = (XCH_OFFSET + BN * 64 * 2 + 7) / 8 * 8;
-  // w_full[WS] w_empty[WS] x_full[XS] a_full[A] a_empty[A] acc_full[2] acc_empty[2] mma_done
-  static constexpr int MISC_OFFSET = BAR_OFFSET + (2 * WS + XS + 2 * AST + 5) * 8;
+  // w_full[WS] w_empty[WS] x_full[XS] x_empty[XS] a_full[A] a_empty[A] acc_full[2] acc_empty[2] mma_done
+  static constexpr int MISC_OFFSET = BAR_OFFSET + (2 * WS + 2 * XS + 2 * AST + 5) * 8;
   static constexpr int TOTAL = MISC_OFFSET + 16;
   static constexpr int DYN_SMEM = TOTAL + 1024;  // + slack for the 1024-byte alignment
   static constexpr uint32_t TMEM_COLS = 256;     // half of the SM's: two CTAs per SM
   static_assert(X_TILE % 1024 == 0 && kRecBytes % 16 == 0, "stage alignment");
+  static_assert(XS >= AST, "a step's activation stage is released after its A stage");
   static_assert(DCOL0 + 2 * BN <= (int)TMEM_COLS, "tensor memory budget");
   static_assert(kMoeCtasPerSm * (DYN_SMEM + 1024) <= 233472, "shared memory budget (two CTAs per SM)");
 };
@@ -573,7 +581,8 @@ __global__ void __launch_bounds__(kMoeThreads, kMoeCtasPerSm)
   const uint32_t w_full = sbase + L::BAR_OFFSET;
   const uint32_t w_empty = w_full + WS * 8;
   const uint32_t x_full = w_empty + WS * 8;
-  const uint32_t a_full = x_full + XS * 8;
+  const uint32_t x_empty = x_full + XS * 8;
+  const uint32_t a_full = x_empty + XS * 8;
   const uint32_t a_empty = a_full + kAStages * 8;
   const uint32_t acc_full = a_empty + kAStages * 8;
   const uint32_t acc_empty = acc_full + 2 * 8;
@@ -589,6 +598,7 @@ __global__ void __launch_bounds__(kMoeThreads, kMoeCtasPerSm)
     }
     for (int s = 0; s < XS; ++s) {
       mbar_init(x_full + 8 * s, 1);
+      mbar_init(x_empty + 8 * s, 1);  // one converter thread relays the MMA commit
     }
     for (int s = 0; s < kAStages; ++s) {
       mbar_init(a_full + 8 * s, 4);
@@ -660,9 +670,8 @@ __global__ void __launch_bounds__(kMoeThreads, kMoeCtasPerSm)
         const Unit w = unit_of(p, blockIdx.x + j * G, BN);
         for (int t = 0; t < nsteps; ++t, ++g) {
           const int s = g % XS;
-          // stage s is free once the MMAs of step g - XS have completed (their
-          // commit releases A stage s and activation stage s together)
-          if (!mbar_wait(a_empty + 8 * s, ((uint32_t)(g / XS) & 1u) ^ 1u, 0x322)) {
+          // stage s is free once the MMAs of step g - XS have completed
+          if (!mbar_wait(x_empty + 8 * s, ((uint32_t)(g / XS) & 1u) ^ 1u, 0x322)) {
             ok = false;
             break;
           }
@@ -689,7 +698,9 @@ __global__ void __launch_bounds__(kMoeThreads, kMoeCtasPerSm)
         for (int t = 0; t < nsteps; ++t, ++g) {
           const int sa = g % kAStages, sx = g % XS;
           // a_full also covers the step's activation tile: a converter saw
-          // x_full before arriving (one wait per step on this thread)
+          // x_full before arriving (one wait per step on this thread); the
+          // commit below frees the A stage, and through a converter the
+          // activation stage
           if (!mbar_wait(a_full + 8 * sa, (uint32_t)(g / kAStages) & 1u, 0x324)) {
             ok = false;
             break;
@@ -713,13 +724,18 @@ __global__ void __launch_bounds__(kMoeThreads, kMoeCtasPerSm)
     }
   } else if (warp >= kConvWarp0 && warp < kEpiWarp0) {
     // ---------------- converters ----------------
+    // each warpgroup takes every kConvGroups-th step, so that many steps'
+    // shared-memory reads and TMEM stores are in flight at once
     const int q = warp & 3;
     const int row = q * 32 + lane;  // weight row of this thread, also its TMEM lane
-    for (int g = 0; g < NS; ++g) {
+    for (int g = (warp - kConvWarp0) >> 2; g < NS; g += kConvGroups) {
       const int s = g % WS, sa = g % kAStages;
       if (!mbar_wait(w_full + 8 * s, (uint32_t)(g / WS) & 1u, 0x327)) break;
       if (!mbar_wait(a_empty + 8 * sa, ((uint32_t)(g / kAStages) & 1u) ^ 1u, 0x328)) break;
       gemm::tc_fence_after();
+      // that wait saw the MMAs of step g - AST complete: their activation
+      // stage may be refilled
+      if (q == 0 && lane == 0 && g >= kAStages) mbar_arrive(x_empty + 8 * ((g - kAStages) % XS));
       const int cnt = step_count(g % nsteps);
       for (int kk = 0; kk < cnt; ++kk) {
         // weight row `row` of record kk: 64 e2m1 values -> 32 f16x2 columns
@@ -748,7 +764,7 @@ __global__ void __launch_bounds__(kMoeThreads, kMoeCtasPerSm)
       // the step's activation tile must have landed before a_full releases the MMA
       if (q == 0) {
         int ok = 1;
-        if (lane == 0) ok = mbar_wait(x_full + 8 * sa, (uint32_t)(g / XS) & 1u, 0x325) ? 1 : 0;
+        if (lane == 0) ok = mbar_wait(x_full + 8 * (g % XS), (uint32_t)(g / XS) & 1u, 0x325) ? 1 : 0;
         if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       }
       __syncwarp();
