@@ -97,3 +97,32 @@ def test_gemm_plan_prefill_sizes(lib_path, T, N, K, grid):
     g = lib.fg_gemm_grid(T, N, K, 0)
     assert g == grid and tiles % g == 0
     assert lib.fg_gemm_workspace_bytes(T, N, K, 0) == 0
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_attn_split_plan_bounds(lib_path, hd):
+    """Attention split plan (planning queries run without a GPU): 1..128 slices
+    per (sequence, kv head), at least 8 pages of 16 tokens per slice, a window
+    bounding the span, and split scratch exactly when there is more than one
+    slice (the merge kernel holds one factor per slice for up to 128)."""
+    from fluidgpu_b200 import _lib
+
+    lib = _lib.lib()
+    nq, nkv = (64, 8) if hd == 64 else (32, 8)
+    for B in (1, 2, 7, 32, 64, 128, 256):
+        for ctx in (1, 16, 129, 512, 4096, 32768, 131072):
+            for window in (0, 128):
+                s = lib.fg_attn_splits(B, nkv, hd, ctx, window)
+                span = min(ctx, window + 16) if window else ctx
+                pages = (span + 15) // 16
+                assert 1 <= s <= 128, (B, ctx, window, s)
+                assert s == 1 or s <= pages // 8, (B, ctx, window, s)
+                ws = lib.fg_attn_workspace_bytes(B, nq, nkv, hd, ctx, window)
+                if s == 1:
+                    assert ws == 0
+                else:
+                    rows = B * nq * s
+                    assert ws == ((rows * hd * 4 + 255) // 256) * 256 + rows * 2 * 4
+    # batch 1 at long context spreads one sequence over many slices
+    assert lib.fg_attn_splits(1, nkv, hd, 32768, 0) > 8
+    assert lib.fg_attn_splits(1, nkv, hd, 32768, 128) <= 2
