@@ -76,25 +76,37 @@ class ClockSampler:
     def __init__(self, gpu_index: int) -> None:
         self.gpu = gpu_index
         self.proc = None
+        self.out = None
         self.path = Path(f"/tmp/fgb200_clocks_{os.getpid()}.csv")
 
     def start(self) -> None:
         try:
+            self.out = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-i", str(self.gpu), "-lms", "200"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                stdout=self.out, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            self._close()
+            self.path.unlink(missing_ok=True)
+
+    def _close(self) -> None:
+        if self.out is not None:
+            self.out.close()
+            self.out = None
 
     def stop(self) -> dict:
         if self.proc is None:
+            self._close()
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
+            self.proc.wait(timeout=5)
+        self._close()
         rows = []
         for line in self.path.read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
