@@ -9,6 +9,10 @@ QueueComm   : ranks as threads joined by queues (the reference tests' pattern,
 P2PComm     : ranks as processes on one NVLink node. Sends are stores into
               the receiver's mailbox over NVLink plus a sequence flag
               (fg_handoff_put / fg_handoff_recv), no NCCL on the data path.
+ProcessGroupComm : the reference's own backend, torch.distributed send /
+              recv / broadcast on a process group (NCCL for CUDA tensors, the
+              baseline the NVLink hand-off replaces; gloo for CPU tensors, so
+              the multi-process protocol is testable without a GPU).
 """
 from __future__ import annotations
 
@@ -237,3 +241,30 @@ class P2PComm:
         self._mb.close()
         if self._dmb is not None:
             self._dmb.close()
+
+
+@dataclass(frozen=True)
+class ProcessGroupComm:
+    """torch.distributed point-to-point comm (fluidgpu_torch/comm.py:14-61).
+    Ranks are global ranks, as the plan's are; `group` restricts the
+    collective (broadcast) and names the group the sends use."""
+
+    group: object = None
+
+    def get_rank(self) -> int:
+        return torch.distributed.get_rank()
+
+    def get_world_size(self) -> int:
+        return torch.distributed.get_world_size(self.group)
+
+    def send_tensor(self, t: torch.Tensor, dst: int) -> None:
+        assert t.is_contiguous(), "send requires a contiguous tensor"
+        torch.distributed.send(t, dst=dst, group=self.group)
+
+    def recv_tensor(self, out: torch.Tensor, src: int) -> None:
+        assert out.is_contiguous(), "recv requires a contiguous tensor"
+        torch.distributed.recv(out, src=src, group=self.group)
+
+    def broadcast_tensor(self, t: torch.Tensor, src: int = 0) -> None:
+        assert t.is_contiguous(), "broadcast requires a contiguous tensor"
+        torch.distributed.broadcast(t, src=src, group=self.group)
