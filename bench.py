@@ -133,6 +133,17 @@ def attn_bytes(meta: dict, lens_sum: int) -> float:
     return 2.0 * nkv * hd * 2 * lens_sum + 2.0 * B * nq * hd * 2
 
 
+def prompt_lengths(batch: int, context: int, mix: str, seed: int = 0) -> list[int]:
+    """Prompt length of each sequence: all `context` ("fixed"), or seeded
+    uniform in [128, context] ("uniform", config 4's request mix)."""
+    if mix == "fixed":
+        return [context] * batch
+    assert mix == "uniform", f"unknown prompt mix {mix!r}"
+    lo = min(128, context)
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(lo, context + 1, (batch,), generator=g).tolist()
+
+
 def cpu_baseline_sample(batch: int, context: int) -> dict:
     from oracle.cpu_baseline import LayerSample, host_threads, time_sample
     from fluidgpu_b200.model import LLAMA3_8B as S
@@ -210,7 +221,7 @@ def run_fgb200(args) -> None:
                        max_batch=B, cuda_graph_decode=not args.eager)
     weights = ModelWeights.random(spec, seed=0, device=dev)
     eng = DecodeEngine(weights, cfg)
-    eng.start(B, prompt_lens=[ctx] * B, reserve_tokens=total)
+    eng.start(B, prompt_lens=prompt_lengths(B, ctx, args.prompt_mix, seed=rank), reserve_tokens=total)
     g = torch.Generator(device=dev).manual_seed(1 + rank)
     eng.kv_cache.pool.normal_(0.0, 1.0, generator=g)
     eng._tok_dev.copy_(torch.randint(0, spec.vocab, (B,), generator=g, device=dev))
@@ -313,7 +324,9 @@ def run_fgb200(args) -> None:
             "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {**config, "batch_per_gpu": B,
-                       "parallelism": f"dp{world} (attention data-parallel by request, FFN co-located)"},
+                       "parallelism": f"dp{world} (attention data-parallel by request, FFN co-located)",
+                       **({"prompt_lens": f"uniform [128, {ctx}], seeded per rank"}
+                          if args.prompt_mix == "uniform" else {})},
             "e2e": {"value": world * B * K / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8},
             "roofline": {"bound": "hbm", "kernel": "fg_paged_decode_attn", "achieved": achieved,
@@ -396,8 +409,8 @@ def run_disagg(args) -> None:
              for a in mine for m in range(M)}
     pps = [PingPongEngine(weights, cfg, prof, lambda m, a=a: comms[(a, m)], micro_batches=M) for a in mine]
     g = torch.Generator(device=dev).manual_seed(1)
-    for pp in pps:
-        pp.start(B, prompt_lens=[ctx] * B, reserve_tokens=total)
+    for a, pp in zip(mine, pps):
+        pp.start(B, prompt_lens=prompt_lengths(B, ctx, args.prompt_mix, seed=a), reserve_tokens=total)
         for eng in pp.engines:
             if eng.kv_cache.pool is not None:
                 eng.kv_cache.pool.normal_(0.0, 1.0, generator=g)
@@ -440,7 +453,9 @@ def run_disagg(args) -> None:
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {**base_cfg, "batch_per_micro_batch": B, "micro_batches": M,
                        "attention_ranks": len(attn_ranks), "ffn_ranks": len(ffn_ranks),
-                       "parallelism": par + ", NVLink hand-offs, ping-pong"},
+                       "parallelism": par + ", NVLink hand-offs, ping-pong",
+                       **({"prompt_lens": f"uniform [128, {ctx}], seeded per attention rank"}
+                          if args.prompt_mix == "uniform" else {})},
             "mode": mode,
         }
         print(json.dumps(line), flush=True)
@@ -469,6 +484,9 @@ def main() -> None:
                     help="N>1: independent co-located replicas (default); attention/FFN disaggregation "
                          "(disagg: 2 GPUs; tp: dense FFN tensor-parallel; ep: gpt-oss experts split)")
     ap.add_argument("--micro-batches", type=int, default=2, help="ping-pong micro-batches (disagg)")
+    ap.add_argument("--prompt-mix", default="fixed", choices=["fixed", "uniform"],
+                    help="prompt lengths: all --context (default), or seeded uniform in [128, --context] "
+                         "per sequence (config 4's request mix)")
     args = ap.parse_args()
     assert args.warmup >= 0 and args.steps > 0
     if args.impl == "reference":

@@ -47,3 +47,13 @@ def test_clock_sampler_without_nvidia_smi(tmp_path, monkeypatch):
     r = s.stop()
     assert r["reasons"] == ["nvidia-smi unavailable"] and r["sm_mhz"] is None
     assert s.out is None and not s.path.exists()
+
+
+def test_prompt_lengths_fixed_and_uniform():
+    assert bench.prompt_lengths(4, 4096, "fixed") == [4096] * 4
+    a = bench.prompt_lengths(256, 4096, "uniform", seed=0)
+    assert len(a) == 256 and all(128 <= x <= 4096 for x in a)
+    assert a == bench.prompt_lengths(256, 4096, "uniform", seed=0)  # seeded
+    assert a != bench.prompt_lengths(256, 4096, "uniform", seed=1)  # per rank
+    assert 1500 < sum(a) / len(a) < 2700  # mean of U[128, 4096] is 2112
+    assert bench.prompt_lengths(3, 100, "uniform") == [100] * 3  # contexts below 128
