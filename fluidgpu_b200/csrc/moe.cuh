@@ -419,13 +419,15 @@ __global__ void pack_mxfp4_kernel(const uint8_t* __restrict__ vals, const uint8_
 // streams HBM instead of saturating shared-memory bandwidth with expanded
 // tiles.
 //
-// What bounds it at decode sizes is the MMA-issuing thread: a 128 x 16 MMA
-// covers only 1088 bytes of MXFP4, and the thread's serial path per step
+// At decode sizes a 128 x 16 MMA covers only 1088 bytes of MXFP4, so the
+// serial per-step paths bound it, not bandwidth: one MMA-issuing thread's
 // (barrier wait, MMAs, commit, issue slots shared with the converters on
-// its sub-partition) costs more than the tensor pipe's ~52 cycles per MMA.
-// So the kernel is built for two resident CTAs per SM (two independent
-// issuing threads, half the tensor memory and shared memory each), and each
-// thread takes one barrier wait and one commit per step.
+// its sub-partition) costs more than the tensor pipe's ~52 cycles per MMA,
+// and one converter warpgroup's (record read, tcgen05.st, arrive) more than
+// a step's share of HBM time. So the kernel is built for two resident CTAs
+// per SM (two issuing threads, half the tensor memory and shared memory
+// each), each issuing thread takes one barrier wait and one commit per step,
+// and each CTA has two converter warpgroups on alternate steps.
 //
 // Persistent: two CTAs per SM walk the work units (permute item x 128-row
 // tile) u = blockIdx.x + j * gridDim.x; a unit's K runs in steps of two
