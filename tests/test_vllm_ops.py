@@ -104,3 +104,69 @@ def test_oracle_decode_split_adds_up():
     parts = ref.vllm_moe_experts(x, lg, w1, b1, w2, b2, k, (0, 3)) + \
         ref.vllm_moe_experts(x, lg, w1, b1, w2, b2, k, (3, E))
     torch.testing.assert_close(parts, full, rtol=1e-5, atol=1e-5)
+
+
+def _fake_worker(tp=1, eager=False, mode="PIECEWISE", splitting=None, max_seqs=48, model="/nonexistent"):
+    from fluidgpu_b200 import vllm_ops
+
+    class Mode:
+        name = mode
+
+        def has_full_cudagraphs(self):
+            return mode.startswith("FULL")
+
+    comp = SimpleNamespace(cudagraph_mode=Mode(), max_cudagraph_capture_size=256,
+                           splitting_ops=splitting if splitting is not None
+                           else [vllm_ops.MOE_FORWARD_OP, vllm_ops.REMOTE_MLP_OP])
+    cfg = SimpleNamespace(
+        parallel_config=SimpleNamespace(tensor_parallel_size=tp, pipeline_parallel_size=1),
+        compilation_config=comp,
+        model_config=SimpleNamespace(enforce_eager=eager, model=model, dtype=torch.bfloat16,
+                                     hf_config=SimpleNamespace(num_experts_per_tok=4)),
+        scheduler_config=SimpleNamespace(max_num_seqs=max_seqs))
+    return SimpleNamespace(vllm_config=cfg, model_runner=SimpleNamespace(model="MODEL"), device="cuda:0")
+
+
+def test_apply_fluid_placement_environment(monkeypatch):
+    """The worker hook reads the reference's environment variables and checks
+    vLLM's configuration the way the reference does (TP=1/PP=1, piecewise
+    graphs split at the ops) before installing anything."""
+    from fluidgpu_b200 import vllm_ops
+
+    seen = {}
+    monkeypatch.setattr(vllm_ops, "install", lambda model, **kw: seen.update(model=model, **kw) or {"moe": 1})
+    monkeypatch.delenv("FLUIDGPU_VLLM_PLACEMENT", raising=False)
+    assert vllm_ops.apply_fluid_placement(_fake_worker()) is None  # default: off
+    monkeypatch.setenv("FLUIDGPU_VLLM_PLACEMENT", "sideways")
+    with pytest.raises(AssertionError, match="unknown placement"):
+        vllm_ops.apply_fluid_placement(_fake_worker())
+    monkeypatch.setenv("FLUIDGPU_VLLM_PLACEMENT", "af")
+    with pytest.raises(AssertionError, match="TP=1/PP=1"):
+        vllm_ops.apply_fluid_placement(_fake_worker(tp=2))
+    with pytest.raises(AssertionError, match="PIECEWISE"):
+        vllm_ops.apply_fluid_placement(_fake_worker(mode="FULL_AND_PIECEWISE"))
+    with pytest.raises(AssertionError, match="splitting_ops"):
+        vllm_ops.apply_fluid_placement(_fake_worker(splitting=[]))
+    # eager mode needs no graph split
+    assert vllm_ops.apply_fluid_placement(_fake_worker(eager=True, splitting=[])) == {"moe": 1}
+    assert seen["expert_device"] == "cuda:1" and seen["decode_split"] == 0.0
+    assert seen["phase_aware"] is False and seen["decode_threshold"] == 96  # max(64, 2 x 48)
+    assert seen["home"] == "cuda:0" and seen["max_tokens"] == 256 and seen["top_k"] == 4
+    assert seen["reader"] is None and seen["model"] == "MODEL"
+    monkeypatch.setenv("FLUIDGPU_EXPERT_DEVICE", "cuda:3")
+    monkeypatch.setenv("FLUIDGPU_DECODE_SPLIT", "0.5")
+    monkeypatch.setenv("FLUIDGPU_PHASE_AWARE", "1")
+    monkeypatch.setenv("FLUIDGPU_DECODE_LOCAL_THRESHOLD", "17")
+    vllm_ops.apply_fluid_placement(_fake_worker())
+    assert seen["expert_device"] == "cuda:3" and seen["decode_split"] == 0.5
+    assert seen["phase_aware"] is True and seen["decode_threshold"] == 17
+
+
+def test_fluid_compilation_config_splits_at_the_ops():
+    pytest.importorskip("vllm.config.compilation")
+    from fluidgpu_b200 import vllm_ops
+
+    cc = vllm_ops.fluid_compilation_config()
+    assert cc["cudagraph_mode"] == "PIECEWISE"
+    assert vllm_ops.MOE_FORWARD_OP in cc["splitting_ops"] and vllm_ops.REMOTE_MLP_OP in cc["splitting_ops"]
+    assert len(cc["splitting_ops"]) == len(set(cc["splitting_ops"]))
