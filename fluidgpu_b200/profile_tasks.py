@@ -15,9 +15,12 @@ Differences from the reference's table, each forced by what is measured:
     `--prefill-len` positions (token-wise RoPE/KV append, causal prefill
     attention over the pages, GEMMs over every position), as the
     reference's whole-prompt HF forward;
-  * for MoE models the groups are layer_i_moe_router / _moe_experts /
-    _moe_combine; a layer_i_mlp row (their sum) is added for planners that
-    expect the coarse attn / mlp split.
+  * for MoE models the measured groups are layer_i_moe_router /
+    _moe_experts / _moe_combine. The table written by default has the
+    reference's task set (attn and mlp rows, profile_llm_tasks.py:94-95),
+    the mlp row being the sum of the three; `--groups moe` writes the three
+    instead. The reference's schedule_llm_layers.py plans every layer_* row
+    it reads, so a table never holds both forms of a layer.
 Weights are random (no checkpoints here); decode cost does not depend on
 their values.
 """
@@ -85,13 +88,32 @@ def measure(model: str, batch: int, context: int, decode_steps: int = 8, warmup:
         d, p = dec.get(n, []), pre.get(n, [])
         assert len(d) == decode_steps, f"{n}: {len(d)} decode samples, expected {decode_steps}"
         rows[n] = {"decode_us": statistics.median(d), "prefill_us": sum(p)}
-    if spec.moe:  # coarse rows for planners that split layers into attn / mlp only
-        for i in range(spec.num_layers):
-            parts = [rows[f"layer_{i}_{s}"] for s in ("moe_router", "moe_experts", "moe_combine")]
-            rows[f"layer_{i}_mlp"] = {k: sum(p[k] for p in parts) for k in ("decode_us", "prefill_us")}
-            names.insert(names.index(f"layer_{i}_moe_combine") + 1, f"layer_{i}_mlp")
     return [{"name": n, "prefill_us": f"{rows[n]['prefill_us']:.3f}", "decode_us": f"{rows[n]['decode_us']:.3f}"}
             for n in names]
+
+
+MOE_GROUPS = ("moe_router", "moe_experts", "moe_combine")
+
+
+def coarse_rows(rows: list[dict[str, str]]) -> list[dict[str, str]]:
+    """The reference's task set (embed, layer_i_attn, layer_i_mlp,
+    norm_lm_head): each MoE layer's router / experts / combine rows become one
+    layer_i_mlp row holding their sum. Dense tables pass through unchanged."""
+    out: list[dict[str, str]] = []
+    acc: dict[str, list[float]] = {}
+    for r in rows:
+        name = r["name"]
+        parts = name.split("_", 2)
+        if len(parts) == 3 and parts[0] == "layer" and parts[2] in MOE_GROUPS:
+            a = acc.setdefault(parts[1], [0.0, 0.0])
+            a[0] += float(r["prefill_us"])
+            a[1] += float(r["decode_us"])
+            if parts[2] == "moe_combine":
+                out.append({"name": f"layer_{parts[1]}_mlp", "prefill_us": f"{a[0]:.3f}",
+                            "decode_us": f"{a[1]:.3f}"})
+        else:
+            out.append(r)
+    return out
 
 
 def write_csv(rows: list[dict[str, str]], path: Path) -> None:
@@ -112,10 +134,15 @@ def main() -> None:
     ap.add_argument("--prefill-len", type=int, default=64)
     ap.add_argument("--device", default="cuda:0")
     ap.add_argument("--output", type=Path, required=True)
+    ap.add_argument("--groups", default="coarse", choices=["coarse", "moe"],
+                    help="coarse: attn / mlp rows (the reference's task set); moe: an MoE layer's "
+                         "router / experts / combine rows instead of its mlp row")
     a = ap.parse_args()
     assert torch.cuda.is_available(), "CUDA is required for kernel-group profiling"
     build.build()
     rows = measure(a.model, a.batch, a.context, a.decode_steps, a.warmup, a.prefill_len, a.device)
+    if a.groups == "coarse":
+        rows = coarse_rows(rows)
     write_csv(rows, a.output)
     print(f"profiled model={a.model} device={torch.cuda.get_device_name(a.device)} tasks={len(rows)} "
           f"batch={a.batch} context={a.context} output={a.output}")

@@ -1,0 +1,92 @@
+"""Generate placement plans with the reference's own planner from this
+package's B200 cost tables, as fixtures for tests/test_cost_tables.py.
+
+Run in a container that has the FluidGPU reference checkout (read-only is
+fine); the plans it writes are committed, so the tests never need the
+reference at run time:
+
+  python tests/golden/make_plans.py <reference>
+
+It runs the reference's examples/fluidgpu_torch/schedule_llm_layers.py (DP
+solver, reading its two cost tables with planner.py:93-103) on:
+  * the same B200 table for both ranks (two identical GPUs): every group on
+    rank 0, since any hand-off only adds cost;
+  * rank 1 given the same table with its feed-forward rows (mlp, or the MoE
+    experts group) at half the cost, a stand-in for a second GPU that is
+    faster at the FFN (this input is synthetic, the tables are measured):
+    the planner moves feed-forward groups to rank 1.
+Each plan carries a "fixture" entry naming its inputs and what it expects.
+"""
+from __future__ import annotations
+
+import csv
+import json
+import os
+import subprocess
+import sys
+import tempfile
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parent.parent
+OUT = HERE / "plans"
+
+MODELS = {
+    "llama3_8b": dict(model="llama-3-8b", hidden=4096, kv=8, hd=128),
+    "gptoss20b": dict(model="gpt-oss-20b", hidden=2880, kv=8, hd=64),
+}
+CASES = [
+    ("llama3_8b", "task_costs_llama3_8b_b64_ctx4096.csv", None),
+    ("llama3_8b", "task_costs_llama3_8b_b64_ctx4096.csv", "_mlp"),
+    ("gptoss20b", "task_costs_gptoss20b_b128_ctx4096.csv", None),
+    ("gptoss20b", "task_costs_gptoss20b_b128_ctx4096_moe_groups.csv", "_moe_experts"),
+]
+
+
+def _scaled_table(src: Path, suffix: str, dst: Path) -> None:
+    with src.open(newline="") as f:
+        rows = list(csv.DictReader(f))
+    for r in rows:
+        if r["name"].endswith(suffix):
+            r["prefill_us"] = f"{float(r['prefill_us']) * 0.5:.3f}"
+            r["decode_us"] = f"{float(r['decode_us']) * 0.5:.3f}"
+    with dst.open("w", newline="") as f:
+        w = csv.DictWriter(f, fieldnames=["name", "prefill_us", "decode_us"])
+        w.writeheader()
+        w.writerows(rows)
+
+
+def main(reference: Path) -> None:
+    runtime = reference / "fluidgpu_runtime"
+    script = runtime / "examples" / "fluidgpu_torch" / "schedule_llm_layers.py"
+    assert script.exists(), f"no planner script at {script}"
+    OUT.mkdir(exist_ok=True)
+    env = {**os.environ, "PYTHONPATH": str(runtime)}
+    with tempfile.TemporaryDirectory() as tmp:
+        for key, table, faster in CASES:
+            m = MODELS[key]
+            rank0 = ROOT / "profiles" / table
+            rank1 = rank0
+            if faster:
+                rank1 = Path(tmp) / f"rank1_{key}{faster}.csv"
+                _scaled_table(rank0, faster, rank1)
+            stem = table.replace("task_costs_", "plan_").replace(".csv", "") + (
+                "_ffn_rank_faster" if faster else "_two_b200")
+            out = OUT / f"{stem}.json"
+            cmd = [sys.executable, str(script), "--rank0-csv", str(rank0), "--rank1-csv", str(rank1),
+                   "--output", str(out), "--model", m["model"], "--hidden-size", str(m["hidden"]),
+                   "--num-kv-heads", str(m["kv"]), "--head-dim", str(m["hd"]), "--max-seq-len", "5120",
+                   "--comm-bw-gbps", "770", "--decode-weight", "32"]
+            r = subprocess.run(cmd, env=env, capture_output=True, text=True, cwd=tmp)
+            assert r.returncode == 0, r.stderr
+            plan = json.loads(out.read_text())
+            plan["fixture"] = {"rank0_csv": table, "rank1": f"same table, {faster} rows x 0.5" if faster
+                               else "same table", "expect_split": bool(faster),
+                               "planner": r.stdout.strip().splitlines()[-1]}
+            out.write_text(json.dumps(plan, indent=1) + "\n")
+            print(out.name, plan["fixture"]["planner"])
+
+
+if __name__ == "__main__":
+    assert len(sys.argv) == 2, "usage: make_plans.py <reference checkout>"
+    main(Path(sys.argv[1]))
