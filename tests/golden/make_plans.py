@@ -16,6 +16,11 @@ solver, reading its two cost tables with planner.py:93-103) on:
     faster at the FFN (this input is synthetic, the tables are measured):
     the planner moves feed-forward groups to rank 1.
 Each plan carries a "fixture" entry naming its inputs and what it expects.
+
+It also records what the reference's plan writer (profile.py:275-326
+make_ranked_task_profile) emits for a few task assignments (attention /
+FFN split, fine attention split, MoE groups, three ranks), in
+reference_writer.json, so the tests can compare this package's writer with it.
 """
 from __future__ import annotations
 
@@ -87,6 +92,31 @@ def main(reference: Path) -> None:
             print(out.name, plan["fixture"]["planner"])
 
 
+WRITER_CASES = [
+    dict(model="m", hidden_size=64, num_kv_heads=2, head_dim=16, max_seq_len=128,
+         task_assignments=[("layer_0_attn", 0), ("layer_0_mlp", 1), ("layer_1_attn", 0), ("layer_1_mlp", 1)]),
+    dict(model="m", hidden_size=64, num_kv_heads=2, head_dim=16, max_seq_len=256,
+         task_assignments=[("layer_0_qkv", 0), ("layer_0_sdpa", 1), ("layer_0_o_proj", 0),
+                           ("layer_0_mlp_gate_up", 1), ("layer_0_mlp_down_proj", 1)]),
+    dict(model="gpt-oss-20b", hidden_size=2880, num_kv_heads=8, head_dim=64, max_seq_len=5120,
+         task_assignments=[("layer_0_attn", 0), ("layer_0_moe_router", 0), ("layer_0_moe_experts", 1),
+                           ("layer_0_moe_combine", 0)]),
+    dict(model="m", hidden_size=64, num_kv_heads=2, head_dim=16, max_seq_len=128, rank_count=3,
+         task_assignments=[("layer_0_attn", 0), ("layer_0_mlp", 2)]),
+]
+
+
+def write_reference_writer_cases(runtime: Path) -> None:
+    sys.path.insert(0, str(runtime))
+    from fluidgpu_torch.profile import make_ranked_task_profile  # the reference's writer
+
+    cases = [{"args": {k: (list(map(list, v)) if k == "task_assignments" else v) for k, v in c.items()},
+              "profile": make_ranked_task_profile(**c)} for c in WRITER_CASES]
+    (OUT / "reference_writer.json").write_text(json.dumps(cases, indent=1) + "\n")
+    print("reference_writer.json", len(cases), "cases")
+
+
 if __name__ == "__main__":
     assert len(sys.argv) == 2, "usage: make_plans.py <reference checkout>"
     main(Path(sys.argv[1]))
+    write_reference_writer_cases(Path(sys.argv[1]) / "fluidgpu_runtime")

@@ -275,3 +275,20 @@ def test_sharded_group_scatter_and_reduce(monkeypatch):
     assert results[1] is None and results[2] is None
     # layer 0: attn 0 -> 1, mlp 1*1 + 2*1 = 3; layer 1: attn 4, mlp 4 + 8 = 12
     assert torch.equal(results[0], torch.full((2, 1, 4), 12.0, dtype=torch.bfloat16))
+
+
+def test_plan_writer_matches_reference():
+    """make_ranked_task_profile writes the same plan JSON as the reference's
+    (profile.py:275-326) for two- and three-rank assignments, fine attention
+    splits and MoE groups (fixture: tests/golden/plans/reference_writer.json,
+    from tests/golden/make_plans.py), and the plans validate here."""
+    from pathlib import Path
+
+    cases = json.loads((Path(__file__).parent / "golden" / "plans" / "reference_writer.json").read_text())
+    assert len(cases) >= 4
+    for case in cases:
+        args = dict(case["args"])
+        args["task_assignments"] = [tuple(a) for a in args["task_assignments"]]
+        ours = make_ranked_task_profile(**args)
+        assert ours == case["profile"], args
+        profile_from_dict(ours)
