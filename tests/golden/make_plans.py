@@ -20,7 +20,10 @@ Each plan carries a "fixture" entry naming its inputs and what it expects.
 It also records what the reference's plan writer (profile.py:275-326
 make_ranked_task_profile) emits for a few task assignments (attention /
 FFN split, fine attention split, MoE groups, three ranks), in
-reference_writer.json, so the tests can compare this package's writer with it.
+reference_writer.json, and what the reference's loader (profile.py:97-167
+profile_from_dict) decides on a set of valid and invalid plans, in
+reference_validation.json, so the tests can compare this package's writer and
+loader with them.
 """
 from __future__ import annotations
 
@@ -116,7 +119,85 @@ def write_reference_writer_cases(runtime: Path) -> None:
     print("reference_writer.json", len(cases), "cases")
 
 
+def _validation_cases(make) -> dict[str, dict]:
+    """Plans, valid and invalid, for the loader's rules: fixed tasks on rank 0,
+    dtype, per-layer task sequences (coarse, attn / mlp, fine attention,
+    MoE groups), decode_rank placement, rank range, unique names, contiguous
+    layers, suffixes."""
+    def af():
+        return make(model="m", task_assignments=[("layer_0_attn", 0), ("layer_0_mlp", 1), ("layer_1_attn", 0),
+                                                 ("layer_1_mlp", 1)],
+                    hidden_size=64, num_kv_heads=2, head_dim=16, max_seq_len=128)
+
+    def fine():
+        return make(model="m", task_assignments=[("layer_0_qkv", 0), ("layer_0_sdpa", 1), ("layer_0_o_proj", 0),
+                                                 ("layer_0_mlp", 1)],
+                    hidden_size=64, num_kv_heads=2, head_dim=16, max_seq_len=128)
+
+    def moe():
+        return make(model="m", task_assignments=[("layer_0_attn", 0), ("layer_0_moe_router", 0),
+                                                 ("layer_0_moe_experts", 1), ("layer_0_moe_combine", 0)],
+                    hidden_size=64, num_kv_heads=2, head_dim=16, max_seq_len=128)
+
+    def renamed(r, i, name):
+        r["tasks"][i] = {**r["tasks"][i], "name": name}
+
+    def drop(r, i):
+        r["tasks"].pop(i)
+        r["task_count"] = len(r["tasks"])
+
+    edits = {
+        "valid_af": (af, lambda r: None),
+        "valid_fine": (fine, lambda r: None),
+        "valid_moe_groups": (moe, lambda r: None),
+        "embed_on_rank1": (af, lambda r: r["tasks"][0].__setitem__("rank", 1)),
+        "head_on_rank1": (af, lambda r: r["tasks"][-1].__setitem__("rank", 1)),
+        "dtype_fp32": (af, lambda r: r.__setitem__("dtype", "float32")),
+        "missing_mlp": (af, lambda r: drop(r, 2)),
+        "decode_rank_on_attn": (af, lambda r: r["tasks"][1].__setitem__("decode_rank", 1)),
+        "decode_rank_on_mlp": (af, lambda r: r["tasks"][2].__setitem__("decode_rank", 0)),
+        "decode_rank_on_moe_experts": (moe, lambda r: r["tasks"][3].__setitem__("decode_rank", 0)),
+        "mlp_before_attn": (af, lambda r: (renamed(r, 1, "layer_0_mlp"), renamed(r, 2, "layer_0_attn"))),
+        "task_count_ignored": (af, lambda r: r.__setitem__("task_count", 99)),
+        "rank_out_of_range": (af, lambda r: r["tasks"][2].__setitem__("rank", 2)),
+        "duplicate_name": (af, lambda r: renamed(r, 3, "layer_0_attn")),
+        "coarse_layer_tasks": (af, lambda r: (r.__setitem__("tasks", [
+            r["tasks"][0], {"task_id": 1, "kernel_group_id": 1, "name": "layer_0", "rank": 0},
+            {"task_id": 2, "kernel_group_id": 2, "name": "layer_1", "rank": 1},
+            {**r["tasks"][-1], "task_id": 3, "kernel_group_id": 3}]), r.__setitem__("task_count", 4))),
+        "fine_missing_sdpa": (fine, lambda r: drop(r, 2)),
+        "task_id_gap": (af, lambda r: r["tasks"][2].__setitem__("task_id", 7)),
+        "layer_gap": (af, lambda r: (renamed(r, 3, "layer_2_attn"), renamed(r, 4, "layer_2_mlp"))),
+        "unknown_suffix": (af, lambda r: renamed(r, 2, "layer_0_ffn")),
+        "mlp_and_moe_in_one_layer": (af, lambda r: r["tasks"].insert(
+            3, {"task_id": 3, "kernel_group_id": 3, "name": "layer_0_moe_router", "rank": 1})),
+    }
+    out = {}
+    for name, (base, edit) in edits.items():
+        r = base()
+        edit(r)
+        out[name] = r
+    return out
+
+
+def write_reference_validation_cases(runtime: Path) -> None:
+    sys.path.insert(0, str(runtime))
+    from fluidgpu_torch.profile import make_ranked_task_profile, profile_from_dict  # the reference's
+
+    cases = []
+    for name, raw in _validation_cases(make_ranked_task_profile).items():
+        try:
+            profile_from_dict(json.loads(json.dumps(raw)))
+            result = {"ok": True}
+        except AssertionError as exc:
+            result = {"ok": False, "error": "AssertionError", "message": str(exc)}
+        cases.append({"name": name, "plan": raw, "reference": result})
+    (OUT / "reference_validation.json").write_text(json.dumps(cases, indent=1) + "\n")
+    print("reference_validation.json", len(cases), "cases")
+
+
 if __name__ == "__main__":
     assert len(sys.argv) == 2, "usage: make_plans.py <reference checkout>"
     main(Path(sys.argv[1]))
     write_reference_writer_cases(Path(sys.argv[1]) / "fluidgpu_runtime")
+    write_reference_validation_cases(Path(sys.argv[1]) / "fluidgpu_runtime")

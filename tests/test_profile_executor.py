@@ -292,3 +292,25 @@ def test_plan_writer_matches_reference():
         ours = make_ranked_task_profile(**args)
         assert ours == case["profile"], args
         profile_from_dict(ours)
+
+
+def test_plan_loader_decisions_match_reference():
+    """Valid and invalid plans (fixed tasks off rank 0, dtype, broken per-layer
+    task sequences, decode_rank on the wrong group, rank range, duplicate
+    names, layer gaps, unknown suffixes, coarse layer tasks, MoE groups): this
+    loader accepts exactly the plans the reference's profile_from_dict
+    accepts, and rejects the others with the same AssertionError text
+    (fixture from tests/golden/make_plans.py)."""
+    from pathlib import Path
+
+    cases = json.loads((Path(__file__).parent / "golden" / "plans" / "reference_validation.json").read_text())
+    assert len(cases) >= 20
+    for case in cases:
+        ref = case["reference"]
+        if ref["ok"]:
+            profile_from_dict(case["plan"])
+        else:
+            with pytest.raises(AssertionError) as info:
+                profile_from_dict(case["plan"])
+            head = ref["message"][:48]
+            assert str(info.value)[:48] == head, (case["name"], str(info.value), ref["message"])
