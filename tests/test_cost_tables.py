@@ -69,7 +69,7 @@ def test_coarse_rows():
 
 
 def _plans():
-    return sorted(PLANS.glob("*.json"))
+    return sorted(PLANS.glob("plan_*.json"))
 
 
 def test_reference_planner_fixtures_present():
