@@ -202,6 +202,14 @@ class PagedKVCache:
         assert kv_length <= self.max_seq_len, f"exceed max_seq_len: {kv_length} > {self.max_seq_len}"
         return kv_length, 0
 
+    def get_usable_length(self, new_seq_length: int, layer_idx: int = 0) -> int:
+        """Cached tokens a step of new_seq_length more can still attend to
+        (kv_cache.py:135-138), for the longest sequence of the batch."""
+        cur = self.get_seq_length(layer_idx)
+        if cur + new_seq_length <= self.max_seq_len:
+            return cur
+        return self.max_seq_len - new_seq_length
+
     def advance(self, seq_len: int) -> None:
         assert seq_len > 0, f"seq_len must be positive, got {seq_len}"
         for b in range(self.batch):
