@@ -23,7 +23,8 @@ FFN split, fine attention split, MoE groups, three ranks), in
 reference_writer.json, and what the reference's loader (profile.py:97-167
 profile_from_dict) decides on a set of valid and invalid plans, in
 reference_validation.json, so the tests can compare this package's writer and
-loader with them.
+loader with them; and whether every plan the reference ships loads the same
+way with both loaders (reference_shipped_plans.json, outcomes only).
 """
 from __future__ import annotations
 
@@ -196,8 +197,39 @@ def write_reference_validation_cases(runtime: Path) -> None:
     print("reference_validation.json", len(cases), "cases")
 
 
+def write_shipped_plan_check(reference: Path) -> None:
+    """Load every plan the reference ships (its profiles/*.json and the
+    validation artifact's profile.json) with its loader and with this
+    package's, and record per file whether both accept it and expand it to
+    the same (name, rank, decode_rank) tasks. Only the outcome is recorded;
+    the plans stay in the reference checkout."""
+    runtime = reference / "fluidgpu_runtime"
+    sys.path.insert(0, str(runtime))
+    sys.path.insert(0, str(ROOT))
+    from fluidgpu_torch.profile import load_profile as reference_load
+
+    from fluidgpu_b200.profile import load_profile as our_load
+
+    def tasks(load, f):
+        try:
+            return [[t.name, t.rank, getattr(t, "decode_rank", None)] for t in load(f).tasks]
+        except AssertionError as exc:
+            return f"AssertionError: {exc}"
+
+    files = sorted((runtime / "profiles").glob("*.json")) + sorted(
+        (reference / "artifacts").rglob("profile.json"))
+    rows = []
+    for f in files:
+        ref, ours = tasks(reference_load, f), tasks(our_load, f)
+        rows.append({"file": str(f.relative_to(reference)), "reference_accepts": isinstance(ref, list),
+                     "tasks": len(ref) if isinstance(ref, list) else 0, "identical": ref == ours})
+    (OUT / "reference_shipped_plans.json").write_text(json.dumps(rows, indent=1) + "\n")
+    print("reference_shipped_plans.json", sum(r["identical"] for r in rows), "of", len(rows), "identical")
+
+
 if __name__ == "__main__":
     assert len(sys.argv) == 2, "usage: make_plans.py <reference checkout>"
     main(Path(sys.argv[1]))
     write_reference_writer_cases(Path(sys.argv[1]) / "fluidgpu_runtime")
     write_reference_validation_cases(Path(sys.argv[1]) / "fluidgpu_runtime")
+    write_shipped_plan_check(Path(sys.argv[1]))
