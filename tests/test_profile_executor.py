@@ -110,6 +110,9 @@ def test_reference_layer_plan_format_loads(tmp_path):
     prof = profile_from_dict(per_phase)
     mlp = prof.task_by_name["layer_0_mlp"]
     assert mlp.rank_for("decode") == 1 and mlp.rank_for("prefill") == 0
+    # KV ownership follows the attention task, never decode_rank
+    # (test_per_phase_placement.py:48-53 in the reference)
+    assert owned_layer_ids(prof, 0) == [0] and owned_layer_ids(prof, 1) == []
 
 
 @pytest.mark.parametrize("mutate,msg", [
