@@ -9,7 +9,9 @@ norm + lm_head, greedy argmax) in float32 on the host cores.
 A full Llama-3-8B step at batch 64 and context 4096 is minutes of CPU work,
 so the measured sample is ONE decoder layer plus the norm/lm_head/argmax
 tail at the full batch and context; the step time is scaled to the model as
-num_layers * t_layer + t_head, and tokens/s = batch / step time.
+num_layers * t_layer + t_head, and tokens/s = batch / step time. The
+reference measures its per-group CPU costs the same way, one group at a time
+at the target dims (examples/fluidgpu_torch/profile_llm_tasks.py:116-160).
 """
 from __future__ import annotations
 
@@ -24,6 +26,8 @@ from . import decode_ref as ref
 
 
 def host_threads() -> int:
+    """Host cores this process may use (len(os.sched_getaffinity(0)), the
+    count the baseline reports beside its number)."""
     try:
         return len(os.sched_getaffinity(0))
     except AttributeError:  # pragma: no cover
@@ -31,7 +35,9 @@ def host_threads() -> int:
 
 
 class LayerSample:
-    """One dense decoder layer + head at (batch, context), fp32, random N(0,0.02)."""
+    """One dense decoder layer + head at (batch, context), fp32, random
+    N(0,0.02): the reference's _run_attn + _run_mlp (runner.py:170-194,
+    :349-352) and _norm_head + argmax (runner.py:167-168, engine.py:337-343)."""
 
     def __init__(self, hidden: int, n_q: int, n_kv: int, head_dim: int, intermediate: int,
                  vocab: int, rope_theta: float, batch: int, context: int, seed: int = 0) -> None:
@@ -53,6 +59,8 @@ class LayerSample:
         self.h = torch.randn(batch, hidden, generator=g)
 
     def layer(self) -> torch.Tensor:
+        """One decode step of the layer for the whole batch (runner.py:170-194
+        attention group, :349-352 MLP group)."""
         B = self.B
         h = self.h
         x = ref.rms_norm(h, self.ln1, 1e-5)
@@ -72,6 +80,8 @@ class LayerSample:
         return h + F.linear(ref.silu_mul(F.linear(x, self.wg), F.linear(x, self.wu)), self.wd)
 
     def head(self) -> torch.Tensor:
+        """Final norm + lm_head + greedy argmax (runner.py:167-168,
+        engine.py:337-343)."""
         x = ref.rms_norm(self.h, self.final_norm, 1e-5)
         return ref.argmax_lowest(F.linear(x, self.lm_head))
 

@@ -10,7 +10,7 @@ decode step of a batch of requests. Reference anchors (FluidGPU project):
     decode_step           :119-165  embed -> L x (attn, ffn) -> norm+lm_head
     _run_attn             :170-194  RMSNorm -> self_attn -> + residual
     _run_attn_qkv         :256-293  q/k/v proj, apply_rotary_pos_emb, KV update
-    _run_attn_sdpa        :295-335  eager_attention_forward with mask and sinks
+    _run_attn_sdpa        :299-335  eager_attention_forward with mask and sinks
     _run_mlp              :349-352  RMSNorm -> mlp -> + residual
     _run_moe_router/experts/combine :432-457
     _attention_mask_for_layer / _sliding_window_mask :713-774 (kv > q - window)
@@ -45,7 +45,9 @@ import torch.nn.functional as F
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, fp32_weight_mul: bool = False) -> torch.Tensor:
     """LlamaRMSNorm (weight * x_normed.to(dtype)) or GptOssRMSNorm
-    ((weight * x_normed).to(dtype))."""
+    ((weight * x_normed).to(dtype)): the layer's input_layernorm /
+    post_attention_layernorm and the final norm the reference calls
+    (runner.py:183, :351, :434, :167-168)."""
     dtype = x.dtype
     h = x.float()
     var = h.pow(2).mean(-1, keepdim=True)
@@ -92,14 +94,16 @@ def yarn_inv_freq(head_dim: int, theta: float, factor: float, original_max: int,
 
 def rope_cos_sin(positions: torch.Tensor, inv_freq: torch.Tensor, scaling: float,
                  dtype: torch.dtype) -> tuple[torch.Tensor, torch.Tensor]:
-    """cos/sin of shape [T, hd/2] computed in fp32, scaled, cast to dtype."""
+    """cos/sin of shape [T, hd/2] computed in fp32, scaled, cast to dtype
+    (the model's rotary_emb, which the reference calls at runner.py:786-801)."""
     freqs = positions.float()[:, None] * inv_freq.float()[None, :]
     return (freqs.cos() * scaling).to(dtype), (freqs.sin() * scaling).to(dtype)
 
 
 def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     """Rotate-half RoPE on x[T, heads, hd] with cos/sin [T, hd/2]; each
-    product and sum rounds to x.dtype like the reference's tensor ops."""
+    product and sum rounds to x.dtype like the reference's tensor ops
+    (runner.py:892-903 _apply_rotary_pos_emb)."""
     x1, x2 = x.chunk(2, dim=-1)
     c = cos[:, None, :]
     s = sin[:, None, :]
@@ -108,7 +112,8 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
 
 def attention_one(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
                   window: int = 0, sinks: torch.Tensor | None = None) -> torch.Tensor:
-    """Decode attention of one sequence in fp32.
+    """Decode attention of one sequence in fp32 (runner.py:299-335 with the
+    window mask of :713-774 and the sinks of :914-920).
     q [nq, hd]; k, v [L, nkv, hd] (the whole cache incl. the new token).
     window > 0 keeps kv positions > (L-1) - window; sinks [nq] join the
     softmax denominator only (eager_attention_forward of gpt-oss)."""
@@ -131,11 +136,14 @@ def attention_one(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: floa
 
 
 def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """SiLU(gate) * up: the dense MLP the reference runs (runner.py:349-352,
+    :416-430; LlamaMLP)."""
     return F.silu(gate) * up
 
 
 def swiglu_oai(gate: torch.Tensor, up: torch.Tensor, alpha: float = 1.702, limit: float = 7.0) -> torch.Tensor:
-    """GptOssExperts._apply_gate: clamp, gate*sigmoid(alpha*gate)*(up+1)."""
+    """GptOssExperts._apply_gate: clamp, gate*sigmoid(alpha*gate)*(up+1)
+    (the experts module the reference calls at runner.py:444-452)."""
     gate = gate.clamp(min=None, max=limit)
     up = up.clamp(min=-limit, max=limit)
     glu = gate * torch.sigmoid(gate * alpha)
@@ -143,7 +151,8 @@ def swiglu_oai(gate: torch.Tensor, up: torch.Tensor, alpha: float = 1.702, limit
 
 
 def argmax_lowest(logits: torch.Tensor) -> torch.Tensor:
-    """Greedy token per row; ties resolve to the lowest index."""
+    """Greedy token per row; ties resolve to the lowest index (torch argmax,
+    as the reference's decode loop, engine.py:337-343)."""
     m = logits.max(dim=-1, keepdim=True).values
     idx = torch.arange(logits.shape[-1])
     big = torch.full_like(idx, logits.shape[-1])
@@ -152,7 +161,8 @@ def argmax_lowest(logits: torch.Tensor) -> torch.Tensor:
 
 def topk_lowest(logits: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
     """Top-k by value, descending; equal values ordered by lower index
-    (a stable descending sort)."""
+    (a stable descending sort): the router's top-k (runner.py:436;
+    vllm_integration.py:462-464)."""
     order = torch.sort(logits, dim=-1, descending=True, stable=True)
     return order.values[..., :k], order.indices[..., :k]
 
@@ -167,7 +177,8 @@ E2M1_VALUES = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0,
 def mxfp4_quantize(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """w [..., K] (K % 32 == 0) -> (packed uint8 [..., K/2] low nibble = even
     element, scales uint8 [..., K/32] e8m0). Scale = 2^ceil(log2(amax/6)),
-    values rounded to the nearest e2m1 (ties to the even code)."""
+    values rounded to the nearest e2m1 (ties to the even code). The layout is
+    the checkpoint's, which the reference decodes at vllm_integration.py:503-513."""
     *lead, K = w.shape
     wb = w.float().reshape(*lead, K // 32, 32)
     amax = wb.abs().amax(dim=-1, keepdim=True)
@@ -192,6 +203,8 @@ def mxfp4_quantize(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 def mxfp4_dequantize(packed: torch.Tensor, scales: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
+    """e2m1 values (low nibble first) x 2^(e8m0 - 127), as
+    transformers' convert_moe_packed_tensors (vllm_integration.py:503-513)."""
     lo = (packed & 0x0F).long()
     hi = (packed >> 4).long()
     codes = torch.stack([lo, hi], dim=-1).reshape(*packed.shape[:-1], packed.shape[-1] * 2)
@@ -368,7 +381,8 @@ class OracleModel:
         return h + out
 
     def step(self, tokens: torch.Tensor) -> torch.Tensor:
-        """Append one token per request; returns logits [B, V] (model dtype)."""
+        """Append one token per request; returns logits [B, V] (model dtype):
+        the reference's decode_step (runner.py:119-165) for every request."""
         s = self.spec
         B = tokens.numel()
         if not self.lengths:
@@ -433,7 +447,8 @@ class OracleModel:
 
     def prefill_stepwise(self, prompts: torch.Tensor) -> torch.Tensor:
         """Feed prompts [B, S] one position at a time (causal attention makes
-        this equal to a full prefill); returns the last logits [B, V]."""
+        this equal to a full prefill, runner.py:66-116); returns the last
+        logits [B, V]."""
         self.reset(prompts.shape[0])
         logits = None
         for t in range(prompts.shape[1]):
@@ -441,7 +456,8 @@ class OracleModel:
         return logits
 
     def generate(self, prompts: torch.Tensor, steps: int) -> tuple[torch.Tensor, list[torch.Tensor]]:
-        """Greedy decode: returns tokens [B, steps] and the logits of every step."""
+        """Greedy decode: returns tokens [B, steps] and the logits of every step
+        (the reference's loop, engine.py:275-357)."""
         logits = self.prefill(prompts)
         toks, all_logits = [], []
         for _ in range(steps):
@@ -456,6 +472,8 @@ class OracleModel:
 # weights straight from a transformers model (the reference runs HF modules)
 # ---------------------------------------------------------------------------
 def spec_from_hf(cfg) -> OracleSpec:
+    """Shapes and options of an HF Llama / GptOss config, as the reference
+    reads them from the model (runner.py:923-941 head counts and sizes)."""
     gpt = cfg.model_type == "gpt_oss"
     hd = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
     params = getattr(cfg, "rope_parameters", None) or {}
@@ -474,6 +492,8 @@ def spec_from_hf(cfg) -> OracleSpec:
 
 
 def weights_from_hf(model) -> dict[str, torch.Tensor]:
+    """The tensors of an HF model the reference's runner uses
+    (runner.py:15-25 extract_components)."""
     m = model.model
     w: dict[str, torch.Tensor] = {"embed": m.embed_tokens.weight.detach(),
                                   "final_norm": m.norm.weight.detach(),
