@@ -126,3 +126,26 @@ def test_attn_split_plan_bounds(lib_path, hd):
     # batch 1 at long context spreads one sequence over many slices
     assert lib.fg_attn_splits(1, nkv, hd, 32768, 0) > 8
     assert lib.fg_attn_splits(1, nkv, hd, 32768, 128) <= 2
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    """No fallback: without the CUDA library every entry point raises (here
+    in a fresh interpreter pointed at a path with no library)."""
+    import os
+    import sys
+
+    code = ("from fluidgpu_b200 import _lib\n"
+            "try:\n    _lib.call('fg_last_error')\nexcept RuntimeError as e:\n    print('RAISED', e)\n")
+    env = {**os.environ, "FGB200_LIB": str(tmp_path / "absent" / "libfgb200.so")}
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True, text=True,
+                       timeout=120)
+    assert r.returncode == 0, r.stderr
+    assert "RAISED" in r.stdout and "not found" in r.stdout
+
+
+def test_product_never_imports_the_oracle():
+    """The oracle is test infrastructure: no module of the package imports it."""
+    for p in (ROOT / "fluidgpu_b200").rglob("*.py"):
+        src = p.read_text()
+        assert not re.search(r"^\s*(from|import)\s+oracle\b", src, re.M), p
+        assert "decode_ref" not in src and "cpu_baseline" not in src, p
