@@ -149,3 +149,17 @@ def test_product_never_imports_the_oracle():
         src = p.read_text()
         assert not re.search(r"^\s*(from|import)\s+oracle\b", src, re.M), p
         assert "decode_ref" not in src and "cpu_baseline" not in src, p
+
+
+@pytest.mark.parametrize("T,k,E,BN", [(1, 4, 32, 16), (32, 4, 32, 16), (64, 4, 32, 16), (65, 4, 32, 32),
+                                      (128, 4, 32, 32), (129, 4, 32, 64), (512, 4, 32, 64), (4096, 4, 32, 64)])
+def test_moe_tile_plan(lib_path, T, k, E, BN):
+    """Token tile of the expert GEMM: room for about twice the mean rows per
+    expert (16 / 32 / 64), so most experts stream their weights once; the
+    work-item bound covers one partial tile per expert plus the full ones."""
+    from fluidgpu_b200 import _lib
+
+    lib = _lib.lib()
+    assert lib.fg_moe_tile_tokens(T, k, E) == BN
+    assert lib.fg_moe_max_items(T, k, E, BN) == E + (T * k + BN - 1) // BN
+    assert lib.fg_moe_max_items(0, k, E, BN) == 0
