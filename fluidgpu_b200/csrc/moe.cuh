@@ -35,14 +35,255 @@ constexpr int kRecBytes = kValBytes + kScaleBytes;  // 4352
 constexpr int kMaxE = 64;
 
 // ---------------------------------------------------------------------------
-// router: logits, top-k (value desc, index asc), softmax over the selected
+// router: logits rounded once from their exact value, top-k, softmax
 // ---------------------------------------------------------------------------
-// One CTA of 32 warps per token: warp w computes the logits of experts w,
-// w+32 (one dot product each, its loads all in flight together), then warp 0
-// selects the top-k.
+// logit[t,e] is the bf16 nearest (ties to even) to the exact real number
+// x[t] . w[e] + b[e]. Every bf16 x bf16 product is exact (16 significant
+// bits), so the only rounding the reference's bf16 linear performs that is
+// implementation-defined is its accumulation; summing the products exactly
+// and rounding once gives the one result every faithful bf16 linear
+// approximates, independent of reduction order. The CPU oracle computes the
+// same number (an exactly rounded sum, then one bf16 rounding), so router
+// indices can be compared with zero tolerance.
+//
+// Exact sums, two ways (both end in the same digit array and rounding):
+//  * fast path, when every nonzero element of x and w[e] is a finite normal
+//    bf16 and their exponents span at most kFastSpan binades: each product is
+//    taken exactly in fp32 (a bf16 x bf16 product of normal operands whose
+//    exponents keep it in fp32's normal range), placed at a fixed binary point
+//    (the smallest product exponent of the row pair) into a 128-bit integer
+//    per lane; lanes are summed with shuffles. No product can fall outside the
+//    window, so nothing is lost.
+//  * full-range path otherwise (subnormals, wide exponent spread): a Kulisch
+//    accumulator, 18 digits of 32 bits (weights 2^-266 .. 2^310) covering
+//    every bf16 x bf16 product, kept in shared memory per warp; lanes add
+//    their products with 64-bit shared atomics (digit sums carry lazily).
+// Non-finite inputs give a NaN logit.
+namespace exact {
+
+constexpr int kDigits = 18;     // 32-bit digits of the full-range accumulator
+constexpr int kOrigin = 266;    // bit 0 of digit 0 weighs 2^-266 (the smallest product LSB)
+constexpr int kFastSpan = 86;   // max (max - min) of summed biased exponents on the fast path
+
+// bf16 bits -> exact (mantissa m >= 0, LSB exponent e): |v| = m * 2^e
+__device__ __forceinline__ void decompose(uint32_t b, int& m, int& e) {
+  const int field = (b >> 7) & 0xff;
+  m = (int)(b & 0x7f) | (field ? 0x80 : 0);
+  e = (field ? field : 1) - 134;
+}
+
+// per-row exponent statistics of bf16 words (two elements per u32):
+// fmax: largest biased exponent field (0x7f80 = non-finite present),
+// fmin: smallest field among nonzero elements (0 = a subnormal present)
+struct ExpStats {
+  uint32_t fmax = 0, fmin = 0x7f807f80u;
+  __device__ __forceinline__ void add(uint32_t w) {
+    const uint32_t f = w & 0x7f807f80u;
+    const uint32_t zero = __vcmpeq2(w & 0x7fff7fffu, 0u);  // 0xffff in zero halves
+    fmax = __vmaxu2(fmax, f);
+    fmin = __vminu2(fmin, f | (zero & 0x7f807f80u));
+  }
+  __device__ __forceinline__ void add4(const uint4& v) {
+    add(v.x); add(v.y); add(v.z); add(v.w);
+  }
+  // reduce over the warp; returns fields as plain integers
+  __device__ __forceinline__ void reduce(int& hi, int& lo) const {
+    uint32_t a = max(fmax >> 23, (fmax >> 7) & 0xffu);
+    uint32_t b = min(fmin >> 23, (fmin >> 7) & 0xffu);
+    hi = (int)__reduce_max_sync(0xffffffffu, a);
+    lo = (int)__reduce_min_sync(0xffffffffu, b);
+  }
+};
+
+// Round sign * sum_i D[i] 2^(32 i - kOrigin) (D normalised, 32-bit digits)
+// to the nearest bf16, ties to even. Returns the bf16 bits.
+__device__ uint16_t round_digits_bf16(const uint32_t* D, bool neg) {
+  int top = -1;
+  for (int i = kDigits - 1; i >= 0; --i)
+    if (D[i]) {
+      top = 32 * i + 31 - __clz(D[i]);
+      break;
+    }
+  if (top < 0) return 0;  // exact zero: +0
+  // bit position (frame) of the last kept bit: 8 significant bits, or the
+  // bf16 subnormal quantum 2^-133
+  int q = max(top - 7, kOrigin - 133);
+  auto bit = [&](int p) -> uint32_t { return (D[p >> 5] >> (p & 31)) & 1u; };
+  uint32_t kept = 0;
+  for (int p = top; p >= q; --p) kept = (kept << 1) | bit(p);
+  const uint32_t rbit = bit(q - 1);
+  bool sticky = false;
+  const int sp = q - 1;  // bits strictly below sp
+  for (int i = 0; i < (sp >> 5); ++i) sticky |= D[i] != 0u;
+  if (sp & 31) sticky |= (D[sp >> 5] & ((1u << (sp & 31)) - 1u)) != 0u;
+  if (rbit && (sticky || (kept & 1u))) ++kept;
+  if (kept == 256u) {
+    kept = 128u;
+    ++q;
+  }
+  uint32_t bits;
+  if (kept < 128u) {
+    bits = kept;  // subnormal (q is the subnormal quantum's position)
+  } else {
+    const int biased = q - kOrigin + 134;
+    bits = biased >= 255 ? 0x7f80u : (((uint32_t)biased << 7) | (kept & 0x7fu));
+  }
+  return (uint16_t)(bits | (neg ? 0x8000u : 0u));
+}
+
+// Normalise lazily-carried int64 digit sums into 32-bit digits + sign and
+// round (one thread).
+__device__ uint16_t finish_digits(const long long* acc) {
+  uint32_t D[kDigits];
+  long long c = 0;
+  for (int i = 0; i < kDigits; ++i) {
+    const long long v = acc[i] + c;
+    D[i] = (uint32_t)v;
+    c = v >> 32;  // arithmetic: floor division
+  }
+  const bool neg = c < 0;
+  if (neg) {  // two's complement negate
+    uint32_t carry = 1;
+    for (int i = 0; i < kDigits; ++i) {
+      const uint64_t v = (uint64_t)(~D[i]) + carry;
+      D[i] = (uint32_t)v;
+      carry = (uint32_t)(v >> 32);
+    }
+  }
+  return round_digits_bf16(D, neg);
+}
+
+// add the signed value v * 2^(pos - kOrigin), |v| < 2^32, to the
+// lazily-carried digits as two pieces of magnitude < 2^32 (one thread)
+__device__ __forceinline__ void add_at(long long* acc, long long v, int pos) {
+  const long long t = v * (1ll << (pos & 31));  // |t| < 2^63
+  acc[pos >> 5] += t & 0xffffffffll;
+  acc[(pos >> 5) + 1] += t >> 32;  // arithmetic: t = hi * 2^32 + lo
+}
+
+// Exact dot product x . w (+ bias) of n8 groups of 8 bf16 over one warp;
+// `acc` is this warp's kDigits shared-memory digits (lane 0 returns the
+// bf16 bits of the rounded result). (xhi, xlo): the x row's exponent stats.
+__device__ uint16_t warp_exact_dot(const uint4* __restrict__ xr, const uint4* __restrict__ wr, int n8,
+                                   const __nv_bfloat16* bias, int xhi, int xlo, long long* acc, int lane) {
+  ExpStats ws;
+  for (int i = lane; i < n8; i += 32) ws.add4(wr[i]);
+  int whi, wlo;
+  ws.reduce(whi, wlo);
+  const uint32_t bbits = bias ? (uint32_t)__bfloat16_as_ushort(*bias) : 0u;
+  const bool nonfinite = xhi == 255 || whi == 255 || ((bbits >> 7) & 0xff) == 0xff;
+  if (nonfinite) return 0x7fc0;  // NaN
+  for (int i = lane; i < kDigits; i += 32) acc[i] = 0;
+  __syncwarp();
+  const bool any = xhi > 0 && whi > 0;  // both rows have a nonzero element
+  const bool fast = any && xlo > 0 && wlo > 0 && (xhi + whi) - (xlo + wlo) <= kFastSpan &&
+                    xlo + wlo >= 128 && xhi + whi <= 380;
+  if (fast) {
+    // fp32 product exponents lie in [xlo + wlo - 127, xhi + whi - 126]; the
+    // binary point sits at the smallest: fp32 product bits (e, m24) land at
+    // shift s = e - e0 in [0, kFastSpan + 1]; |sum| < 2^(24 + 87 + 14) < 2^127.
+    const int e0 = xlo + wlo - 127;
+    unsigned __int128 sum = 0;
+    for (int i = lane; i < n8; i += 32) {
+      const uint4 a = xr[i], b = wr[i];
+      const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+      const uint32_t* pb = reinterpret_cast<const uint32_t*>(&b);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 fa = unpack_bf16x2(pa[q]), fb = unpack_bf16x2(pb[q]);
+        const float p2[2] = {__fmul_rn(fa.x, fb.x), __fmul_rn(fa.y, fb.y)};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t pbits = __float_as_uint(p2[h]);
+          const int e = (int)((pbits >> 23) & 0xffu);
+          if (e == 0) continue;  // a zero operand (nonzero products are normal here)
+          const uint64_t m = (pbits & 0x7fffffu) | 0x800000u;
+          const unsigned __int128 v = (unsigned __int128)m << (e - e0);
+          sum = (pbits >> 31) ? sum - v : sum + v;
+        }
+      }
+    }
+    uint64_t lo = (uint64_t)sum, hi = (uint64_t)(sum >> 64);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t olo = __shfl_xor_sync(0xffffffffu, lo, o);
+      const uint64_t ohi = __shfl_xor_sync(0xffffffffu, hi, o);
+      const uint64_t nlo = lo + olo;
+      hi = hi + ohi + (nlo < lo ? 1u : 0u);
+      lo = nlo;
+    }
+    if (lane == 0) {
+      // sum * 2^(e0 - 150): fp32 significand LSB weight is 2^(e - 150);
+      // the two's complement words go in at their positions, the top one signed
+      const int pos = e0 - 150 + kOrigin;  // frame position of the sum's bit 0
+      add_at(acc, (long long)(uint32_t)lo, pos);
+      add_at(acc, (long long)(uint32_t)(lo >> 32), pos + 32);
+      add_at(acc, (long long)(uint32_t)hi, pos + 64);
+      add_at(acc, (long long)(int32_t)(hi >> 32), pos + 96);
+    }
+  } else if (any) {
+    for (int i = lane; i < n8; i += 32) {
+      const uint4 a = xr[i], b = wr[i];
+      const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+      const uint32_t* pb = reinterpret_cast<const uint32_t*>(&b);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint32_t xa = (pa[q >> 1] >> (16 * (q & 1))) & 0xffffu;
+        const uint32_t wb = (pb[q >> 1] >> (16 * (q & 1))) & 0xffffu;
+        int mx, ex, mw, ew;
+        decompose(xa, mx, ex);
+        decompose(wb, mw, ew);
+        const long long p = (long long)(mx * mw);
+        if (p == 0) continue;
+        const int pos = ex + ew + kOrigin;
+        const long long v = p << (pos & 31);  // p > 0, < 2^47
+        atomicAdd(reinterpret_cast<unsigned long long*>(acc + (pos >> 5)),
+                  (unsigned long long)(((xa ^ wb) & 0x8000u) ? -v : v));
+      }
+    }
+  }
+  __syncwarp();
+  if (lane != 0) return 0;
+  if (bias) {
+    int mb, eb;
+    decompose(bbits, mb, eb);
+    if (mb) add_at(acc, (bbits & 0x8000u) ? -(long long)mb : (long long)mb, eb + kOrigin);
+  }
+  return finish_digits(acc);
+}
+
+// bf16 nearest (ties to even) to a finite double
+__device__ __forceinline__ uint16_t dbl_to_bf16(double v) {
+  const uint64_t b = __double_as_longlong(v);
+  const uint16_t sign = (uint16_t)((b >> 48) & 0x8000u);
+  const int ef = (int)((b >> 52) & 0x7ff);
+  if (ef == 0x7ff) return (uint16_t)(sign | 0x7fc0u);
+  if (ef == 0) return sign;  // fp64 subnormals are far below bf16's range
+  const uint64_t m = (b & 0xfffffffffffffull) | (1ull << 52);  // value = m * 2^(ef - 1075)
+  // last kept bit: 8 significant bits, or the bf16 subnormal quantum 2^-133
+  const int lsb_exp = max(ef - 1023 - 7, -133);
+  const int drop = lsb_exp - (ef - 1075);  // >= 45
+  if (drop >= 64) return sign;             // below half the smallest subnormal
+  uint64_t kept = m >> drop;
+  const uint64_t rem = m & ((1ull << drop) - 1), half = 1ull << (drop - 1);
+  if (rem > half || (rem == half && (kept & 1))) ++kept;
+  int e = lsb_exp;
+  if (kept == 256) {
+    kept = 128;
+    ++e;
+  }
+  if (kept < 128) return (uint16_t)(sign | kept);
+  const int biased = e + 7 + 127;
+  if (biased >= 255) return (uint16_t)(sign | 0x7f80u);
+  return (uint16_t)(sign | ((uint32_t)biased << 7) | (kept & 0x7f));
+}
+
+}  // namespace exact
+
 // Top-k of the E <= 64 logits a warp holds (lane e has experts e and e+32),
-// by value with the lower expert id first on ties, then the softmax over
-// the k selected (fp32, rounded to bf16). Lane 0 writes the k pairs.
+// by value with the lower expert id first on ties, then the softmax over the
+// k selected: p_j = exp(v_j - v_0) in fp64, s = p_0 + ... + p_{k-1} in order,
+// weight_j = bf16(p_j / s) rounded once. Lane 0 writes the k pairs.
 __device__ __forceinline__ void warp_topk_softmax(float v0, float v1, int lane, int E, int k,
                                                   __nv_bfloat16* __restrict__ out_w,
                                                   int32_t* __restrict__ out_idx) {
@@ -71,18 +312,21 @@ __device__ __forceinline__ void warp_topk_softmax(float v0, float v1, int lane, 
     if (bi == lane + 32) v1 = -INFINITY;
   }
   if (lane == 0) {
-    float m = sel_v[0], s = 0.f, p[8];
+    double p[8], s = 0.0;
     for (int j = 0; j < k; ++j) {
-      p[j] = __expf(sel_v[j] - m);
+      p[j] = exp((double)sel_v[j] - (double)sel_v[0]);
       s += p[j];
     }
     for (int j = 0; j < k; ++j) {
       out_idx[j] = sel_i[j];
-      out_w[j] = f2bf(p[j] / s);
+      out_w[j] = __ushort_as_bfloat16(exact::dbl_to_bf16(p[j] / s));
     }
   }
 }
 
+// One CTA of 32 warps per token: the x row's exponent statistics first (all
+// warps), then warp w computes the exactly rounded logits of experts w, w+32,
+// and warp 0 selects the top-k.
 __global__ void __launch_bounds__(1024) router_topk_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
     const __nv_bfloat16* __restrict__ bias, int H, int E, int k, __nv_bfloat16* __restrict__ out_w,
@@ -90,29 +334,35 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(
   griddep_wait();
   griddep_launch_dependents();
   __shared__ float logit[kMaxE];
+  __shared__ long long digits[32][exact::kDigits];
+  __shared__ int s_hi[32], s_lo[32];
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)t * H);
   const int H8 = H >> 3;
+  {
+    exact::ExpStats xs;
+    for (int i = threadIdx.x; i < H8; i += blockDim.x) xs.add4(xr[i]);
+    int hi, lo;
+    xs.reduce(hi, lo);
+    if (lane == 0) {
+      s_hi[warp] = hi;
+      s_lo[warp] = lo;
+    }
+  }
+  __syncthreads();
+  int xhi = 0, xlo = 255;
+  for (int i = 0; i < 32; ++i) {
+    xhi = max(xhi, s_hi[i]);
+    xlo = min(xlo, s_lo[i]);
+  }
   for (int e = warp; e < E; e += 32) {
     const uint4* wr = reinterpret_cast<const uint4*>(w + (int64_t)e * H);
-    float acc = 0.f;
-#pragma unroll 4
-    for (int i = lane; i < H8; i += 32) {
-      const uint4 a = xr[i], b = wr[i];
-      const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
-      const uint32_t* pb = reinterpret_cast<const uint32_t*>(&b);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 fa = unpack_bf16x2(pa[q]), fb = unpack_bf16x2(pb[q]);
-        acc += fa.x * fb.x + fa.y * fb.y;
-      }
-    }
-    acc = warp_sum(acc);
+    const uint16_t b = exact::warp_exact_dot(xr, wr, H8, bias ? bias + e : nullptr, xhi, xlo,
+                                             digits[warp], lane);
     if (lane == 0) {
-      const float v = rbf(acc + (bias ? bf2f(bias[e]) : 0.f));  // bf16 logits, as the linear
-      logit[e] = v;
-      if (out_logits) out_logits[(int64_t)t * E + e] = f2bf(v);
+      logit[e] = bf2f(__ushort_as_bfloat16(b));
+      if (out_logits) out_logits[(int64_t)t * E + e] = __ushort_as_bfloat16(b);
     }
   }
   __syncthreads();
@@ -877,9 +1127,10 @@ int fg_moe_router_topk(const fg_bf16* x, const fg_bf16* w, const fg_bf16* bias, 
                        int k, fg_bf16* weights, int32_t* indices, fg_bf16* logits,
                        fg_stream_t stream) {
   FG_REQUIRE(x && w && weights && indices, "fg_moe_router_topk: null pointer");
-  FG_REQUIRE(T >= 0 && H > 0 && H % 8 == 0 && E > 0 && E <= fg::moe::kMaxE && k > 0 && k <= 8 &&
-                 k <= E,
-             "fg_moe_router_topk: bad sizes T=%d H=%d E=%d k=%d", T, H, E, k);
+  FG_REQUIRE(T >= 0 && H > 0 && H % 8 == 0 && H <= 16384 && E > 0 && E <= fg::moe::kMaxE && k > 0 &&
+                 k <= 8 && k <= E,
+             "fg_moe_router_topk: bad sizes T=%d H=%d E=%d k=%d (H %% 8 == 0, H <= 16384, E <= 64, k <= 8)",
+             T, H, E, k);
   FG_REQUIRE((((uintptr_t)x | (uintptr_t)w) & 15) == 0, "fg_moe_router_topk: x/w must be 16-byte aligned");
   if (T == 0) return FG_OK;
   return fg::launch_k("fg_moe_router_topk", fg::moe::router_topk_kernel, dim3(T), dim3(1024), 0,

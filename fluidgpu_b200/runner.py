@@ -86,8 +86,13 @@ class FluidRunner:
         self.record_routing = False
         self.last_routing: dict[int, torch.Tensor] = {}
         # with record_routing: every pass's (layer, positions per sequence,
-        # indices [B * n, k]) in order, when this is a list
-        self.routing_log: list[tuple[int, int, torch.Tensor]] | None = None
+        # indices [B * n, k], router input [B * n, H] or None where the ids
+        # came from another rank) in order, when this is a list
+        self.routing_log: list[tuple[int, int, torch.Tensor, torch.Tensor | None]] | None = None
+        # with record_routing: the router's input of the last pass per layer
+        # (the normalised hidden [B * n, H]), so a test can evaluate another
+        # router on exactly the rows this one saw
+        self.last_router_input: dict[int, torch.Tensor] = {}
 
     # -- sequence admission ---------------------------------------------------
     def start(self, batch: int, prompt_lens: list[int] | None = None,
@@ -377,7 +382,7 @@ class FluidRunner:
         weights, idx = moe.router_topk(x, W["router_w"], W.get("router_b"), s.top_k)
         self._moe_states[layer] = {"residual": h, "weights": weights, "indices": idx}
         if self.record_routing:
-            self._record_routing(layer, idx)
+            self._record_routing(layer, idx, x)
         return x.view(B0, n, s.hidden)
 
     def _run_moe_experts(self, hidden: torch.Tensor, *, layer: int, shard: tuple[int, int] | None = None,
@@ -416,10 +421,12 @@ class FluidRunner:
         st["fused"] = fuse
         return y.view(B0, n, s.hidden)
 
-    def _record_routing(self, layer: int, idx: torch.Tensor) -> None:
+    def _record_routing(self, layer: int, idx: torch.Tensor, x: torch.Tensor | None = None) -> None:
         self.last_routing[layer] = idx
+        if x is not None:
+            self.last_router_input[layer] = x.clone()
         if self.routing_log is not None:
-            self.routing_log.append((layer, self._n, idx.clone()))
+            self.routing_log.append((layer, self._n, idx.clone(), None if x is None else x.clone()))
 
     def _run_moe_combine(self, hidden: torch.Tensor, *, layer: int, out: torch.Tensor | None = None,
                          **_: Any) -> torch.Tensor:

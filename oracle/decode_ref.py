@@ -35,6 +35,7 @@ from __future__ import annotations
 import math
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 import torch.nn.functional as F
 
@@ -165,6 +166,78 @@ def topk_lowest(logits: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tenso
     vllm_integration.py:462-464)."""
     order = torch.sort(logits, dim=-1, descending=True, stable=True)
     return order.values[..., :k], order.indices[..., :k]
+
+
+# ---------------------------------------------------------------------------
+# router with exactly rounded bf16 logits (GptOssTopKRouter: linear -> topk
+# -> softmax over the top-k, the module the reference calls at
+# runner.py:432-442; top-k then softmax as vllm_integration.py:462-464)
+# ---------------------------------------------------------------------------
+def round_bf16_f64(v: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray, np.ndarray]:
+    """Nearest bf16 (ties to even) of float64 values, as float64.
+    Returns (rounded, tie mask, k, q) where k = v / 2^q, 2^q the bf16
+    quantum at v, so a tie is a k with fractional part exactly 1/2."""
+    v = np.asarray(v, dtype=np.float64)
+    _, ex = np.frexp(v)                      # v = m * 2^ex, 0.5 <= |m| < 1
+    q = np.maximum(ex - 8, -133)             # 8 significant bits, or the subnormal quantum
+    k = np.ldexp(v, -q)
+    r = np.rint(k)                           # round half to even
+    out = np.ldexp(r, q)
+    out = np.where(np.abs(out) >= 2.0 ** 128, np.copysign(np.inf, v), out)
+    tie = np.abs(k - np.trunc(k)) == 0.5
+    return out, tie, k, q
+
+
+def exact_linear_bf16(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None) -> torch.Tensor:
+    """bf16(x @ w.T + b) rounded once from the exact real value (ties to
+    even): x [T,H], w [E,H], b [E] bf16. Every bf16 x bf16 product is exact in
+    float64; math.fsum returns the correctly rounded float64 of their exact
+    sum, and its bf16 rounding equals the exact value's unless the float64
+    lies exactly on a bf16 midpoint, which exact rational arithmetic then
+    decides. This is the one value every bf16 linear with wider accumulation
+    approximates; the B200 router kernel computes the same (exact sums)."""
+    from fractions import Fraction
+
+    x64 = x.to(torch.float64).numpy()
+    w64 = w.to(torch.float64).numpy()
+    b64 = b.to(torch.float64).numpy() if b is not None else np.zeros(w64.shape[0])
+    T, E = x64.shape[0], w64.shape[0]
+    S = np.empty((T, E))
+    prods = x64[:, None, :] * w64[None, :, :]
+    for t in range(T):
+        for e in range(E):
+            S[t, e] = math.fsum(prods[t, e].tolist() + [float(b64[e])])
+    out, tie, k, q = round_bf16_f64(S)
+    for t, e in zip(*np.nonzero(tie)):
+        exact = sum(Fraction(p) for p in prods[t, e].tolist()) + Fraction(float(b64[e]))
+        if exact != Fraction(float(S[t, e])):  # not a true tie: round towards the exact value
+            r = math.ceil(k[t, e]) if exact > Fraction(float(S[t, e])) else math.floor(k[t, e])
+            out[t, e] = math.ldexp(r, int(q[t, e]))
+    return torch.from_numpy(out).to(torch.bfloat16)
+
+
+def softmax_topk_bf16(top_v: torch.Tensor) -> torch.Tensor:
+    """Softmax over the k selected logits (ordered by value): p_j =
+    exp(v_j - v_0) and their sum in selection order in float64, each weight
+    p_j / s rounded once to bf16 (GptOssTopKRouter's softmax in the router's
+    dtype)."""
+    v = top_v.to(torch.float64).numpy()
+    p = np.exp(v - v[..., :1])
+    s = np.zeros(v.shape[:-1])
+    for j in range(v.shape[-1]):
+        s = s + p[..., j]
+    out = round_bf16_f64(p / s[..., None])[0]
+    return torch.from_numpy(out).to(torch.bfloat16)
+
+
+def router_topk_exact(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None,
+                      k: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(weights bf16 [T,k], expert ids [T,k], logits bf16 [T,E]) of the
+    router on bf16 inputs: exactly rounded logits, top-k by value with the
+    lower expert id first on ties, softmax over the k."""
+    logits = exact_linear_bf16(x, w, b)
+    top_v, top_i = topk_lowest(logits.float(), k)
+    return softmax_topk_bf16(top_v), top_i, logits
 
 
 # ---------------------------------------------------------------------------
@@ -312,6 +385,10 @@ class OracleModel:
         # per layer, last step: each token's gap between its k-th and (k+1)-th
         # router logit (a small gap is a near tie that rounding may flip)
         self.router_margins: list[torch.Tensor] = []
+        # per layer, last step: the router's input x (normalised hidden), kept
+        # when record_router_inputs is set
+        self.record_router_inputs = False
+        self.router_inputs: list[torch.Tensor] = []
 
     def reset(self, batch: int) -> None:
         L = self.spec.num_layers
@@ -357,10 +434,17 @@ class OracleModel:
     def _moe_ffn(self, i: int, h: torch.Tensor) -> torch.Tensor:
         s = self.spec
         x = rms_norm(h, self.w[f"{i}.ln2"], s.eps, s.fp32_weight_mul)
-        logits = self._linear(x, f"{i}.router_w", f"{i}.router_b")
-        top_v, top_i = topk_lowest(logits, s.top_k)
-        scores = torch.softmax(top_v, dim=-1, dtype=top_v.dtype) if self.dtype != torch.float32 \
-            else torch.softmax(top_v, dim=-1)
+        if self.dtype == torch.bfloat16:
+            # bf16 router logits rounded once from their exact value (the
+            # order-independent result of the bf16 linear), softmax rounded once
+            scores, top_i, logits = router_topk_exact(x, self.w[f"{i}.router_w"], self.w.get(f"{i}.router_b"),
+                                                      s.top_k)
+        else:
+            logits = self._linear(x, f"{i}.router_w", f"{i}.router_b")
+            top_v, top_i = topk_lowest(logits, s.top_k)
+            scores = torch.softmax(top_v, dim=-1)
+        if self.record_router_inputs:
+            self.router_inputs.append(x.clone())
         self.router_indices.append(top_i.clone())
         if s.top_k < s.num_experts:
             kk = torch.topk(logits.float(), s.top_k + 1, dim=-1).values
@@ -391,6 +475,7 @@ class OracleModel:
         h = self.w["embed"][tokens.reshape(-1)]
         self.router_indices = []
         self.router_margins = []
+        self.router_inputs = []
         for i in range(s.num_layers):
             h = self._attention(i, h, positions)
             h = self._moe_ffn(i, h) if s.moe else self._dense_ffn(i, h)
