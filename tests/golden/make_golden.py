@@ -18,6 +18,10 @@ Fixtures (all small):
                      (the reference runner is batch 1, runner.py:67, :120).
                      Saved: greedy tokens [8, 32] and the top-64 logits
                      (values, indices) of every decision [8, 32, 64].
+  llama_c1_bf16.pt   The same config-1 run with the weights cast to bf16 and
+                     the runner in bf16 (EngineConfig's own dtype): the
+                     reference's bf16 path, which the B200 kernels' greedy
+                     tokens are compared with.
   llama_tiny_bf16.pt The reference tests' tiny bf16 Llama
                      (test_fine_dense_runtime.py:150-168) through the runner
                      with a split fine-grained plan: prefill logits of
@@ -146,12 +150,12 @@ def _run_both(runners, method, arg):
     return results[0]
 
 
-def make_c1(tmp: Path) -> dict:
-    model = c1_model(torch.float32)
+def make_c1(tmp: Path, dtype=torch.float32) -> dict:
+    model = c1_model(dtype)
     assign = []
     for i in range(C1["layers"]):
         assign += [(f"layer_{i}_attn", 0), (f"layer_{i}_mlp", 1)]
-    runners = _two_rank_runners(model, assign, 512, torch.float32, tmp, "c1")
+    runners = _two_rank_runners(model, assign, 512, dtype, tmp, "c1")
     prompts = c1_prompts()
     tokens = torch.zeros(C1["batch"], C1["steps"], dtype=torch.int64)
     vals = torch.zeros(C1["batch"], C1["steps"], C1["topk"])
@@ -166,8 +170,9 @@ def make_c1(tmp: Path) -> dict:
             tokens[b, s] = tok
             if s + 1 < C1["steps"]:
                 logits = _run_both(runners, "decode_step", torch.tensor([[tok]]))
+    name = "fp32" if dtype == torch.float32 else "bf16"
     return {"config": C1, "tokens": tokens, "top_values": vals, "top_indices": idxs,
-            "source": "fluidgpu_torch.runner.CausalLMRunner, 2 ranks (attn rank 0, mlp rank 1), fp32"}
+            "source": f"fluidgpu_torch.runner.CausalLMRunner, 2 ranks (attn rank 0, mlp rank 1), {name}"}
 
 
 def make_tiny_bf16(tmp: Path) -> dict:
@@ -200,17 +205,21 @@ def make_gptoss() -> dict:
     return out
 
 
-def main() -> None:
+def main(only: str | None = None) -> None:
     with tempfile.TemporaryDirectory() as d:
         tmp = Path(d)
-        torch.save(make_tiny_bf16(tmp), HERE / "llama_tiny_bf16.pt")
-        torch.save(make_gptoss(), HERE / "gptoss_tiny.pt")
-        torch.save(make_c1(tmp), HERE / "llama_c1_fp32.pt")
+        jobs = {"llama_tiny_bf16.pt": lambda: make_tiny_bf16(tmp), "gptoss_tiny.pt": make_gptoss,
+                "llama_c1_fp32.pt": lambda: make_c1(tmp),
+                "llama_c1_bf16.pt": lambda: make_c1(tmp, torch.bfloat16)}
+        for name, job in jobs.items():
+            if only is None or only == name:
+                torch.save(job(), HERE / name)
     for p in sorted(HERE.glob("*.pt")):
         print(p.name, p.stat().st_size)
 
 
 if __name__ == "__main__":
+    # make_golden.py <reference checkout> [fixture name]
     if len(sys.argv) > 1:
         sys.path.insert(0, str(Path(sys.argv[1]) / "fluidgpu_runtime"))
-    main()
+    main(sys.argv[2] if len(sys.argv) > 2 else None)

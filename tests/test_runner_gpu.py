@@ -1,15 +1,31 @@
-"""End-to-end decode parity: FluidRunner on the B200 against the CPU oracle on
-the same HF-initialised weights (bf16), teacher-forced on identical tokens.
+"""End-to-end decode parity at benchmark config 1's shape (4 layers, hidden
+1024, 16/4 heads, FFN 2816, vocab 32000, batch 8, 256-token prompts, 32
+greedy steps), bf16 weights.
 
-Tolerance (north star, bf16): |logit - oracle| <= 2e-2 + 1e-2 * |oracle|
-elementwise, or no worse than the reference's own bf16 arithmetic (see
-Judge); the greedy token must agree wherever the exact model's top-2 margin
-exceeds twice that bound (a closer call is a bf16 tie that summation order
-may break either way)."""
+- Teacher-forced: FluidRunner on the B200 against the CPU oracle on the same
+  weights. Tolerance (north star, bf16): |logit - oracle| <= 2e-2 + 1e-2 *
+  |oracle| elementwise, or no worse than the reference's own bf16
+  arithmetic (see Judge); the greedy token must agree wherever the exact
+  model's top-2 margin exceeds twice that bound (a closer call is a bf16 tie
+  that summation order may break either way). The number of steps that
+  needed the bf16-arithmetic fallback is reported.
+- Free-running: 32 greedy steps from the config-1 prompts against the
+  reference's own CausalLMRunner run in bf16 (tests/golden/llama_c1_bf16.pt,
+  top-64 logits of every decision). Along each sequence the GPU's token must
+  equal the reference's at every step; the one allowed exception is a step
+  whose reference top-2 margin is no larger than twice the GPU's measured
+  deviation from the reference logits at that very step (a tie at the bf16
+  noise floor, after which the two trajectories part). How many sequences
+  match all 32 steps, and every parting step with its margin and deviation,
+  is reported."""
+from pathlib import Path
+
 import pytest
 import torch
 
 from oracle import decode_ref as ref
+
+GOLD = Path(__file__).resolve().parent / "golden"
 
 pytestmark = pytest.mark.gpu
 
@@ -65,7 +81,7 @@ class Judge:
         self.err, self.ref_err, self.loose = 0.0, 0.0, []
 
     def prefill(self, prompts):
-        return self.truth.prefill_stepwise(prompts), self.bf16.prefill_stepwise(prompts)
+        return self.truth.prefill(prompts), self.bf16.prefill(prompts)
 
     def step(self, tok):
         return self.truth.step(tok), self.bf16.step(tok)
@@ -86,13 +102,15 @@ class Judge:
         assert torch.equal(ref.argmax_lowest(got)[decided], ref.argmax_lowest(truth)[decided]), (
             f"step {step}: greedy token mismatch")
 
-    def final(self):
+    def final(self, what=""):
+        print(f"{what}: {len(self.loose)} step(s) outside 2e-2 + 1e-2|x| of both oracles {self.loose}; "
+              f"worst max-abs {self.err:.4f}, reference-bf16 worst {self.ref_err:.4f}")
         assert not self.loose or self.err <= 1.25 * self.ref_err + 1e-3, (
             f"steps {self.loose} outside atol/rtol; worst max-abs {self.err:.4f} vs "
             f"reference-bf16 worst {self.ref_err:.4f}")
 
 
-@pytest.mark.parametrize("batch,prompt,steps", [(8, 24, 32), (3, 5, 8)])
+@pytest.mark.parametrize("batch,prompt,steps", [(8, 256, 32), (3, 5, 8)])
 def test_llama_decode_matches_oracle(batch, prompt, steps):
     from fluidgpu_b200 import kernels
 
@@ -110,29 +128,36 @@ def test_llama_decode_matches_oracle(batch, prompt, steps):
         got = eng.runner.decode_step(tok.cuda()).reshape(batch, -1)
         truth, bf16 = judge.step(tok)
         judge.check(got, truth, bf16, s)
-    judge.final()
+    judge.final(f"batch {batch} prompt {prompt}")
     kernels.check_device("llama decode")
 
 
-def test_greedy_generate_tokens_match_oracle():
-    """Free-running greedy decode for 32 steps (config-1 model shape, batch 8)."""
-    model = _tiny_llama()
-    batch, prompt, steps = 8, 16, 32
-    eng = _engine(model, batch, prompt + steps + 2)
-    w = ref.weights_from_hf(model)
-    oracle = ref.OracleModel(ref.spec_from_hf(model.config), {k: v.float() for k, v in w.items()},
-                             torch.float32)
-    g = torch.Generator().manual_seed(1)
-    prompts = torch.randint(0, model.config.vocab_size, (batch, prompt), generator=g)
+def test_config1_greedy_tokens_match_reference_runner():
+    """Free-running greedy decode of config 1 (batch 8, 256-token prompts, 32
+    steps) against the reference's CausalLMRunner in bf16 on the same
+    weights and prompts."""
+    from tests.golden import make_golden as mg
+
+    gold = torch.load(GOLD / "llama_c1_bf16.pt")
+    model = mg.c1_model(torch.bfloat16)
+    prompts = mg.c1_prompts()
+    batch, steps = prompts.shape[0], mg.C1["steps"]
+    eng = _engine(model, batch, prompts.shape[1] + steps + 2)
     toks, logits = eng.generate(prompts, steps)
-    exp_toks, exp_logits = oracle.generate(prompts, steps)
-    assert (toks[:, 0] == exp_toks[:, 0]).float().mean() >= 0.75
-    # tokens agree until the first step whose oracle decision is within tolerance
+    parted, worst = [], 0.0
     for b in range(batch):
         for s in range(steps):
-            if toks[b, s] != exp_toks[b, s]:
-                e = exp_logits[s][b].float()
-                top2 = e.topk(2).values
-                assert (top2[0] - top2[1]).item() <= 2 * (ATOL + RTOL * top2[0].abs().item()), (
-                    f"seq {b} step {s}: token {int(toks[b, s])} vs oracle {int(exp_toks[b, s])}")
-                break
+            idx = gold["top_indices"][b, s].long()
+            val = gold["top_values"][b, s].float()
+            dev = (logits[s][b].float()[idx] - val).abs().max().item()
+            worst = max(worst, dev)
+            if int(toks[b, s]) != int(gold["tokens"][b, s]):
+                margin = (val[0] - val[1]).item()
+                assert margin <= 2 * dev, (
+                    f"sequence {b} step {s}: token {int(toks[b, s])} vs reference {int(gold['tokens'][b, s])} "
+                    f"at margin {margin:.4f} > 2 x deviation {dev:.4f}")
+                parted.append((b, s, round(margin, 4), round(dev, 4)))
+                break  # the trajectories part here
+    print(f"config 1 greedy vs reference bf16 runner: {batch - len(parted)} of {batch} sequences equal over "
+          f"{steps} steps; parted at near ties (seq, step, margin, deviation): {parted}; "
+          f"worst top-64 deviation before parting {worst:.4f}")
