@@ -13,8 +13,10 @@
 //
 // Contract.
 //  - The first call on a device resolves the array's device address
-//    (cudaGetSymbolAddress, with that device current) and caches it; make
-//    that first call before any stream capture.
+//    (cudaGetSymbolAddress, with that device current) and caches it with
+//    the CUDA context it belongs to; make that first call before any stream
+//    capture. A call under a different context (after cudaDeviceReset, or a
+//    driver-API context of its own) resolves the address again.
 //  - Calls whose split partials would not fit in 8 MiB (see
 //    fg_attn_workspace_bytes) are rejected with FG_ERR_ARG before any work.
 //  - All calls on a device share the one array and it keeps the previous
@@ -23,6 +25,8 @@
 //    overlap on the GPU (different streams, no ordering) race on it.
 //  - Results are those of fg_paged_decode_attn with the same arguments.
 #pragma once
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "attention.cuh"
@@ -33,21 +37,54 @@ namespace attn {
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-static void* g_noalloc_addr[64] = {nullptr};
+constexpr int kNoAllocMaxDevices = 64;
+static void* g_noalloc_addr[kNoAllocMaxDevices] = {nullptr};
+static CUcontext g_noalloc_ctx[kNoAllocMaxDevices] = {nullptr};
 static std::mutex g_noalloc_mu;
+
+// The calling thread's current CUDA context (driver entry point, no -lcuda).
+static int current_context(CUcontext* ctx) {
+  static PFN_cuCtxGetCurrent_v4000 get = nullptr;
+  if (!get) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      set_last_error("fg_paged_decode_attn_noalloc: cuCtxGetCurrent unavailable");
+      return FG_ERR_CUDA;
+    }
+    get = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+  }
+  if (get(ctx) != CUDA_SUCCESS) {
+    set_last_error("fg_paged_decode_attn_noalloc: cuCtxGetCurrent failed");
+    return FG_ERR_CUDA;
+  }
+  return FG_OK;
+}
 
 // Device address of g_noalloc_scratch on the current device. The host-side
 // symbol is only a stand-in for the device array and must never be handed to
-// a kernel; the address comes from cudaGetSymbolAddress.
+// a kernel; the address comes from cudaGetSymbolAddress, cached per device
+// together with the context it was resolved in.
 static int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+  if (e != cudaSuccess) {
     set_last_error("fg_paged_decode_attn_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
     return FG_ERR_CUDA;
   }
+  if (dev < 0 || dev >= kNoAllocMaxDevices) {
+    set_last_error("fg_paged_decode_attn_noalloc: device ordinal %d is beyond the %d this entry point "
+                   "keeps addresses for", dev, kNoAllocMaxDevices);
+    return FG_ERR_ARG;
+  }
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
+  CUcontext ctx = nullptr;
+  if (g_noalloc_addr[dev] != nullptr) {
+    const int rc = current_context(&ctx);
+    if (rc) return rc;
+  }
+  if (g_noalloc_addr[dev] == nullptr || ctx != g_noalloc_ctx[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -55,7 +92,10 @@ static int noalloc_scratch(void** out) {
                      cudaGetErrorString(e));
       return FG_ERR_CUDA;
     }
+    const int rc = current_context(&ctx);  // the runtime made the device's context current
+    if (rc) return rc;
     g_noalloc_addr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_addr[dev];
   return FG_OK;
