@@ -145,6 +145,9 @@ def prompt_lengths(batch: int, context: int, mix: str, seed: int = 0) -> list[in
 
 
 def cpu_baseline_sample(batch: int, context: int) -> dict:
+    """The oracle port timed on the host cores: one decoder layer plus the
+    norm/lm_head/argmax tail at the full batch and context, fp32. The layer
+    count it stands for is stated in its own keys."""
     from oracle.cpu_baseline import LayerSample, host_threads, time_sample
     from fluidgpu_b200.model import LLAMA3_8B as S
 
@@ -155,42 +158,170 @@ def cpu_baseline_sample(batch: int, context: int) -> dict:
     sample.layer()  # warm-up
     r = time_sample(sample, S.num_layers, reps=2)
     return {"value": r["tokens_per_s"], "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sampled_layers": 1, "layers": S.num_layers,
+            "sampled_ms": {"layer": r["t_layer_s"] * 1e3, "head": r["t_head_s"] * 1e3},
             "sample": (f"oracle (CPU restatement, fp32) of 1 Llama-3-8B decoder layer + norm/lm_head/argmax"
-                       f" at batch {batch}, context {context}; step = 32 x {r['t_layer_s']:.3f} s"
-                       f" + {r['t_head_s']:.3f} s")}
+                       f" at batch {batch}, context {context}, timed; the value stands for "
+                       f"{S.num_layers} x layer + head = {r['step_s']:.2f} s per step")}
+
+
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+class ReferenceRunner:
+    """The reference's own decode path on the host cores: fluidgpu_torch's
+    CausalLMRunner + LayerExecutor (installed from the reference's source into
+    baseline/_ref), with every task of a Llama-3-8B-architecture model on rank
+    0, bf16 (EngineConfig's dtype), its LayerKVCache seeded with `context`
+    synthetic tokens. The reference runner decodes one sequence at a time
+    (it asserts a [1, 1] token, runner.py:120), so one step here is one token
+    of one sequence through embed, 32 x (attention, MLP), norm and lm_head,
+    and a batch of B sequences costs B such steps per token."""
+
+    def __init__(self, context: int, seed: int = 0) -> None:
+        import tempfile
+
+        sys.path.insert(0, str(REF_DIR))
+        from fluidgpu_torch.config import EngineConfig
+        from fluidgpu_torch.executor import LayerExecutor
+        from fluidgpu_torch.profile import load_profile, make_ranked_task_profile, owned_layer_ids
+        from fluidgpu_torch.runner import CausalLMRunner
+        from transformers.models.llama import LlamaConfig, LlamaForCausalLM
+        from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding
+
+        from fluidgpu_b200.model import LLAMA3_8B as S
+
+        cfg = LlamaConfig(num_hidden_layers=S.num_layers, vocab_size=S.vocab, hidden_size=S.hidden,
+                          intermediate_size=S.intermediate, num_attention_heads=S.n_q,
+                          num_key_value_heads=S.n_kv, head_dim=S.head_dim, rope_theta=S.rope_theta,
+                          max_position_embeddings=max(8192, context + 64))
+        with torch.device("meta"):
+            model = LlamaForCausalLM(cfg).to(torch.bfloat16)
+        model.to_empty(device="cpu")
+        g = torch.Generator().manual_seed(seed)
+        with torch.no_grad():
+            # N(0, 0.02) values: one seeded block of 2^20 tiled over each
+            # parameter (the step's work does not depend on the values)
+            block = (torch.randn(1 << 20, generator=g) * 0.02).to(torch.bfloat16)
+            for p in model.parameters():
+                flat = p.view(-1)
+                n, b = flat.numel(), block.numel()
+                q = n // b
+                if q:
+                    flat[: q * b].view(q, b).copy_(block.unsqueeze(0).expand(q, b))
+                if n > q * b:
+                    flat[q * b:].copy_(block[: n - q * b])
+            for m in model.modules():
+                if hasattr(m, "variance_epsilon"):
+                    m.weight.fill_(1.0)
+        model.model.rotary_emb = LlamaRotaryEmbedding(cfg)  # its buffers were left empty on meta
+        model.eval()
+        assign = []
+        for i in range(S.num_layers):
+            assign += [(f"layer_{i}_attn", 0), (f"layer_{i}_mlp", 0)]
+        max_len = context + 64
+        raw = make_ranked_task_profile(model=S.name, task_assignments=assign, hidden_size=S.hidden,
+                                       num_kv_heads=S.n_kv, head_dim=S.head_dim, max_seq_len=max_len)
+        self._tmp = tempfile.TemporaryDirectory()
+        path = Path(self._tmp.name) / "profile.json"
+        path.write_text(json.dumps(raw))
+        profile = load_profile(path, model_name=S.name, hf_config=cfg)
+        ecfg = EngineConfig(model_name=S.name, profiling_json=path, max_seq_len=max_len, device="cpu",
+                            strict_transformers_version=False)
+
+        class _OneRank:  # every task is on rank 0: nothing is ever sent
+            def get_rank(self):
+                return 0
+
+            def send_tensor(self, t, dst):
+                raise AssertionError("co-located plan sent a tensor")
+
+            def recv_tensor(self, t, src):
+                raise AssertionError("co-located plan received a tensor")
+
+            def broadcast_tensor(self, t, src=0):
+                return None
+
+        self.runner = CausalLMRunner(model, None, LayerExecutor(profile, ecfg, comm_backend=_OneRank()), ecfg,
+                                     owned_layer_ids(profile, 0))
+        kv = self.runner.kv_cache
+        with torch.no_grad():
+            kb = torch.randn(S.n_kv, context, S.head_dim, generator=g).to(torch.bfloat16)
+            for layer in range(S.num_layers):
+                kv.key_cache[layer][0, :, :context].copy_(kb)
+                kv.value_cache[layer][0, :, :context].copy_(kb)
+        kv.advance(context)
+        self.token = torch.tensor([[17]])
+
+    def step(self) -> float:
+        """One greedy decode step of the sequence; returns its seconds."""
+        t0 = time.perf_counter()
+        logits = self.runner.decode_step(self.token)
+        self.token = logits.reshape(1, -1).argmax(-1).view(1, 1)
+        return time.perf_counter() - t0
 
 
 def run_reference(args) -> None:
+    """The reference arm: the reference's own CPU decode path on the host
+    cores (ReferenceRunner) when its package is installed in baseline/_ref,
+    else the oracle port (cpu_baseline_sample), each step a bounded sample of
+    the workload that the line's keys state."""
     world, rank, local = dist_env()
     if rank != 0:
         return
-    from oracle.cpu_baseline import LayerSample, host_threads, time_sample
-    from fluidgpu_b200.model import LLAMA3_8B as S
+    from oracle.cpu_baseline import host_threads
 
     threads = host_threads()
     torch.set_num_threads(threads)
-    sample = LayerSample(S.hidden, S.n_q, S.n_kv, S.head_dim, S.intermediate, S.vocab, S.rope_theta,
-                         64, 4096)
-    with torch.inference_mode():
-        for _ in range(max(args.warmup, 0)):
-            sample.layer()
-    steps = []
-    for _ in range(args.steps):
-        r = time_sample(sample, S.num_layers, reps=1)
-        steps.append(r["step_s"])
-    step_s = statistics.mean(steps)
-    value = 64 / step_s
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": CONFIG,
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": "each step: 1 Llama-3-8B decoder layer + norm/lm_head/argmax at "
-                                   "batch 64, context 4096 on the host cores (the reference's CPU "
-                                   "algorithm restated in oracle/), scaled to 32 layers"},
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
+    ctx = args.context
+    common = {"impl": "reference", "metric": METRIC, "unit": "tokens/s", "n_gpus": args.gpus,
+              "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+              "vs_baseline": None, "data": "synthetic", "config": CONFIG}
+    if (REF_DIR / "fluidgpu_torch").is_dir():
+        t0 = time.perf_counter()
+        ref = ReferenceRunner(ctx)
+        setup_s = time.perf_counter() - t0
+        with torch.inference_mode():
+            for _ in range(max(args.warmup, 0)):
+                ref.step()
+            times = [ref.step() for _ in range(args.steps)]
+        step_s = statistics.mean(times)
+        value = 1.0 / step_s  # one token of one sequence per step
+        sample = (f"fluidgpu_torch CausalLMRunner + LayerExecutor (the reference, installed from its source), "
+                  f"every task on one rank, bf16, Llama-3-8B architecture, context {ctx}: each step is one "
+                  f"decode step of one sequence (the runner's batch is 1; a batch of 64 takes 64 such steps "
+                  f"per token), all 32 layers + norm + lm_head + argmax, {threads} threads")
+        line = {**common, "value": value, "ms_per_step": step_s * 1e3, "dtype": "bf16",
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                                 "sample": sample},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "tokens_per_step": 1, "setup_s": setup_s,
+                "cpu_port": cpu_baseline_sample(64, ctx)}
+    else:
+        from fluidgpu_b200.model import LLAMA3_8B as S
+        from oracle.cpu_baseline import LayerSample, time_sample
+
+        sample = LayerSample(S.hidden, S.n_q, S.n_kv, S.head_dim, S.intermediate, S.vocab, S.rope_theta,
+                             64, ctx)
+        with torch.inference_mode():
+            for _ in range(max(args.warmup, 0)):
+                sample.layer()
+        layer_s, head_s = [], []
+        for _ in range(args.steps):
+            r = time_sample(sample, S.num_layers, reps=1)
+            layer_s.append(r["t_layer_s"])
+            head_s.append(r["t_head_s"])
+        t_layer, t_head = statistics.mean(layer_s), statistics.mean(head_s)
+        full_step_s = S.num_layers * t_layer + t_head
+        value = 64 / full_step_s
+        line = {**common, "value": value, "ms_per_step": (t_layer + t_head) * 1e3, "dtype": "f32",
+                "sampled_layers": 1, "layers": S.num_layers, "scale": full_step_s / (t_layer + t_head),
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                 "sample": f"each timed step: 1 Llama-3-8B decoder layer + norm/lm_head/argmax "
+                                           f"at batch 64, context {ctx} (the oracle's restatement, fp32); "
+                                           f"value = 64 tokens / (32 x layer + head); the reference package "
+                                           f"is not installed in baseline/_ref"},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
