@@ -111,6 +111,27 @@ class _PeerMailbox:
         self.peers.clear()
 
 
+class _LocalMailbox:
+    """A mailbox in this process's device memory whose peers are other
+    _LocalMailbox objects of the same process and device (plain device
+    pointers, no IPC): the mailbox set of P2PComm.same_device_group."""
+
+    def __init__(self, world: int, nslot: int, slot_bytes: int, device: torch.device) -> None:
+        from . import _lib
+
+        nbytes = _lib.lib().fg_mailbox_bytes(world, nslot, slot_bytes)
+        assert nbytes > 0, f"bad mailbox geometry world={world} nslot={nslot} slot={slot_bytes}"
+        self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        self.peers: dict[int, tuple[int, int]] = {}
+
+    @property
+    def ptr(self) -> int:
+        return self.buf.data_ptr()
+
+    def close(self) -> None:
+        self.peers.clear()
+
+
 class _DeviceArray:
     """A CUDA array interface over a raw device pointer (a peer's slot), so
     torch can wrap it without copying."""
@@ -145,23 +166,59 @@ class P2PComm:
         import torch.distributed as dist
 
         assert dist.is_available() and dist.is_initialized(), "P2PComm needs torch.distributed"
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        slot = (int(slot_bytes) + 15) // 16 * 16
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        mb = _PeerMailbox(dist, group, rank, world, nslot, slot, device)
+        dmb = _PeerMailbox(dist, group, rank, world, 1, slot, device) if direct else None
+        self._setup(dist, group, rank, world, mb, dmb, slot, nslot, timeout_ms, tag, device)
+        dist.barrier(group=group)
+
+    def _setup(self, dist, group, rank: int, world: int, mb, dmb, slot_bytes: int, nslot: int,
+               timeout_ms: int, tag: int, device: torch.device) -> None:
         self._dist = dist
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
-        self.device = device or torch.device("cuda", torch.cuda.current_device())
-        self.slot_bytes = (int(slot_bytes) + 15) // 16 * 16
+        self.rank = rank
+        self.world = world
+        self.device = device
+        self.slot_bytes = slot_bytes
         self.nslot = nslot
         self.timeout_ms = timeout_ms
         self.tag = tag
-        self._mb = _PeerMailbox(dist, group, self.rank, self.world, nslot, self.slot_bytes, self.device)
-        self.mailbox = self._mb.buf
-        self.peers = self._mb.peers
-        self.direct = bool(direct)
-        self._dmb = (_PeerMailbox(dist, group, self.rank, self.world, 1, self.slot_bytes, self.device)
-                     if direct else None)
+        self._mb = mb
+        self.mailbox = mb.buf
+        self.peers = mb.peers
+        self.direct = dmb is not None
+        self._dmb = dmb
         self._views: dict[tuple, torch.Tensor] = {}
-        dist.barrier(group=group)
+
+    @classmethod
+    def same_device_group(cls, world: int, slot_bytes: int, *, nslot: int = 2, timeout_ms: int = 2000,
+                          device: torch.device | None = None, direct: bool = False) -> list["P2PComm"]:
+        """`world` ranks in one process on one device, one comm per rank:
+        each rank's mailbox lives in that device's memory and the others
+        address it directly (no IPC, no torch.distributed). The hand-off
+        kernels use the same slots, flags and sequence numbers as between
+        GPUs. Ranks that share a GPU must be ordered by the host: a rank's
+        receive (or wait) may only be enqueued behind the matching send (or
+        signal) through a CUDA event or the same stream, because two launches
+        on one GPU are not guaranteed to run at the same time, so a receive
+        left to spin on a send that has not started would only end at its
+        timeout. This serves single-GPU tests and debugging of multi-rank
+        plans."""
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        slot = (int(slot_bytes) + 15) // 16 * 16
+        mbs = [_LocalMailbox(world, nslot, slot, device) for _ in range(world)]
+        dmbs = [_LocalMailbox(world, 1, slot, device) for _ in range(world)] if direct else None
+        for boxes in (mbs, dmbs or []):
+            for r, box in enumerate(boxes):
+                box.peers.update({p: (boxes[p].ptr, 0) for p in range(world) if p != r})
+        comms = []
+        for r in range(world):
+            c = cls.__new__(cls)
+            c._setup(None, None, r, world, mbs[r], dmbs[r] if dmbs else None, slot, nslot, timeout_ms, 0, device)
+            comms.append(c)
+        return comms
 
     def get_rank(self) -> int:
         return self.rank
@@ -232,6 +289,7 @@ class P2PComm:
 
     def broadcast_tensor(self, t: torch.Tensor, src: int = 0) -> None:
         # src is a rank of this comm's group
+        assert self._dist is not None, "a same-device group has no process group to broadcast over"
         g = src if self.group is None else self._dist.get_global_rank(self.group, src)
         self._dist.broadcast(t, src=g, group=self.group)
 

@@ -112,6 +112,28 @@ class DecodeEngine:
         return self._next_dev
 
     @torch.inference_mode()
+    def step_static(self) -> torch.Tensor | None:
+        """One greedy step from the static token buffer into the static
+        next-token buffer, which also feeds the following step: a graph
+        replay when CUDA graphs are on, eager launches otherwise. Returns the
+        next-token buffer on the norm_lm_head rank, None elsewhere."""
+        assert self._tok_dev is not None, "call start() first"
+        if self.use_graph:
+            nxt = self.replay()
+            return nxt if self.runner.executor.task_rank("norm_lm_head", "decode") == self.rank else None
+        logits = self.runner.decode_step(self._tok_dev)
+        if logits is None:
+            return None
+        kernels.argmax(logits.reshape(logits.shape[0], -1), out=self._next_dev)
+        self._tok_dev.copy_(self._next_dev)
+        return self._next_dev
+
+    def set_tokens(self, tokens: torch.Tensor) -> None:
+        """Load the static token buffer (the next step's input) from tokens [B]."""
+        assert self._tok_dev is not None, "call start() first"
+        self._tok_dev.copy_(tokens.reshape(-1), non_blocking=True)
+
+    @torch.inference_mode()
     def step(self, tokens_host: torch.Tensor) -> torch.Tensor | None:
         """One greedy step from host tokens [B] to host tokens [B]."""
         assert self._tok_dev is not None, "call start() first"

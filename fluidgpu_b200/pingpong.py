@@ -10,7 +10,8 @@ M micro-batches each own a FluidRunner (their own paged-KV slice on the
 attention rank), a P2PComm channel set (their own mailboxes, so sequence
 numbers never mix) and a CUDA stream; the weights are shared. Each rank
 replays one captured decode-step graph per micro-batch on that
-micro-batch's stream. Within a rank the streams only meet at the SMs: while
+micro-batch's stream (or, with EngineConfig.cuda_graph_decode off, launches
+the step's kernels eagerly on it). Within a rank the streams only meet at the SMs: while
 micro-batch A waits in its receive kernel for the FFN rank, micro-batch B's
 attention runs, and the FFN rank works on A while the attention rank works
 on B. Earlier micro-batches get higher stream priority, as in the reference.
@@ -57,14 +58,16 @@ class PingPongEngine:
         return [e.kv_cache for e in self.engines]
 
     def step(self) -> list[torch.Tensor | None]:
-        """One decode step of every micro-batch (graph replays, interleaved)."""
+        """One decode step of every micro-batch, interleaved on their streams;
+        returns each micro-batch's next-token buffer on the norm_lm_head rank
+        (None elsewhere)."""
         outs = []
         cur = torch.cuda.current_stream(self.device)
         for s in self.streams:
             s.wait_stream(cur)
         for eng, s in zip(self.engines, self.streams):
             with torch.cuda.stream(s):
-                outs.append(eng.replay() if self.rank == 0 else (eng.replay(), None)[1])
+                outs.append(eng.step_static())
         for s in self.streams:
             cur.wait_stream(s)
         return outs
