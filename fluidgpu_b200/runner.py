@@ -42,6 +42,18 @@ Generalisations over the reference: a batch of B requests decodes together
 the KV cache is paged (kv_cache.PagedKVCache). prefill() feeds the prompt
 position by position through the decode kernels (causal attention makes the
 result identical to a full-sequence prefill).
+
+Drop-in: the runner also runs under the reference's own objects. Its
+executor may be fluidgpu_torch.executor.LayerExecutor (which forwards every
+extra keyword to the kernel-group callable and has no shard or hand-off
+extensions; then a batch larger than 1 only works where no hidden state
+crosses ranks, its receive buffers being [1, 1, H]), its cfg
+fluidgpu_torch.config.EngineConfig (no max_batch: one sequence), and the
+override points take the reference's keywords: `layer` as the HF decoder
+layer or its index, attention_mask / position_ids / past_key_value /
+use_cache / cache_position / position_embeddings (accepted and unused: the
+masks are implicit in the attention kernels, positions live in the paged
+cache), layer_id for the fine-grained groups.
 """
 from __future__ import annotations
 
@@ -72,8 +84,8 @@ class FluidRunner:
         self.kv_cache = PagedKVCache(
             num_layers=self.spec.num_layers, owned_layer_ids=owned_layer_ids,
             max_seq_len=cfg.max_seq_len, num_kv_heads=self.spec.n_kv, head_dim=self.spec.head_dim,
-            dtype=cfg.dtype, device=self.device, max_batch=cfg.max_batch, num_blocks=num_blocks,
-            allocation=cfg.kv_allocation)
+            dtype=cfg.dtype, device=self.device, max_batch=getattr(cfg, "max_batch", 1), num_blocks=num_blocks,
+            allocation=getattr(cfg, "kv_allocation", "vllm"))
         self._mode, self._n = "decode", 1
         self._moe_states: dict[int, dict[str, torch.Tensor]] = {}
         self._attn_states: dict[int, dict[str, torch.Tensor]] = {}
@@ -121,7 +133,7 @@ class FluidRunner:
             self.start(B)
         ids = input_ids.to(self.device)
         step = 1 if has_fine_groups(self.executor.profile) else max(1, chunk or self.prefill_chunk)
-        cap = self.executor.message_capacity()
+        cap = self.executor.message_capacity() if hasattr(self.executor, "message_capacity") else None
         if cap is not None and self.executor.profile.rank_count > 1:
             # every hand-off of a chunk must fit one mailbox slot
             step = max(1, min(step, cap // self.max_message_bytes(B)))
@@ -209,14 +221,18 @@ class FluidRunner:
     # -- kernel groups (override points of the reference runner) ---------------
     # `out`: where the group's result must land (the next rank's slot of a
     # zero-copy hand-off); the group's last kernel writes there directly
-    def _embed(self, tokens: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    def _embed(self, tokens: torch.Tensor, out: torch.Tensor | None = None, **_: Any) -> torch.Tensor:
         B, n = tokens.shape
         o = kernels.embed(tokens.reshape(-1).contiguous(), self.weights.embed,
                           out=None if out is None else out.view(B * n, -1))
         return o.view(B, n, -1) if out is None else out
 
-    def _run_attn(self, hidden: torch.Tensor, *, layer: int, out: torch.Tensor | None = None,
+    def _run_attn(self, hidden: torch.Tensor, *, layer: Any, out: torch.Tensor | None = None,
+                  attention_mask: Any = None, position_ids: Any = None, past_key_value: Any = None,
+                  use_cache: bool = True, cache_position: Any = None, position_embeddings: Any = None,
                   **_: Any) -> torch.Tensor:
+        """The attention group (runner.py:170-194, same keywords)."""
+        layer = _layer_index(layer)
         s = self.spec
         W = self.weights.layers[layer]
         kv = self.kv_cache
@@ -253,7 +269,9 @@ class FluidRunner:
         return seq, pos.to(torch.int32).contiguous()
 
     # fine attention groups (runner.py:256-347)
-    def _run_attn_qkv(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+    def _run_attn_qkv(self, hidden: torch.Tensor, *, layer: Any, layer_id: int | None = None,
+                      **_: Any) -> torch.Tensor:
+        layer = _layer_index(layer, layer_id)
         s = self.spec
         W = self.weights.layers[layer]
         B = hidden.shape[0]
@@ -263,7 +281,9 @@ class FluidRunner:
         self._attn_states[layer] = {"residual": h, "qkv": qkv}
         return x.view(B, 1, s.hidden)
 
-    def _run_attn_sdpa(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+    def _run_attn_sdpa(self, hidden: torch.Tensor, *, layer: Any, layer_id: int | None = None,
+                       **_: Any) -> torch.Tensor:
+        layer = _layer_index(layer, layer_id)
         s = self.spec
         W = self.weights.layers[layer]
         kv = self.kv_cache
@@ -278,7 +298,9 @@ class FluidRunner:
                                       slot=self.slot + ".attn")
         return a.view(B, 1, s.n_q * s.head_dim)
 
-    def _run_attn_o_proj(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+    def _run_attn_o_proj(self, hidden: torch.Tensor, *, layer: Any, layer_id: int | None = None,
+                         **_: Any) -> torch.Tensor:
+        layer = _layer_index(layer, layer_id)
         s = self.spec
         W = self.weights.layers[layer]
         B = hidden.shape[0]
@@ -316,8 +338,10 @@ class FluidRunner:
             st["residual"] = self._recv_aux((B, self.spec.hidden), torch.bfloat16, src)
         return st
 
-    def _run_mlp(self, hidden: torch.Tensor, *, layer: int, shard: tuple[int, int] | None = None,
+    def _run_mlp(self, hidden: torch.Tensor, *, layer: Any, shard: tuple[int, int] | None = None,
                  out: torch.Tensor | None = None, **_: Any) -> torch.Tensor:
+        """The FFN group (runner.py:349-352, same keywords)."""
+        layer = _layer_index(layer)
         s = self.spec
         W = self.weights.layers[layer]
         B0, n = hidden.shape[0], hidden.shape[1]
@@ -338,7 +362,9 @@ class FluidRunner:
         return o.view(B0, n, s.hidden) if out is None else out
 
     # fine dense FFN groups (runner.py:416-430)
-    def _run_mlp_gate_up(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+    def _run_mlp_gate_up(self, hidden: torch.Tensor, *, layer: Any, layer_id: int | None = None,
+                         **_: Any) -> torch.Tensor:
+        layer = _layer_index(layer, layer_id)
         s = self.spec
         W = self.weights.layers[layer]
         B = hidden.shape[0]
@@ -348,7 +374,9 @@ class FluidRunner:
         self._mlp_states[layer] = {"residual": h, "intermediate": act}
         return x.view(B, 1, s.hidden)
 
-    def _run_mlp_down_proj(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+    def _run_mlp_down_proj(self, hidden: torch.Tensor, *, layer: Any, layer_id: int | None = None,
+                           **_: Any) -> torch.Tensor:
+        layer = _layer_index(layer, layer_id)
         s = self.spec
         W = self.weights.layers[layer]
         B = hidden.shape[0]
@@ -370,9 +398,11 @@ class FluidRunner:
         self._send_aux(st["intermediate"], dst)
         self._send_aux(st["residual"], dst)
 
-    def _run_moe_router(self, hidden: torch.Tensor, *, layer: int, **_: Any) -> torch.Tensor:
+    def _run_moe_router(self, hidden: torch.Tensor, *, layer: Any, layer_id: int | None = None,
+                        **_: Any) -> torch.Tensor:
         from . import moe
 
+        layer = _layer_index(layer, layer_id)
         s = self.spec
         W = self.weights.layers[layer]
         B0, n = hidden.shape[0], hidden.shape[1]
@@ -385,10 +415,11 @@ class FluidRunner:
             self._record_routing(layer, idx, x)
         return x.view(B0, n, s.hidden)
 
-    def _run_moe_experts(self, hidden: torch.Tensor, *, layer: int, shard: tuple[int, int] | None = None,
-                         **_: Any) -> torch.Tensor:
+    def _run_moe_experts(self, hidden: torch.Tensor, *, layer: Any, shard: tuple[int, int] | None = None,
+                         layer_id: int | None = None, **_: Any) -> torch.Tensor:
         from . import moe
 
+        layer = _layer_index(layer, layer_id)
         s = self.spec
         B0, n = hidden.shape[0], hidden.shape[1]
         B = B0 * n  # token rows
@@ -428,10 +459,11 @@ class FluidRunner:
         if self.routing_log is not None:
             self.routing_log.append((layer, self._n, idx.clone(), None if x is None else x.clone()))
 
-    def _run_moe_combine(self, hidden: torch.Tensor, *, layer: int, out: torch.Tensor | None = None,
-                         **_: Any) -> torch.Tensor:
+    def _run_moe_combine(self, hidden: torch.Tensor, *, layer: Any, out: torch.Tensor | None = None,
+                         layer_id: int | None = None, **_: Any) -> torch.Tensor:
         from . import moe
 
+        layer = _layer_index(layer, layer_id)
         B0, n = hidden.shape[0], hidden.shape[1]
         B = B0 * n  # token rows
         self._ensure_residual(self._moe_states, layer, B, src=self._rank_of(layer, "moe_experts"))
@@ -477,11 +509,12 @@ class FluidRunner:
 
     # -- aux routing (runner.py:462-670) ----------------------------------------
     def _rank_of(self, layer: int, suffix: str) -> int:
-        return self.executor.task_rank(f"layer_{layer}_{suffix}", "decode")
+        ex = self.executor
+        return ex.tasks[ex.task_index_by_name[f"layer_{layer}_{suffix}"]].rank_for("decode")
 
     def _shards_of(self, layer: int, suffix: str) -> tuple[int, ...] | None:
         ex = self.executor
-        return ex.tasks[ex.task_index_by_name[f"layer_{layer}_{suffix}"]].shard_ranks
+        return getattr(ex.tasks[ex.task_index_by_name[f"layer_{layer}_{suffix}"]], "shard_ranks", None)
 
     def _send_aux(self, t: torch.Tensor, dst: int) -> None:
         self.executor.send_aux_tensor(t if t.is_contiguous() else t.contiguous(), dst=dst)
@@ -496,7 +529,7 @@ class FluidRunner:
         if "residual" not in st:
             st["residual"] = self._recv_aux((B, self.spec.hidden), torch.bfloat16, src)
 
-    def _norm_head(self, hidden: torch.Tensor) -> torch.Tensor:
+    def _norm_head(self, hidden: torch.Tensor, **_: Any) -> torch.Tensor:
         s = self.spec
         B = hidden.shape[0]
         if hidden.dim() == 3 and hidden.shape[1] > 1:  # a prefill chunk: the last position only
@@ -504,7 +537,7 @@ class FluidRunner:
         x = kernels.rmsnorm(hidden.reshape(B, s.hidden), self.weights.final_norm, s.eps, s.norm_mode)
         return kernels.gemm(x, self.weights.lm_head, slot=self.slot + ".gemm").view(B, 1, s.vocab)
 
-    def _skip_head(self, hidden: torch.Tensor) -> torch.Tensor:
+    def _skip_head(self, hidden: torch.Tensor, **_: Any) -> torch.Tensor:
         return hidden
 
     def max_message_bytes(self, batch: int) -> int:
@@ -518,7 +551,7 @@ class FluidRunner:
             sizes += [batch * s.qkv_width * 2, batch * s.n_q * s.head_dim * 2]
         if any(n.endswith("_mlp_gate_up") for n in names):
             sizes.append(batch * s.intermediate * 2)
-        if any(t.shard_ranks is not None for t in self.executor.tasks):
+        if any(getattr(t, "shard_ranks", None) is not None for t in self.executor.tasks):
             sizes.append(batch * s.hidden * 4)  # fp32 partials
         return max(sizes)
 
@@ -536,3 +569,16 @@ class FluidRunner:
             shapes += [(2 * s.intermediate, s.hidden), (s.hidden, s.intermediate)]
         gemm = max(lib.fg_gemm_workspace_bytes(batch, n, k, 0) for n, k in shapes)
         kernels.Workspace.get(gemm, self.device, self.slot + ".gemm")
+
+
+def _layer_index(layer: Any, layer_id: int | None = None) -> int:
+    """Layer index from the override point's arguments: an int (this
+    runner's walk), layer_id (the reference's fine-grained groups), or the
+    HF decoder layer the reference's walk passes (its self_attn.layer_idx)."""
+    if isinstance(layer, int):
+        return layer
+    if layer_id is not None:
+        return int(layer_id)
+    idx = getattr(getattr(layer, "self_attn", None), "layer_idx", None)
+    assert idx is not None, f"cannot tell the layer index of {type(layer).__name__}"
+    return int(idx)
