@@ -19,8 +19,14 @@ roofline: paged attention (the dominant kernel, ~60% of the step), its
         duration from CUDA event pairs around each of its launches during R
         steps run right after the timed region from the host (the same
         kernels and split plans the graph replays).
-Under torchrun (N > 1) every rank decodes its own batch of 64 requests
-(attention data-parallel by request, co-located FFN: weak scaling).
+Under torchrun (N > 1) the default is the disaggregated step
+(fluidgpu_b200.disagg): the first N/2 GPUs hold attention for 64 requests
+each (2 ping-pong micro-batches of 32), the other N/2 hold the FFN
+tensor-parallel over the intermediate dimension (one GPU at N = 2), every
+FFN GPU merging all attention GPUs' rows of a micro-batch into one GEMM per
+layer; hidden states cross NVLink as stores from the producing GEMM's
+epilogue (weak scaling in the attention GPUs). --mode replicas runs N
+independent co-located engines instead.
 """
 from __future__ import annotations
 
@@ -479,11 +485,213 @@ def run_fgb200(args) -> None:
         dist.destroy_process_group()
 
 
+def run_disagg_fused(args) -> None:
+    """The disaggregated decode step of fluidgpu_b200.disagg on N GPUs: N/2
+    attention GPUs with `batch` sequences each in M micro-batches, N/2 FFN
+    GPUs (tensor-parallel, merged batches), fused NVLink hand-offs; every
+    rank replays its CUDA graphs."""
+    world, rank, local = dist_env()
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    from fluidgpu_b200 import build, kernels
+    from fluidgpu_b200.disagg import AttentionRank, DisaggLayout, Fabric, FFNRank, nvlink_bytes_per_step
+    from fluidgpu_b200.model import LLAMA3_8B as spec
+    from fluidgpu_b200.model import ModelWeights
+
+    build.build()
+    M = args.micro_batches
+    B = args.batch or 64
+    assert B % M == 0, f"--batch {B} must split into {M} micro-batches"
+    b = B // M
+    lay = DisaggLayout.split(world, M, b)
+    role, idx = lay.role(rank)
+    ctx, W, K, R = args.context, args.warmup, args.steps, 3
+    total = ctx + W + 2 * K + 3 * R + 8
+    weights = ModelWeights.random(spec, seed=0, device=dev,
+                                  ffn_shard=(idx, lay.S) if role == "ffn" and lay.S > 1 else None)
+    if role == "attn":
+        r = AttentionRank(lay, rank, weights, total, device=dev)
+        lens = [prompt_lengths(b, ctx, args.prompt_mix, seed=rank * M + m) for m in range(M)]
+        r.start(lens, reserve_tokens=total)
+        g = torch.Generator(device=dev).manual_seed(1 + rank)
+        for m, mb in enumerate(r.mbs):
+            mb["kv"].pool.normal_(0.0, 1.0, generator=g)
+            r.set_tokens(m, torch.randint(0, spec.vocab, (b,), generator=g, device=dev))
+    else:
+        r = FFNRank(lay, rank, weights, device=dev)
+    imports = Fabric.ipc(r)
+
+    def step(graphs=True):
+        r.step(graphs=graphs)
+
+    n0 = kernels.launch_count()
+    step(graphs=False)  # one eager step: the launches a step issues
+    launches = kernels.launch_count() - n0
+    for _ in range(max(W - 1, 1)):
+        step()
+    torch.cuda.synchronize()
+    kernels.check_device("disagg warm-up")
+
+    sampler = ClockSampler(local)
+    dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    kernels.check_device("disagg timed region")
+
+    # ---- end to end: host tokens in, host tokens out, every step ----
+    host_in = [torch.zeros(b, dtype=torch.int64).pin_memory() for _ in range(M)]
+    host_out = [torch.zeros(b, dtype=torch.int64).pin_memory() for _ in range(M)]
+    if role == "attn":
+        for m, mb in enumerate(r.mbs):
+            host_in[m].copy_(mb["tok"])
+    dist.barrier()
+    torch.cuda.synchronize()
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(K):
+        if role == "attn":
+            for m in range(M):
+                r.set_tokens(m, host_in[m].to(dev, non_blocking=True))
+            outs = r.step(graphs=True)
+            for m in range(M):
+                host_out[m].copy_(outs[m], non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            host_in, host_out = host_out, host_in
+        else:
+            r.step(graphs=True)
+    f1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e2e_ms = f0.elapsed_time(f1)
+
+    # ---- per-role kernel times from event pairs on the launching stream ----
+    # FFN GPUs: R eager steps of every rank (the FFN GEMM pair after each wait)
+    if role == "ffn":
+        kernels.KernelTimer.enable("ffn")
+    for _ in range(R):
+        step(graphs=False)
+    torch.cuda.synchronize()
+    timed = kernels.KernelTimer.durations_ms("ffn") if role == "ffn" else []
+    kernels.KernelTimer.disable()
+    kernels.check_device("disagg roofline region")
+    dist.barrier()
+    role_stats = {}
+    if role == "attn":
+        # attention GPUs: the attention-side kernels alone (FFN left out), one
+        # micro-batch after another on one stream, so launches do not overlap
+        lens0 = [mb["kv"].seq_lengths() for mb in r.mbs]
+        kernels.KernelTimer.enable("attn")
+        for _ in range(R):
+            r.step_serial_standalone()
+        torch.cuda.synchronize()
+        timed = kernels.KernelTimer.durations_ms("attn")
+        kernels.KernelTimer.disable()
+        tot_b, tot_ms = 0.0, 0.0
+        for i, (d, meta) in enumerate(timed):
+            st, m = i // (M * spec.num_layers), (i // spec.num_layers) % M
+            tot_b += attn_bytes(meta, sum(l + 1 + st for l in lens0[m]))
+            tot_ms += d
+        role_stats = {"attn_bytes": tot_b, "attn_ms": tot_ms, "attn_launches": len(timed)}
+        # the same attention-side work with the FFN left out, on the step's
+        # streams: what the hand-offs and the remote FFN add to the step
+        for _ in range(R):
+            r.step(graphs=True, standalone=True)
+        torch.cuda.synchronize()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(R):
+            r.step(graphs=True, standalone=True)
+        a1.record()
+        torch.cuda.synchronize()
+        role_stats["alone_ms_per_step"] = a0.elapsed_time(a1) / R
+    else:
+        tot_ms = sum(d for d, _ in timed)
+        tot_b = sum(3.0 * meta["H"] * meta["I"] * 2 + meta["T"] * meta["H"] * 2 * 2 for _, meta in timed)
+        tot_f = sum(2.0 * meta["T"] * 3 * meta["H"] * meta["I"] for _, meta in timed)
+        role_stats = {"ffn_bytes": tot_b, "ffn_flops": tot_f, "ffn_ms": tot_ms, "ffn_pairs": len(timed),
+                      "T": timed[0][1]["T"] if timed else 0}
+    kernels.check_device("disagg stand-alone region")
+    t = torch.tensor([ms, e2e_ms, float(launches)], device=dev)
+    dist.all_reduce(t[:2], op=dist.ReduceOp.MAX)
+    dist.all_reduce(t[2:], op=dist.ReduceOp.SUM)
+    ms, e2e_ms, launches_all = float(t[0]), float(t[1]), int(t[2])
+    stats: list = [None] * world
+    dist.all_gather_object(stats, (role, role_stats))
+    if rank == 0:
+        peaks = measured_peaks()
+        hbm = peaks.get("hbm_gbs") or 6650.0
+        peak_src = "measured" if peaks.get("hbm_gbs") else "fallback"
+        tflops = peaks.get("bf16_tflops_sustained") or 1400.0
+        a_stats = [s for ro, s in stats if ro == "attn"]
+        f_stats = [s for ro, s in stats if ro == "ffn"]
+        attn_gbs = sum(s["attn_bytes"] for s in a_stats) / (sum(s["attn_ms"] for s in a_stats) * 1e-3) / 1e9
+        ffn_ms = sum(s["ffn_ms"] for s in f_stats)
+        ffn_gbs = sum(s["ffn_bytes"] for s in f_stats) / (ffn_ms * 1e-3) / 1e9
+        ffn_tf = sum(s["ffn_flops"] for s in f_stats) / (ffn_ms * 1e-3) / 1e12
+        step_ms = ms / K
+        alone = max(s["alone_ms_per_step"] for s in a_stats)
+        nv = nvlink_bytes_per_step(lay, spec.hidden, spec.num_layers)
+        tokens = lay.A * M * b * K
+        line = {
+            "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {**CONFIG, "batch_per_gpu": B, "attention_gpus": lay.A, "ffn_gpus": lay.S,
+                       "micro_batches": M, "sequences_per_micro_batch": b,
+                       "parallelism": (f"disaggregated: attention dp{lay.A} / FFN tp{lay.S}, {M} ping-pong micro-"
+                                       f"batches of {b} per attention GPU, FFN batches merged over the attention "
+                                       f"GPUs ({lay.A * b} tokens), hand-offs stored by the producing GEMM over NVLink"),
+                       **({"prompt_lens": f"uniform [128, {ctx}], seeded per micro-batch"}
+                          if args.prompt_mix == "uniform" else {})},
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": lay.A * M * b * 8, "d2h_bytes_per_step": lay.A * M * b * 8},
+            "roofline": {"bound": "hbm", "kernel": "fg_paged_decode_attn (attention GPUs)", "achieved": attn_gbs,
+                         "peak": hbm, "unit": "GB/s", "frac": attn_gbs / hbm, "peak_source": f"{peak_src} (hbm_gbs)",
+                         "traffic": None},
+            "ffn_roofline": {"kernel": "gate_up + down GEMMs (FFN GPUs)", "tokens_per_gemm": f_stats[0]["T"],
+                             "achieved_gbs": ffn_gbs, "hbm_frac": ffn_gbs / hbm, "achieved_tflops": ffn_tf,
+                             "tensor_frac": ffn_tf / tflops, "tensor_peak_source": "measured (bf16_tflops_sustained)"},
+            "handoff": {"nvlink_bytes_per_step": nv, "nvlink_us_per_step_at_770GBs": nv / 770e9 * 1e6,
+                        "attention_alone_ms_per_step": alone,
+                        "exposed_frac": max(0.0, 1.0 - alone / step_ms),
+                        "note": "exposed_frac = 1 - (attention GPU's own kernels, FFN left out) / step: what the "
+                                "hand-offs and the remote FFN add to the attention GPUs' step"},
+            "gpu_launches": launches_all * K,
+            "cuda_graph": True,
+            "clocks": clocks,
+            "mode": "disagg",
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    r.release_graphs()
+    torch.cuda.synchronize()
+    dist.barrier()
+    imports.close()
+    dist.destroy_process_group()
+
+
 def run_disagg(args) -> None:
     """Disaggregated decode over NVLink (P2PComm hand-offs, no NCCL on the data
-    path), every rank replaying captured graphs, M ping-pong micro-batches of
-    `batch` sequences per attention rank:
-      disagg : attention (+ embed, head) on GPU 0, the FFN on GPU 1 (config 2)
+    path) driven by a placement plan through the executor, every rank replaying
+    captured graphs, M ping-pong micro-batches of `batch` sequences per
+    attention rank:
+      pipeline : attention (+ embed, head) on GPU 0, the FFN on GPU 1 (config 2)
       tp     : attention data-parallel on the first half of the GPUs, each
                layer's dense FFN tensor-parallel over the second half (config 4)
       ep     : gpt-oss, attention data-parallel on the first half, the experts
@@ -507,8 +715,8 @@ def run_disagg(args) -> None:
 
     build.build()
     mode = args.mode
-    if mode == "disagg":
-        assert world == 2, "--mode disagg runs on two GPUs (attention rank 0, FFN rank 1)"
+    if mode == "pipeline":
+        assert world == 2, "--mode pipeline runs on two GPUs (attention rank 0, FFN rank 1)"
         attn_ranks, ffn_ranks = [0], [1]
     else:
         assert world >= 2 and world % 2 == 0, f"--mode {mode} needs an even number of GPUs"
@@ -521,7 +729,7 @@ def run_disagg(args) -> None:
 
     # one process group per pipeline: its attention rank is the plan's rank 0
     # (embed and head there), the FFN ranks follow in order
-    if mode == "disagg":
+    if mode == "pipeline":
         raw = attn_ffn_profile(spec.name, spec.num_layers, spec.hidden, spec.n_kv, spec.head_dim, total)
     else:
         raw = sharded_ffn_profile(spec.name, spec.num_layers, spec.hidden, spec.n_kv, spec.head_dim, total,
@@ -536,7 +744,7 @@ def run_disagg(args) -> None:
     slot = max(B * spec.hidden * 4, B * spec.qkv_width * 2)
     # zero-copy main-path hand-offs where the plan allows them (disagg)
     comms = {(a, m): P2PComm(slot_bytes=slot, nslot=2, group=groups[a], tag=m, timeout_ms=10000,
-                             direct=mode == "disagg")
+                             direct=mode == "pipeline")
              for a in mine for m in range(M)}
     pps = [PingPongEngine(weights, cfg, prof, lambda m, a=a: comms[(a, m)], micro_batches=M) for a in mine]
     g = torch.Generator(device=dev).manual_seed(1)
@@ -575,7 +783,7 @@ def run_disagg(args) -> None:
     ms = float(t[0])
     tokens = len(attn_ranks) * M * B * K
     if rank == 0:
-        par = {"disagg": "attention GPU0 / FFN GPU1",
+        par = {"pipeline": "attention GPU0 / FFN GPU1",
                "tp": f"attention dp{len(attn_ranks)} / FFN tp{len(ffn_ranks)} (reduce-by-consumer)",
                "ep": f"attention dp{len(attn_ranks)} / experts ep{len(ffn_ranks)} (reduce-by-consumer)"}[mode]
         line = {
@@ -611,18 +819,27 @@ def main() -> None:
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch every kernel from the host (no CUDA graph)")
-    ap.add_argument("--mode", default="replicas", choices=["replicas", "disagg", "tp", "ep"],
-                    help="N>1: independent co-located replicas (default); attention/FFN disaggregation "
-                         "(disagg: 2 GPUs; tp: dense FFN tensor-parallel; ep: gpt-oss experts split)")
-    ap.add_argument("--micro-batches", type=int, default=2, help="ping-pong micro-batches (disagg)")
+    ap.add_argument("--mode", default="auto", choices=["auto", "replicas", "disagg", "pipeline", "tp", "ep"],
+                    help="auto: co-located at N=1, disagg at N>1. disagg: attention / merged-batch FFN GPUs with "
+                         "fused hand-offs (fluidgpu_b200.disagg); replicas: N independent co-located engines; "
+                         "pipeline / tp / ep: placement plans through the executor with P2PComm (pipeline: "
+                         "2 GPUs; tp: dense FFN tensor-parallel; ep: gpt-oss experts split)")
+    ap.add_argument("--micro-batches", type=int, default=2,
+                    help="ping-pong micro-batches per attention GPU (disagg, pipeline, tp, ep)")
     ap.add_argument("--prompt-mix", default="fixed", choices=["fixed", "uniform"],
                     help="prompt lengths: all --context (default), or seeded uniform in [128, --context] "
                          "per sequence (config 4's request mix)")
     args = ap.parse_args()
     assert args.warmup >= 0 and args.steps > 0
+    world = dist_env()[0]
+    mode = args.mode if args.mode != "auto" else ("disagg" if world > 1 else "replicas")
+    args.mode = mode
     if args.impl == "reference":
         run_reference(args)
-    elif args.mode in ("disagg", "tp", "ep"):
+    elif mode == "disagg":
+        assert args.model == "llama-3-8b", "the disaggregated step serves the dense model (gpt-oss: --mode ep)"
+        run_disagg_fused(args)
+    elif mode in ("pipeline", "tp", "ep"):
         run_disagg(args)
     else:
         run_fgb200(args)

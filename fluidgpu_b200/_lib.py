@@ -33,6 +33,9 @@ FG_EPI_F32 = 4
 FG_NORM_LLAMA = 0
 FG_NORM_FP32MUL = 1
 
+FG_ROUTE_SPLIT = 1
+FG_ROUTE_BROADCAST = 2
+
 # name -> (restype, argtypes); every symbol include/fgb200.h declares
 SIGNATURES: dict[str, tuple] = {
     "fg_last_error": (ctypes.c_char_p, []),
@@ -43,6 +46,11 @@ SIGNATURES: dict[str, tuple] = {
     "fg_rmsnorm": (c_int, [_P, _P, _P, c_int, c_int, c_float, c_int, _P]),
     "fg_gemm_bf16": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, c_size_t, _P]),
     "fg_gemm_bf16_packed": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, c_size_t, _P]),
+    "fg_gemm_bf16_packed_routed": (
+        c_int,
+        [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, c_int, c_int, c_int, _P, c_int, _P, c_uint,
+         c_uint, _P, _P],
+    ),
     "fg_pack_weight_bf16": (c_int, [_P, _P, c_int, c_int, _P]),
     "fg_packed_weight_bytes": (c_size_t, [c_int, c_int]),
     "fg_gemm_grid": (c_int, [c_int, c_int, c_int, c_int]),
@@ -100,7 +108,24 @@ SIGNATURES: dict[str, tuple] = {
     "fg_mailbox_slot": (_P, [_P, c_int, c_int, c_size_t, c_int, c_int]),
     "fg_handoff_signal": (c_int, [_P, _P, c_int, c_int, c_int, c_size_t, _P]),
     "fg_handoff_wait": (c_int, [_P, c_int, c_int, c_int, c_size_t, c_int, _P]),
+    "fg_rmsnorm_wait": (
+        c_int, [_P, _P, _P, c_int, c_int, c_float, c_int, _P, c_int, c_int, _P, c_uint, c_uint, c_int, _P],
+    ),
+    "fg_sum_rmsnorm_wait": (
+        c_int,
+        [_P, c_int, _P, _P, _P, c_int, c_int, c_float, c_int, _P, c_int, _P, c_uint, c_uint, c_int, _P],
+    ),
+    "fg_counter_add": (c_int, [_P, c_uint, _P]),
 }
+
+
+def ptr_array(ptrs) -> ctypes.Array:
+    """A C array of void* (the pointer-array arguments of the routed hand-off
+    entry points); keep it alive for the duration of the call."""
+    arr = (c_void_p * max(len(ptrs), 1))()
+    for i, p in enumerate(ptrs):
+        arr[i] = p
+    return arr
 
 
 def lib_path() -> Path:

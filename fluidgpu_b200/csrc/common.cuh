@@ -51,6 +51,36 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 constexpr uint64_t kMbarTimeoutNs = 2000000000ull;  // 2 s
 
 // ---------------------------------------------------------------------------
+// flags written by another GPU (system scope)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// spin (bounded) until *p reaches seq (wrap-safe); false on timeout, after
+// recording a peer flag timeout at `site` in the device status word
+__device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t seq, uint64_t timeout_ns,
+                                              unsigned int site) {
+  if ((int32_t)(ld_acquire_sys(p) - seq) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if ((int32_t)(ld_acquire_sys(p) - seq) >= 0) return true;
+    if ((it & 63u) == 0) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        record_device_error(DEV_FLAG_TIMEOUT, site);
+        return false;
+      }
+      __nanosleep(256);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // bf16 helpers
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }

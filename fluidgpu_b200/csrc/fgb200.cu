@@ -8,3 +8,4 @@
 #include "attention_noalloc.cuh"
 #include "moe.cuh"
 #include "handoff.cuh"
+#include "disagg.cuh"

@@ -56,6 +56,8 @@ constexpr int kThreads = 192;
 constexpr int kMaxTickets = 16384;
 constexpr size_t kTicketBytes = kMaxTickets * sizeof(unsigned int);
 
+constexpr int kMaxRoutes = 8;  // peer destinations / flags of a routed GEMM
+
 struct Params {
   __nv_bfloat16* out;
   const __nv_bfloat16* residual;
@@ -71,7 +73,50 @@ struct Params {
   int grid;                  // G (stream-K) / tiles (cluster kernel)
   int max_contrib;
   int split;                 // S: CTAs per tile along K (cluster kernel)
+  // routed output (fg_gemm_bf16_packed_routed): row t of the result goes to
+  // dst[t / dst_rows] at row t % dst_rows (FG_ROUTE_SPLIT) or to every dst[d]
+  // at row dst_row0 + t (FG_ROUTE_BROADCAST); route 0 writes `out`
+  int route, n_dst, dst_rows, dst_row0;
+  void* dst[kMaxRoutes];
+  // completion signal: after every CTA's stores, the last CTA (ticket)
+  // release-stores epoch[0] * seq_mul + seq_add into each sig[i] (system scope)
+  int n_sig, total_ctas;
+  uint32_t* sig[kMaxRoutes];
+  const uint32_t* epoch;
+  uint32_t seq_mul, seq_add;
+  unsigned int* sig_ticket;
 };
+
+// Store value v of output row t (a token), column n, where the Params route it.
+template <typename T>
+__device__ __forceinline__ void store_out(const Params& p, int t, int n, T v) {
+  if (p.route == 0) {
+    reinterpret_cast<T*>(p.out)[(int64_t)t * p.ldo + n] = v;
+  } else if (p.route == FG_ROUTE_SPLIT) {
+    const int d = t / p.dst_rows;
+    reinterpret_cast<T*>(p.dst[d])[(int64_t)(t - d * p.dst_rows) * p.ldo + n] = v;
+  } else {
+    for (int d = 0; d < p.n_dst; ++d)
+      reinterpret_cast<T*>(p.dst[d])[(int64_t)(p.dst_row0 + t) * p.ldo + n] = v;
+  }
+}
+
+// After a CTA's last store: publish the result once every CTA of the grid
+// has stored (see Params). Executed by all threads of the CTA.
+__device__ __forceinline__ void signal_done(const Params& p) {
+  if (p.n_sig == 0) return;
+  __threadfence_system();  // this thread's (peer) stores before the ticket
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int prev = atomicAdd(p.sig_ticket, 1u);
+    if (prev == (unsigned int)(p.total_ctas - 1)) {
+      __threadfence_system();
+      const uint32_t v = *p.epoch * p.seq_mul + p.seq_add;
+      for (int i = 0; i < p.n_sig; ++i) st_release_sys(p.sig[i], v);
+      *p.sig_ticket = 0u;  // rearmed: the next grid's CTAs count after griddep_wait
+    }
+  }
+}
 
 template <int BN, int STAGES>
 struct Layout {
@@ -215,11 +260,11 @@ __device__ __forceinline__ void apply_epilogue(const Params& p, int n_tile, int 
         float y = v[i] + b;
         if (p.epilogue == FG_EPI_F32) {
           if (p.residual) y += bf2f(p.residual[(int64_t)t * p.ldo + n]);
-          reinterpret_cast<float*>(p.out)[(int64_t)t * p.ldo + n] = y;
+          store_out<float>(p, t, n, y);
           continue;
         }
         if (p.epilogue == FG_EPI_RESIDUAL) y = bf2f(p.residual[(int64_t)t * p.ldo + n]) + rbf(y);
-        p.out[(int64_t)t * p.ldo + n] = f2bf(y);
+        store_out<__nv_bfloat16>(p, t, n, f2bf(y));
       }
     }
   }
@@ -635,7 +680,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                  "r"(L::TMEM_COLS)
                  : "memory");
   }
-  if (S == 1) return;
+  if (S == 1) {
+    signal_done(p);
+    return;
+  }
 
   // ---------------- cluster reduction through distributed shared memory ----------------
   namespace cgx = cooperative_groups;
@@ -698,16 +746,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           float y = vv[i] + b;
           if (p.epilogue == FG_EPI_F32) {
             if (p.residual) y += bf2f(p.residual[(int64_t)t * p.ldo + nn]);
-            reinterpret_cast<float*>(p.out)[(int64_t)t * p.ldo + nn] = y;
+            store_out<float>(p, t, nn, y);
             continue;
           }
           if (p.epilogue == FG_EPI_RESIDUAL) y = bf2f(p.residual[(int64_t)t * p.ldo + nn]) + rbf(y);
-          p.out[(int64_t)t * p.ldo + nn] = f2bf(y);
+          store_out<__nv_bfloat16>(p, t, nn, f2bf(y));
         }
       }
     }
   }
   cluster.sync();  // peers may still read this CTA's partial tile
+  signal_done(p);
 }
 
 // ---------------------------------------------------------------------------
@@ -838,12 +887,25 @@ int launch(const Params& p, const CUtensorMap& tw, const CUtensorMap& tx, cudaSt
                    L::DYN_SMEM, st, tw, tx, p);
 }
 
+// Routing and completion signal of fg_gemm_bf16_packed_routed (none for the
+// plain entry points).
+struct Route {
+  int route = 0, n_dst = 0, dst_rows = 0, dst_row0 = 0;
+  void* const* dst = nullptr;
+  int n_sig = 0;
+  uint32_t* const* sig = nullptr;
+  const uint32_t* epoch = nullptr;
+  uint32_t seq_mul = 0, seq_add = 0;
+  uint32_t* ticket = nullptr;
+};
+
 template <bool PACKED>
 int run(const fg_bf16* x, const void* w, fg_bf16* out, const fg_bf16* residual, const fg_bf16* bias,
         int T, int N, int K, int epilogue, int splits, void* workspace, size_t workspace_bytes_,
-        cudaStream_t st) {
+        cudaStream_t st, const Route& rt = Route()) {
   const Plan pl = make_plan(T, N, K, splits);
   Params p;
+  memset(&p, 0, sizeof(p));
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.residual = reinterpret_cast<const __nv_bfloat16*>(residual);
   p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
@@ -862,6 +924,22 @@ int run(const fg_bf16* x, const void* w, fg_bf16* out, const fg_bf16* residual, 
   p.split = pl.split;
   p.partial = nullptr;
   p.tickets = nullptr;
+  p.route = rt.route;
+  p.n_dst = rt.n_dst;
+  p.dst_rows = rt.dst_rows;
+  p.dst_row0 = rt.dst_row0;
+  for (int i = 0; i < rt.n_dst; ++i) p.dst[i] = rt.dst[i];
+  p.n_sig = rt.n_sig;
+  for (int i = 0; i < rt.n_sig; ++i) p.sig[i] = rt.sig[i];
+  p.epoch = rt.epoch;
+  p.seq_mul = rt.seq_mul;
+  p.seq_add = rt.seq_add;
+  p.sig_ticket = rt.ticket;
+  p.total_ctas = pl.grid * pl.split;
+  if (rt.route != 0 || rt.n_sig != 0) {
+    FG_REQUIRE(!pl.streamk, "fg_gemm_bf16_packed_routed: T=%d N=%d K=%d plans the persistent kernel; "
+               "routed output and signals need a decode-size plan", T, N, K);
+  }
   const size_t need = workspace_bytes(pl);
   if (need) {
     const long long tiles = (long long)pl.n_tiles * pl.t_tiles;
@@ -962,6 +1040,47 @@ int fg_gemm_bf16_packed(const fg_bf16* x, const void* w_packed, fg_bf16* out,
   if (rc || T == 0) return rc;
   return fg::gemm::run<true>(x, w_packed, out, residual, bias, T, N, K, epilogue, splits,
                              workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int fg_gemm_bf16_packed_routed(const fg_bf16* x, const void* w_packed, const fg_bf16* residual,
+                               const fg_bf16* bias, int T, int N, int K, int epilogue, int route,
+                               void* const* dst, int n_dst, int dst_rows, int dst_row0,
+                               uint32_t* const* sig_flags, int n_sig, const uint32_t* epoch,
+                               uint32_t seq_mul, uint32_t seq_add, uint32_t* ticket,
+                               fg_stream_t stream) {
+  using fg::gemm::kMaxRoutes;
+  FG_REQUIRE(route == FG_ROUTE_SPLIT || route == FG_ROUTE_BROADCAST,
+             "fg_gemm_bf16_packed_routed: route must be FG_ROUTE_SPLIT or FG_ROUTE_BROADCAST");
+  FG_REQUIRE(epilogue == FG_EPI_STORE || epilogue == FG_EPI_RESIDUAL || epilogue == FG_EPI_F32,
+             "fg_gemm_bf16_packed_routed: epilogue %d cannot be routed (STORE, RESIDUAL or F32)", epilogue);
+  FG_REQUIRE(dst && n_dst >= 1 && n_dst <= kMaxRoutes, "fg_gemm_bf16_packed_routed: n_dst=%d (1..%d)",
+             n_dst, kMaxRoutes);
+  for (int i = 0; i < n_dst; ++i) FG_REQUIRE(dst[i] != nullptr, "fg_gemm_bf16_packed_routed: dst[%d] is null", i);
+  FG_REQUIRE(route != FG_ROUTE_SPLIT || (dst_rows > 0 && (long long)dst_rows * n_dst >= T),
+             "fg_gemm_bf16_packed_routed: %d destinations of %d rows cannot take %d rows", n_dst, dst_rows, T);
+  FG_REQUIRE(route != FG_ROUTE_BROADCAST || dst_row0 >= 0, "fg_gemm_bf16_packed_routed: dst_row0 < 0");
+  FG_REQUIRE(n_sig >= 0 && n_sig <= kMaxRoutes, "fg_gemm_bf16_packed_routed: n_sig=%d (0..%d)", n_sig,
+             kMaxRoutes);
+  FG_REQUIRE(n_sig == 0 || (sig_flags && epoch && ticket),
+             "fg_gemm_bf16_packed_routed: signalling needs flags, an epoch and a ticket");
+  for (int i = 0; i < n_sig; ++i)
+    FG_REQUIRE(sig_flags[i] != nullptr, "fg_gemm_bf16_packed_routed: sig_flags[%d] is null", i);
+  FG_REQUIRE(residual != nullptr || epilogue != FG_EPI_RESIDUAL,
+             "fg_gemm_bf16_packed_routed: FG_EPI_RESIDUAL needs a residual");
+  fg::gemm::Route rt;
+  rt.route = route;
+  rt.n_dst = n_dst;
+  rt.dst = dst;
+  rt.dst_rows = dst_rows;
+  rt.dst_row0 = dst_row0;
+  rt.n_sig = n_sig;
+  rt.sig = sig_flags;
+  rt.epoch = epoch;
+  rt.seq_mul = seq_mul;
+  rt.seq_add = seq_add;
+  rt.ticket = ticket;
+  return fg::gemm::run<true>(x, w_packed, nullptr, residual, bias, T, N, K, epilogue, 0, nullptr, 0,
+                             (cudaStream_t)stream, rt);
 }
 
 }  // extern "C"

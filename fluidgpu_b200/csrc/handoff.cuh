@@ -53,32 +53,6 @@ struct Geometry {
   }
 };
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// spin (bounded) until *p reaches seq (wrap-safe); false on timeout
-__device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t seq, uint64_t timeout_ns,
-                                              unsigned int site) {
-  if ((int32_t)(ld_acquire_sys(p) - seq) >= 0) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if ((int32_t)(ld_acquire_sys(p) - seq) >= 0) return true;
-    if ((it & 63u) == 0) {
-      if (globaltimer_ns() - t0 > timeout_ns) {
-        record_device_error(DEV_FLAG_TIMEOUT, site);
-        return false;
-      }
-      __nanosleep(256);
-    }
-  }
-}
-
 // grid-stride 16-byte copy, four loads in flight per thread before their
 // stores (a remote store stream needs many outstanding requests)
 __device__ __forceinline__ void copy16(uint4* __restrict__ dst, const uint4* __restrict__ src,

@@ -1,0 +1,524 @@
+"""Disaggregated decode step over the GPUs of one NVLink node, with merged
+feed-forward batches and hand-offs fused into the kernels on either side.
+
+The B200 form of FluidGPU's attention/FFN disaggregation (the placement of
+benchmark configs 2 and 4: attention on some GPUs, the FFN on others; the
+reference hands the hidden state over with NCCL send/recv at every task
+boundary, executor.py:104-123, and pipelines micro-batches with the remote
+FFN, vllm_integration.py:1141-1237).
+
+Roles (A attention ranks, S FFN ranks, M micro-batches of b sequences on
+every attention rank):
+  attention rank a : embed; per layer RMSNorm -> QKV GEMM -> RoPE + paged KV
+                     append -> paged attention -> O-proj GEMM (+ residual);
+                     final norm -> lm_head -> argmax. Each micro-batch has its
+                     own paged KV cache, stream and CUDA graph, so one
+                     micro-batch's attention runs while another's FFN is away.
+  FFN rank j       : the FFN of layer l for micro-batch m of ALL A attention
+                     ranks at once: their rows form one batch of A*b tokens
+                     (one RMSNorm, one gate/up GEMM with the SwiGLU epilogue,
+                     one down GEMM), over its slice j of the intermediate
+                     dimension (tensor-parallel, S shards). One graph per
+                     step walks (layer, micro-batch) in order.
+
+Hand-offs (per layer and micro-batch; no NCCL and no copy kernels):
+  a -> every j : the O-proj epilogue stores its b rows of h (bf16) into
+                 in[m] rows [a*b, (a+1)*b) of every FFN rank (broadcast
+                 route), and its last CTA raises in_flag[m][a] there.
+  j -> every a : the down-proj epilogue stores rows [a*b, (a+1)*b) of its
+                 result into rank a's ret[m] (split route) and raises
+                 ret_flag[m][j] there: with S == 1 the finished residual
+                 stream bf16(h + FFN(h)); with S > 1 an fp32 partial (shard 0
+                 adds h), summed in shard order by the consumer.
+  The first kernel reading a message waits for its flag itself
+  (fg_rmsnorm_wait / fg_sum_rmsnorm_wait). Flag values are epoch * L +
+  layer + 1, where each side counts its own finished steps (fg_counter_add
+  at the end of its graph), so no flag is ever reset and no acknowledgement
+  travels back: a buffer is rewritten only after its reader has answered a
+  later message, which it sends after its last read.
+
+Memory: every rank owns one mailbox (data, then flags 128 bytes apart) in its
+own HBM; the other role's ranks map it through CUDA IPC. In one process on
+one device (tests), Fabric.local wires the same buffers by plain pointers.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+
+from . import _lib, kernels
+from ._lib import call, ptr_array
+from .kv_cache import PagedKVCache
+from .model import ModelWeights
+
+FLAG_STRIDE = 128  # bytes between flags (one per cache line)
+
+
+@dataclass(frozen=True)
+class DisaggLayout:
+    """Global ranks of the two roles, micro-batches per attention rank and
+    sequences per micro-batch."""
+
+    attn_ranks: tuple[int, ...]
+    ffn_ranks: tuple[int, ...]
+    micro_batches: int
+    rows: int
+
+    def __post_init__(self) -> None:
+        assert self.attn_ranks and self.ffn_ranks, "need at least one attention and one FFN rank"
+        assert not set(self.attn_ranks) & set(self.ffn_ranks), "a rank has one role"
+        assert len(self.attn_ranks) <= 8 and len(self.ffn_ranks) <= 8, "at most 8 ranks per role"
+        assert self.micro_batches >= 1 and self.rows >= 1
+
+    @property
+    def A(self) -> int:
+        return len(self.attn_ranks)
+
+    @property
+    def S(self) -> int:
+        return len(self.ffn_ranks)
+
+    @property
+    def world(self) -> int:
+        return self.A + self.S
+
+    def role(self, rank: int) -> tuple[str, int]:
+        if rank in self.attn_ranks:
+            return "attn", self.attn_ranks.index(rank)
+        assert rank in self.ffn_ranks, f"rank {rank} has no role"
+        return "ffn", self.ffn_ranks.index(rank)
+
+    @classmethod
+    def split(cls, world: int, micro_batches: int, rows: int) -> "DisaggLayout":
+        """First half of the ranks attention, second half FFN (one of each for 2)."""
+        assert world >= 2 and world % 2 == 0, f"a split layout needs an even world, got {world}"
+        h = world // 2
+        return cls(tuple(range(h)), tuple(range(h, world)), micro_batches, rows)
+
+
+class _Mailbox:
+    """`data_bytes` of message rows, then `n_flags` u32 flags, zeroed, in this
+    GPU's memory."""
+
+    def __init__(self, data_bytes: int, n_flags: int, device: torch.device) -> None:
+        self.data_bytes = (data_bytes + 255) // 256 * 256
+        self.buf = torch.zeros(self.data_bytes + n_flags * FLAG_STRIDE, dtype=torch.uint8, device=device)
+
+    @property
+    def ptr(self) -> int:
+        return self.buf.data_ptr()
+
+
+def _flag(base: int, data_bytes: int, i: int) -> int:
+    return base + data_bytes + i * FLAG_STRIDE
+
+
+class _Rank:
+    """State shared by both roles: layout, weights, mailbox, peers' mailbox
+    base addresses (filled by a Fabric), hooks."""
+
+    def __init__(self, layout: DisaggLayout, rank: int, weights: ModelWeights, device: torch.device,
+                 timeout_ms: int) -> None:
+        self.layout = layout
+        self.rank = rank
+        self.role, self.index = layout.role(rank)
+        self.w = weights
+        self.spec = weights.spec
+        self.device = device
+        self.timeout_ms = timeout_ms
+        self.L = self.spec.num_layers
+        self.peer_base: dict[int, int] = {}  # global rank -> its mailbox base address as seen here
+        # host-side ordering hooks for ranks that share a GPU (tests); None on
+        # separate GPUs, where the flags alone order the ranks
+        self.hooks: Any = None
+
+    # mailbox geometry of each role (identical on every rank)
+    def ffn_geometry(self) -> tuple[int, int]:
+        lay, H = self.layout, self.spec.hidden
+        data = lay.micro_batches * lay.A * lay.rows * H * 2
+        return (data + 255) // 256 * 256, lay.micro_batches * lay.A
+
+    def attn_geometry(self) -> tuple[int, int]:
+        lay, H = self.layout, self.spec.hidden
+        elem = 4 if lay.S > 1 else 2
+        data = lay.micro_batches * lay.S * lay.rows * H * elem
+        return (data + 255) // 256 * 256, lay.micro_batches * lay.S
+
+    def _hook(self, what: str, *args) -> None:
+        if self.hooks is not None:
+            getattr(self.hooks, what)(self, *args)
+
+
+class AttentionRank(_Rank):
+    """One attention rank: M micro-batches of b sequences, each with its own
+    paged KV cache, buffers, stream and graph."""
+
+    def __init__(self, layout: DisaggLayout, rank: int, weights: ModelWeights, max_seq_len: int, *,
+                 device: torch.device, timeout_ms: int = 10000) -> None:
+        super().__init__(layout, rank, weights, device, timeout_ms)
+        assert self.role == "attn"
+        s, lay = self.spec, layout
+        data, nflag = self.attn_geometry()
+        self.mailbox = _Mailbox(data, nflag, device)
+        self.max_seq_len = max_seq_len
+        b, H = lay.rows, s.hidden
+        self.mbs = []
+        for m in range(lay.micro_batches):
+            kv = PagedKVCache(num_layers=s.num_layers, owned_layer_ids=list(range(s.num_layers)),
+                              max_seq_len=max_seq_len, num_kv_heads=s.n_kv, head_dim=s.head_dim,
+                              dtype=torch.bfloat16, device=device, max_batch=b)
+            self.mbs.append({
+                "kv": kv,
+                "tok": torch.zeros(b, dtype=torch.int64, device=device),
+                "next": torch.zeros(b, dtype=torch.int64, device=device),
+                "h": torch.empty(b, H, dtype=torch.bfloat16, device=device),
+                "x": torch.empty(b, H, dtype=torch.bfloat16, device=device),
+                "epoch": torch.zeros(1, dtype=torch.int32, device=device),
+                "tickets": torch.zeros(s.num_layers, dtype=torch.int32, device=device),
+                "slot": f"disagg{id(self):x}.{m}",
+                "graph": None,
+                "logits": None,
+            })
+        self.streams = [torch.cuda.Stream(device, priority=-(lay.micro_batches - 1 - m))
+                        for m in range(lay.micro_batches)]
+
+    # -- views of this rank's mailbox -------------------------------------
+    def ret_view(self, m: int) -> torch.Tensor:
+        """This rank's return buffer of micro-batch m: [S, b, H] fp32 (S > 1)
+        or [b, H] bf16 (S == 1)."""
+        lay, H = self.layout, self.spec.hidden
+        if lay.S > 1:
+            plane = lay.rows * H
+            flat = self.mailbox.buf[: self.mailbox.data_bytes].view(torch.float32)
+            return flat[m * lay.S * plane:(m + 1) * lay.S * plane].view(lay.S, lay.rows, H)
+        flat = self.mailbox.buf[: self.mailbox.data_bytes].view(torch.bfloat16)
+        return flat[m * lay.rows * H:(m + 1) * lay.rows * H].view(lay.rows, H)
+
+    def ret_flags(self, m: int) -> list[int]:
+        return [_flag(self.mailbox.ptr, self.mailbox.data_bytes, m * self.layout.S + j)
+                for j in range(self.layout.S)]
+
+    def ffn_in_rows(self, m: int) -> list[int]:
+        """Address of this rank's row block of in[m] on every FFN rank."""
+        lay, H = self.layout, self.spec.hidden
+        out = []
+        for r in lay.ffn_ranks:
+            base = self.peer_base[r]
+            out.append(base + (m * lay.A * lay.rows) * H * 2)
+        return out
+
+    def ffn_in_flags(self, m: int) -> list[int]:
+        data, _ = self.ffn_geometry()
+        return [_flag(self.peer_base[r], data, m * self.layout.A + self.index) for r in self.layout.ffn_ranks]
+
+    # -- batch --------------------------------------------------------------
+    def start(self, prompt_lens: list[list[int]], reserve_tokens: int) -> None:
+        """prompt_lens[m]: cached tokens of micro-batch m's b sequences."""
+        for mb, lens in zip(self.mbs, prompt_lens):
+            assert len(lens) == self.layout.rows
+            mb["kv"].start_batch(lens, reserve_tokens)
+            mb["graph"] = None
+
+    def set_tokens(self, m: int, tokens: torch.Tensor) -> None:
+        self.mbs[m]["tok"].copy_(tokens.reshape(-1))
+
+    # -- one decode step of micro-batch m, enqueued on the current stream ----
+    def _norm_in(self, m: int, layer: int, weight: torch.Tensor) -> None:
+        """x = RMSNorm(h) of the residual stream after the FFN of `layer - 1`
+        (waiting for the FFN ranks' message)."""
+        s, lay, mb = self.spec, self.layout, self.mbs[m]
+        self._hook("before_wait", "ret", m, layer - 1)
+        flags = ptr_array(self.ret_flags(m))
+        stream = kernels._stream(self.device)
+        if lay.S == 1:
+            ret = self.ret_view(m)
+            call("fg_rmsnorm_wait", ret.data_ptr(), weight.data_ptr(), mb["x"].data_ptr(), lay.rows, s.hidden,
+                 float(s.eps), s.norm_mode, flags, 1, lay.rows, mb["epoch"].data_ptr(), self.L, layer,
+                 self.timeout_ms, stream)
+        else:
+            call("fg_sum_rmsnorm_wait", self.ret_view(m).data_ptr(), lay.S, mb["h"].data_ptr(),
+                 weight.data_ptr(), mb["x"].data_ptr(), lay.rows, s.hidden, float(s.eps), s.norm_mode, flags,
+                 lay.S, mb["epoch"].data_ptr(), self.L, layer, self.timeout_ms, stream)
+
+    def _residual(self, m: int) -> torch.Tensor:
+        """The residual stream h of micro-batch m (in the return buffer when
+        one FFN rank sends it finished)."""
+        if self.layout.S == 1:
+            return self.ret_view(m)
+        return self.mbs[m]["h"]
+
+    def step_mb(self, m: int, standalone: bool = False) -> None:
+        """Enqueue one decode step of micro-batch m on the current stream.
+        standalone=True runs the same attention-side kernels with the FFN
+        left out (no hand-offs, the O-proj result is the next layer's input):
+        a timing reference for how much of the step the hand-offs and the
+        remote FFN add, not a model computation."""
+        s, lay, mb, W = self.spec, self.layout, self.mbs[m], self.w
+        kv = mb["kv"]
+        b = lay.rows
+        kernels.embed(mb["tok"], W.embed, out=mb["h"])
+        kernels.rmsnorm(mb["h"], W.layers[0]["ln1"], s.eps, s.norm_mode, out=mb["x"])
+        dsts = ptr_array(self.ffn_in_rows(m)) if not standalone else None
+        sigs = ptr_array(self.ffn_in_flags(m)) if not standalone else None
+        stream = kernels._stream(self.device)
+        for i in range(s.num_layers):
+            L = W.layers[i]
+            h = mb["h"] if (i == 0 or standalone) else self._residual(m)
+            if i > 0:
+                if standalone:
+                    kernels.rmsnorm(mb["h"], L["ln1"], s.eps, s.norm_mode, out=mb["x"])
+                else:
+                    self._norm_in(m, i, L["ln1"])
+            qkv = kernels.gemm(mb["x"], L["wqkv"], bias=L.get("bqkv"), slot=mb["slot"] + ".gemm")
+            kp, vp = kv.layer_pages(i)
+            q = kernels.rope_kv_append(qkv, kv.positions[:b], W.inv_freq, W.rope_scaling, kv.block_table[:b],
+                                       kp, vp, s.n_q, s.n_kv, s.head_dim)
+            a = kernels.paged_decode_attn(q, kp, vp, kv.block_table[:b], kv.seq_lens[:b], kv.plan_len(),
+                                          window=s.window(i), sinks=L.get("sinks"), slot=mb["slot"] + ".attn")
+            if standalone:
+                kernels.gemm(a, L["wo"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h, bias=L.get("bo"), out=mb["h"],
+                             slot=mb["slot"] + ".gemm")
+                continue
+            wo = L["wo"]
+            call("fg_gemm_bf16_packed_routed", a.data_ptr(), wo.data.data_ptr(), h.data_ptr(),
+                 None if L.get("bo") is None else L["bo"].data_ptr(), b, s.hidden, s.n_q * s.head_dim,
+                 _lib.FG_EPI_RESIDUAL, _lib.FG_ROUTE_BROADCAST, dsts, lay.S, b, self.index * b, sigs, lay.S,
+                 mb["epoch"].data_ptr(), self.L, i + 1, mb["tickets"][i:i + 1].data_ptr(), stream)
+            self._hook("after_send", "in", m, i)
+        if standalone:
+            kernels.rmsnorm(mb["h"], W.final_norm, s.eps, s.norm_mode, out=mb["x"])
+        else:
+            self._norm_in(m, s.num_layers, W.final_norm)
+        logits = kernels.gemm(mb["x"], W.lm_head, slot=mb["slot"] + ".gemm")
+        mb["logits"] = logits
+        kernels.argmax(logits, out=mb["next"])
+        mb["tok"].copy_(mb["next"])
+        kernels.advance(kv.positions[:b], kv.seq_lens[:b])
+        if not standalone:
+            call("fg_counter_add", mb["epoch"].data_ptr(), 1, stream)
+
+    # -- graphs -----------------------------------------------------------------
+    def reserve(self, m: int) -> None:
+        """Scratch at the size the current length bucket needs (before capture)."""
+        s, mb = self.spec, self.mbs[m]
+        kv = mb["kv"]
+        lib = _lib.lib()
+        plan = kv.plan_len()
+        need = max(lib.fg_attn_workspace_bytes(self.layout.rows, s.n_q, s.n_kv, s.head_dim, plan, s.window(i))
+                   for i in range(s.num_layers))
+        kernels.Workspace.get(need, self.device, mb["slot"] + ".attn")
+
+    def capture(self, m: int, standalone: bool = False) -> None:
+        mb = self.mbs[m]
+        kv = mb["kv"]
+        kv.prepare_step(1)
+        bucket = kv.bucket(kv.max_attended())
+        self.reserve(m)
+        snap = kv.snapshot_host()
+        kv.plan_len_override = bucket
+        g = torch.cuda.CUDAGraph()
+        s = self.streams[m]
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        try:
+            with torch.cuda.stream(s), torch.inference_mode():
+                with torch.cuda.graph(g, stream=s):
+                    self.step_mb(m, standalone)
+        finally:
+            kv.plan_len_override = None
+            kv.restore_host(snap)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        key = "alone" if standalone else "graph"
+        mb[key], mb[key + "_bucket"] = g, bucket
+
+    def step(self, graphs: bool = True, standalone: bool = False) -> list[torch.Tensor]:
+        """One decode step of every micro-batch, interleaved on their
+        streams; returns the next-token buffers."""
+        cur = torch.cuda.current_stream(self.device)
+        for s in self.streams:
+            s.wait_stream(cur)
+        key = "alone" if standalone else "graph"
+        for m, (mb, s) in enumerate(zip(self.mbs, self.streams)):
+            kv = mb["kv"]
+            with torch.cuda.stream(s):
+                kv.prepare_step(1)
+                if graphs:
+                    if mb.get(key) is None or kv.bucket(kv.max_attended()) != mb[key + "_bucket"]:
+                        self.capture(m, standalone)
+                    mb[key].replay()
+                else:
+                    with torch.inference_mode():
+                        self.step_mb(m, standalone)
+                kv.host_advance(1)
+        for s in self.streams:
+            cur.wait_stream(s)
+        return [mb["next"] for mb in self.mbs]
+
+    def step_serial_standalone(self) -> None:
+        """Every micro-batch's attention-side step with the FFN left out, one
+        after another on the current stream (kernels timed one at a time)."""
+        with torch.inference_mode():
+            for m, mb in enumerate(self.mbs):
+                mb["kv"].prepare_step(1)
+                self.step_mb(m, standalone=True)
+                mb["kv"].host_advance(1)
+
+    def release_graphs(self) -> None:
+        for mb in self.mbs:
+            mb["graph"] = None
+            mb["alone"] = None
+
+
+class FFNRank(_Rank):
+    """One FFN rank: shard `index` of every layer's dense FFN, applied to the
+    merged rows of all attention ranks, micro-batch by micro-batch."""
+
+    def __init__(self, layout: DisaggLayout, rank: int, weights: ModelWeights, *, device: torch.device,
+                 timeout_ms: int = 10000) -> None:
+        super().__init__(layout, rank, weights, device, timeout_ms)
+        assert self.role == "ffn"
+        assert not self.spec.moe, "the merged-FFN rank serves dense FFNs"
+        if layout.S > 1:
+            assert weights.ffn_shard == (self.index, layout.S), (
+                f"FFN rank {self.index} needs the weights of shard ({self.index}, {layout.S})")
+        data, nflag = self.ffn_geometry()
+        self.mailbox = _Mailbox(data, nflag, device)
+        T = layout.A * layout.rows
+        self.x = torch.empty(T, self.spec.hidden, dtype=torch.bfloat16, device=device)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self.tickets = torch.zeros(self.spec.num_layers * layout.micro_batches, dtype=torch.int32, device=device)
+        self.slot = f"disagg-ffn{id(self):x}"
+        self.stream = torch.cuda.Stream(device)
+        self.graph = None
+
+    def in_view(self, m: int) -> torch.Tensor:
+        lay, H = self.layout, self.spec.hidden
+        T = lay.A * lay.rows
+        flat = self.mailbox.buf[: self.mailbox.data_bytes].view(torch.bfloat16)
+        return flat[m * T * H:(m + 1) * T * H].view(T, H)
+
+    def in_flags(self, m: int) -> list[int]:
+        return [_flag(self.mailbox.ptr, self.mailbox.data_bytes, m * self.layout.A + a)
+                for a in range(self.layout.A)]
+
+    def ret_rows(self, m: int) -> list[int]:
+        """Address of this shard's plane of ret[m] on every attention rank."""
+        lay, H = self.layout, self.spec.hidden
+        out = []
+        for r in lay.attn_ranks:
+            base = self.peer_base[r]
+            if lay.S > 1:
+                out.append(base + ((m * lay.S + self.index) * lay.rows * H) * 4)
+            else:
+                out.append(base + (m * lay.rows * H) * 2)
+        return out
+
+    def ret_flags(self, m: int) -> list[int]:
+        data, _ = self.attn_geometry()
+        return [_flag(self.peer_base[r], data, m * self.layout.S + self.index) for r in self.layout.attn_ranks]
+
+    def step(self, graphs: bool = True) -> None:
+        if graphs:
+            if self.graph is None:
+                self.capture()
+            self.graph.replay()
+        else:
+            with torch.inference_mode():
+                self._step()
+
+    def _step(self) -> None:
+        s, lay, W = self.spec, self.layout, self.w
+        T = lay.A * lay.rows
+        stream = kernels._stream(self.device)
+        epi = _lib.FG_EPI_RESIDUAL if lay.S == 1 else _lib.FG_EPI_F32
+        for i in range(s.num_layers):
+            L = W.layers[i]
+            for m in range(lay.micro_batches):
+                self._hook("before_wait", "in", m, i)
+                inp = self.in_view(m)
+                call("fg_rmsnorm_wait", inp.data_ptr(), L["ln2"].data_ptr(), self.x.data_ptr(), T, s.hidden,
+                     float(s.eps), s.norm_mode, ptr_array(self.in_flags(m)), lay.A, lay.rows,
+                     self.epoch.data_ptr(), self.L, i + 1, self.timeout_ms, stream)
+                ev = kernels.KernelTimer.start("ffn")
+                act = kernels.gemm(self.x, L["w_gate_up"], epilogue=_lib.FG_EPI_SWIGLU, slot=self.slot)
+                wd = L["w_down"]
+                res = inp if (lay.S == 1 or self.index == 0) else None
+                t = i * lay.micro_batches + m
+                call("fg_gemm_bf16_packed_routed", act.data_ptr(), wd.data.data_ptr(),
+                     None if res is None else res.data_ptr(), None, T, s.hidden, wd.K, epi, _lib.FG_ROUTE_SPLIT,
+                     ptr_array(self.ret_rows(m)), lay.A, lay.rows, 0, ptr_array(self.ret_flags(m)), lay.A,
+                     self.epoch.data_ptr(), self.L, i + 1, self.tickets[t:t + 1].data_ptr(), stream)
+                kernels.KernelTimer.stop("ffn", ev, T=T, H=s.hidden, I=wd.K)
+                self._hook("after_send", "ret", m, i)
+        call("fg_counter_add", self.epoch.data_ptr(), 1, stream)
+
+    def capture(self) -> None:
+        g = torch.cuda.CUDAGraph()
+        s = self.stream
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s), torch.inference_mode():
+            with torch.cuda.graph(g, stream=s):
+                self._step()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self.graph = g
+
+    def release_graphs(self) -> None:
+        self.graph = None
+
+
+class Fabric:
+    """Makes every rank's mailbox reachable from the ranks of the other role."""
+
+    @staticmethod
+    def local(ranks: list[_Rank]) -> None:
+        """Ranks of one process on one device: plain device pointers."""
+        bases = {r.rank: r.mailbox.ptr for r in ranks}
+        for r in ranks:
+            r.peer_base = dict(bases)
+
+    @staticmethod
+    def ipc(rank: _Rank, group=None) -> "Fabric._Imports":
+        """Ranks in separate processes: export this rank's mailbox through
+        CUDA IPC, gather every rank's handle (torch.distributed), import the
+        mailboxes of the other role. Returns the imports (close() them)."""
+        import torch.distributed as dist
+
+        torch.cuda.synchronize(rank.device)
+        handle = ctypes.create_string_buffer(64)
+        off = ctypes.c_size_t(0)
+        call("fg_ipc_export", rank.mailbox.ptr, handle, ctypes.byref(off))
+        world = dist.get_world_size(group)
+        allh: list = [None] * world
+        dist.all_gather_object(allh, (rank.rank, rank.role, bytes(handle.raw), off.value), group=group)
+        imports = Fabric._Imports()
+        rank.peer_base = {rank.rank: rank.mailbox.ptr}
+        for r, role, h, o in allh:
+            if r == rank.rank or role == rank.role:
+                continue
+            p = ctypes.c_void_p()
+            call("fg_ipc_import", h, o, ctypes.byref(p))
+            rank.peer_base[r] = p.value
+            imports.items.append((p.value, o))
+        dist.barrier(group=group)
+        return imports
+
+    class _Imports:
+        def __init__(self) -> None:
+            self.items: list[tuple[int, int]] = []
+
+        def close(self) -> None:
+            for ptr, off in self.items:
+                call("fg_ipc_close", ptr, off)
+            self.items.clear()
+
+
+def nvlink_bytes_per_step(layout: DisaggLayout, hidden: int, layers: int) -> int:
+    """Bytes every step moves between GPUs: per layer and micro-batch, each
+    attention rank's h rows to every FFN rank (bf16) and every FFN rank's
+    result rows back (bf16 with one FFN rank, fp32 partials otherwise)."""
+    lay = layout
+    out = lay.A * lay.S * lay.rows * hidden * 2
+    back = lay.A * lay.S * lay.rows * hidden * (4 if lay.S > 1 else 2)
+    return (out + back) * lay.micro_batches * layers

@@ -46,6 +46,10 @@ typedef struct CUstream_st* fg_stream_t; /* == cudaStream_t */
 #define FG_EPI_F32 4       /* out[t,n] = acc (+ bias) (+ residual[t,n] if given), fp32 out: a
                             * tensor-parallel partial sum, added up by fg_sum_partials */
 
+/* routes of fg_gemm_bf16_packed_routed */
+#define FG_ROUTE_SPLIT 1     /* row t -> dst[t / dst_rows], row t % dst_rows */
+#define FG_ROUTE_BROADCAST 2 /* row t -> every dst[d], row dst_row0 + t */
+
 /* RMSNorm weight application (fg_rmsnorm) */
 #define FG_NORM_LLAMA 0    /* w * bf16(x * rstd)    (LlamaRMSNorm)  */
 #define FG_NORM_FP32MUL 1  /* bf16(w * (x * rstd))  (GptOssRMSNorm) */
@@ -106,6 +110,31 @@ int fg_gemm_bf16_packed(const fg_bf16* x, const void* w_packed, fg_bf16* out,
                         const fg_bf16* residual, const fg_bf16* bias, int T, int N, int K,
                         int epilogue, int splits, void* workspace, size_t workspace_bytes,
                         fg_stream_t stream);
+/* fg_gemm_bf16_packed whose result goes straight to other ranks' buffers
+ * and announces itself there: the hand-off of the disaggregated step made by
+ * the producing kernel, in place of the reference's NCCL send at the task
+ * boundary (fluidgpu_torch/executor.py:104-123, comm.py:24-46).
+ *   route FG_ROUTE_SPLIT     : result row t (a token) -> dst[t / dst_rows] at
+ *                              row t % dst_rows (rows of several ranks' batches
+ *                              back to their ranks)
+ *   route FG_ROUTE_BROADCAST : row t -> every dst[d] at row dst_row0 + t (one
+ *                              rank's rows to each shard of a sharded group)
+ * dst holds n_dst <= 8 row-major buffers of row stride N (fp32 for
+ * FG_EPI_F32, else bf16), usually peer memory mapped through CUDA IPC. When
+ * every CTA has stored, the last one (counted on `ticket`, a zeroed u32 of
+ * this GPU that the call leaves zero again; one per call site) release-stores
+ * epoch[0] * seq_mul + seq_add into each of the n_sig <= 8 u32 flags
+ * (system scope), which fg_rmsnorm_wait / fg_sum_rmsnorm_wait on the
+ * receiving GPU wait for. Epilogues STORE, RESIDUAL (residual local, [T,N])
+ * and F32; decode-size T only (the cluster kernel's plans). The pointer
+ * arrays are read at the call (copied into the launch). No counterpart in
+ * the reference. */
+int fg_gemm_bf16_packed_routed(const fg_bf16* x, const void* w_packed, const fg_bf16* residual,
+                               const fg_bf16* bias, int T, int N, int K, int epilogue, int route,
+                               void* const* dst, int n_dst, int dst_rows, int dst_row0,
+                               uint32_t* const* sig_flags, int n_sig, const uint32_t* epoch,
+                               uint32_t seq_mul, uint32_t seq_add, uint32_t* ticket,
+                               fg_stream_t stream);
 /* Pack a row-major weight w:[N,K] into [ceil(N/128)][ceil(K/64)] tiles of
  * 128 x 64 bf16 (16 KB), each stored as the 128-byte-swizzled K-major image
  * the tensor cores read (16-byte chunk c of row r at chunk c ^ (r % 8));
@@ -327,6 +356,32 @@ int fg_handoff_signal(void* my_mailbox, void* peer_mailbox, int world, int me, i
                       fg_stream_t stream);
 int fg_handoff_wait(void* my_mailbox, int world, int me, int src, size_t slot_bytes, int timeout_ms,
                     fg_stream_t stream);
+
+/* ---- consumers of routed hand-offs (fg_gemm_bf16_packed_routed) -------
+ * The first kernel that reads rows another GPU stored waits for their flags
+ * itself (no separate wait kernel). A flag carries a value: the consumer
+ * waits until it reaches epoch[0] * seq_mul + seq_add (wrap-safe), computed
+ * from its own per-step epoch counter exactly as the producer computed the
+ * value it stored, so every CTA waits for the same message whenever it
+ * starts. Waits give up after timeout_ms (device status 2, site 0x5xx).
+ * flags: n_flags <= 8 u32 pointers in this GPU's memory (read at the call).
+ * No counterpart in the reference (its receive is an NCCL recv into a
+ * buffer, executor.py:104-123). */
+/* fg_rmsnorm after row r's flag (flags[r / rows_per_flag]) has arrived. */
+int fg_rmsnorm_wait(const fg_bf16* x, const fg_bf16* weight, fg_bf16* out, int T, int H, float eps,
+                    int weight_mode, uint32_t* const* flags, int n_flags, int rows_per_flag,
+                    const uint32_t* epoch, uint32_t seq_mul, uint32_t seq_add, int timeout_ms,
+                    fg_stream_t stream);
+/* After all n_flags flags: h_out[r] = bf16(partials[0][r] + ... +
+ * partials[S-1][r]) (fp32 sums in shard order, as fg_sum_partials; partials
+ * [S][T][H] fp32) and x_out[r] = fg_rmsnorm(h_out[r]): the reduce-by-consumer
+ * of a tensor-parallel FFN fused with the next layer's input norm. */
+int fg_sum_rmsnorm_wait(const float* partials, int S, fg_bf16* h_out, const fg_bf16* weight, fg_bf16* x_out,
+                        int T, int H, float eps, int weight_mode, uint32_t* const* flags, int n_flags,
+                        const uint32_t* epoch, uint32_t seq_mul, uint32_t seq_add, int timeout_ms,
+                        fg_stream_t stream);
+/* *counter += delta on the device (the per-step epoch of the hand-offs). */
+int fg_counter_add(uint32_t* counter, uint32_t delta, fg_stream_t stream);
 
 /* positions[b] += 1 and seq_lens[b] += 1 after a decode step
  * (LayerKVCache.advance, kv_cache.py:140-144). Either pointer may be NULL. */

@@ -1,0 +1,234 @@
+"""Disaggregated decode with fused hand-offs (fluidgpu_b200.disagg): attention
+ranks and merged-batch FFN ranks exchanging hidden states by stores from the
+producing GEMM's epilogue and flags the next RMSNorm waits for.
+
+One GPU: every rank is a thread on cuda:0 (each attention micro-batch its own
+thread and stream). The host orders them: a consumer kernel is enqueued only
+behind a CUDA event recorded after its producer kernel, so every flag a
+kernel waits for is already set when it starts (two launches on one GPU are
+not guaranteed to run at the same time). The kernels, buffers, routes,
+flag values and epochs are those of the multi-GPU runs.
+  - 1 attention rank + 1 FFN rank, 2 micro-batches: logits equal a
+    co-located engine per micro-batch bit for bit (same kernels, same
+    reduction orders).
+  - 2 attention ranks + 2 FFN ranks (tensor-parallel FFN, fp32 partials
+    summed by the consumer), 2 micro-batches: logits within the bf16
+    tolerance of the co-located engines, teacher-forced on their tokens.
+Two GPUs (skipped on one): ranks as processes, every rank replaying its CUDA
+graphs concurrently, greedy tokens equal the co-located engines'."""
+import os
+import queue
+import socket
+import threading
+import traceback
+from collections import defaultdict
+from datetime import timedelta
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 2e-2, 1e-2
+
+
+def _model():
+    from transformers.models.llama import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(0)
+    cfg = LlamaConfig(num_hidden_layers=3, vocab_size=2048, hidden_size=512, intermediate_size=1024,
+                      num_attention_heads=8, num_key_value_heads=2, max_position_embeddings=256)
+    return LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+
+
+class _Board:
+    """Host-side ordering of ranks that share one GPU (see module doc)."""
+
+    def __init__(self, layout):
+        self.layout = layout
+        self.q = defaultdict(queue.Queue)
+
+    def _peers(self, kind, rank):
+        lay = self.layout
+        return lay.attn_ranks if kind == "in" else lay.ffn_ranks
+
+    def after_send(self, r, kind, m, layer):
+        lay = self.layout
+        dsts = lay.ffn_ranks if kind == "in" else lay.attn_ranks
+        for d in dsts:
+            ev = torch.cuda.Event()
+            ev.record()
+            self.q[(kind, m, layer, r.rank, d)].put(ev)
+
+    def before_wait(self, r, kind, m, layer):
+        for src in self._peers(kind, r):
+            ev = self.q[(kind, m, layer, src, r.rank)].get(timeout=60)
+            torch.cuda.current_stream().wait_event(ev)
+
+
+def _run_parallel(fns):
+    errors = []
+
+    def run(fn):
+        try:
+            torch.cuda.set_device(0)
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                fn()
+            s.synchronize()
+        except BaseException:  # noqa: BLE001
+            errors.append(traceback.format_exc())
+
+    ts = [threading.Thread(target=run, args=(f,)) for f in fns]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join(timeout=300)
+    assert not any(t.is_alive() for t in ts), "a rank thread did not finish"
+    assert not errors, "\n".join(errors)
+
+
+def _colocated(model, prompts):
+    from fluidgpu_b200.config import EngineConfig
+    from fluidgpu_b200.engine import DecodeEngine
+    from fluidgpu_b200.model import ModelWeights
+
+    B = prompts.shape[0]
+    eng = DecodeEngine(ModelWeights.from_hf(model, "cuda:0"),
+                       EngineConfig(model_name="colo", max_seq_len=64, world_size=1, device="cuda:0", max_batch=B))
+    eng.start(B, reserve_tokens=60)
+    return eng
+
+
+@pytest.mark.parametrize("A,S", [(1, 1), (2, 2)])
+def test_fused_disagg_one_gpu(A, S):
+    from fluidgpu_b200 import build, kernels
+    from fluidgpu_b200.disagg import AttentionRank, DisaggLayout, Fabric, FFNRank
+    from fluidgpu_b200.model import ModelWeights
+
+    build.build()
+    model = _model()
+    M, b, steps = 2, 3, 12
+    lay = DisaggLayout(tuple(range(A)), tuple(range(A, A + S)), M, b)
+    dev = torch.device("cuda", 0)
+    attn = [AttentionRank(lay, a, ModelWeights.from_hf(model, dev), 64, device=dev, timeout_ms=5000)
+            for a in range(A)]
+    ffn = [FFNRank(lay, A + j, ModelWeights.from_hf(model, dev, ffn_shard=(j, S) if S > 1 else None),
+                   device=dev, timeout_ms=5000) for j in range(S)]
+    Fabric.local(attn + ffn)
+    board = _Board(lay)
+    for r in attn + ffn:
+        r.hooks = board
+    g = torch.Generator().manual_seed(4)
+    toks = {(a, m): torch.randint(0, 2048, (b,), generator=g) for a in range(A) for m in range(M)}
+    refs = {k: _colocated(model, v[:, None]) for k, v in toks.items()}
+    for r in attn:
+        r.start([[0] * b for _ in range(M)], reserve_tokens=60)
+    kernels.device_status(reset=True)
+    for step in range(steps):
+        for (a, m), t in toks.items():
+            attn[a].set_tokens(m, t.cuda())
+        torch.cuda.synchronize()  # the rank threads run on streams of their own
+
+        def attn_mb(a, m):
+            def go():
+                kv = attn[a].mbs[m]["kv"]
+                kv.prepare_step(1)
+                with torch.inference_mode():
+                    attn[a].step_mb(m)
+                kv.host_advance(1)
+            return go
+
+        fns = [attn_mb(a, m) for a in range(A) for m in range(M)] + [lambda j=j: ffn[j].step(graphs=False)
+                                                                        for j in range(S)]
+        _run_parallel(fns)
+        torch.cuda.synchronize()
+        for (a, m), t in toks.items():
+            want = refs[(a, m)].runner.decode_step(t.cuda()).reshape(b, -1).float().cpu()
+            got = attn[a].mbs[m]["logits"].float().cpu()
+            if S == 1:
+                assert torch.equal(got, want), f"step {step} rank {a} micro-batch {m}: logits differ"
+            else:
+                err = (got - want).abs()
+                assert (err <= ATOL + RTOL * want.abs()).all(), f"step {step} rank {a} mb {m}: {err.max()}"
+            toks[(a, m)] = want.argmax(-1)  # teacher forcing on the co-located choice
+    kernels.check_device("fused disaggregated decode")
+
+
+# ---------------------------------------------------------------------------
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, port, q):
+    try:
+        import torch.distributed as dist
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("gloo", rank=rank, world_size=2, timeout=timedelta(seconds=60))
+        from fluidgpu_b200 import build, kernels
+        from fluidgpu_b200.disagg import AttentionRank, DisaggLayout, Fabric, FFNRank
+        from fluidgpu_b200.model import ModelWeights
+
+        build.build()
+        model = _model()
+        M, b, steps = 2, 4, 10
+        lay = DisaggLayout((0,), (1,), M, b)
+        w = ModelWeights.from_hf(model, dev)
+        r = AttentionRank(lay, 0, w, 64, device=dev) if rank == 0 else FFNRank(lay, 1, w, device=dev)
+        imports = Fabric.ipc(r)
+        g = torch.Generator().manual_seed(5)
+        first = [torch.randint(0, 2048, (b,), generator=g) for _ in range(M)]
+        out = []
+        if rank == 0:
+            r.start([[0] * b for _ in range(M)], reserve_tokens=60)
+            for m in range(M):
+                r.set_tokens(m, first[m].to(dev))
+        dist.barrier()
+        for _ in range(steps):  # graphs on both ranks, replayed concurrently
+            if rank == 0:
+                out.append([t.cpu().clone() for t in r.step(graphs=True)])
+            else:
+                r.step(graphs=True)
+        torch.cuda.synchronize()
+        kernels.check_device(f"rank {rank}")
+        dist.barrier()
+        r.release_graphs()
+        imports.close()
+        dist.destroy_process_group()
+        q.put((rank, True, (first, out) if rank == 0 else None, ""))
+    except BaseException:  # noqa: BLE001
+        q.put((rank, False, None, traceback.format_exc()))
+
+
+def test_fused_disagg_two_gpus_graphs():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = sorted((q.get(timeout=300) for _ in procs), key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, _, msg in results:
+        assert ok, f"rank {rank} failed:\n{msg}"
+    first, out = results[0][2]
+    from fluidgpu_b200 import build
+
+    build.build()
+    model = _model()
+    for m, t in enumerate(first):
+        eng = _colocated(model, t[:, None])
+        tok = t.cuda()
+        for s, step in enumerate(out):
+            tok = eng.runner.decode_step(tok).reshape(len(t), -1).float().argmax(-1)
+            assert torch.equal(tok.cpu(), step[m]), f"micro-batch {m} step {s}: tokens differ"
