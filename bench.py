@@ -523,7 +523,15 @@ def run_disagg_fused(args) -> None:
             r.set_tokens(m, torch.randint(0, spec.vocab, (b,), generator=g, device=dev))
     else:
         r = FFNRank(lay, rank, weights, device=dev)
+    t_start = time.perf_counter()
+
+    def trace(what):
+        if args.verbose:
+            print(f"[rank {rank} {role} {time.perf_counter() - t_start:8.2f}s] {what}", file=sys.stderr, flush=True)
+
+    trace("weights and caches ready")
     imports = Fabric.ipc(r)
+    trace("mailboxes mapped")
 
     def step(graphs=True):
         r.step(graphs=graphs)
@@ -531,9 +539,13 @@ def run_disagg_fused(args) -> None:
     n0 = kernels.launch_count()
     step(graphs=False)  # one eager step: the launches a step issues
     launches = kernels.launch_count() - n0
+    torch.cuda.synchronize()
+    trace("eager step done")
+    kernels.check_device("disagg eager step")
     for _ in range(max(W - 1, 1)):
         step()
     torch.cuda.synchronize()
+    trace("warm-up done")
     kernels.check_device("disagg warm-up")
 
     sampler = ClockSampler(local)
@@ -550,6 +562,7 @@ def run_disagg_fused(args) -> None:
     dist.barrier()
     clocks = sampler.stop()
     ms = e0.elapsed_time(e1)
+    trace(f"timed region done: {ms / K:.3f} ms/step")
     kernels.check_device("disagg timed region")
 
     # ---- end to end: host tokens in, host tokens out, every step ----
@@ -826,6 +839,7 @@ def main() -> None:
                          "2 GPUs; tp: dense FFN tensor-parallel; ep: gpt-oss experts split)")
     ap.add_argument("--micro-batches", type=int, default=2,
                     help="ping-pong micro-batches per attention GPU (disagg, pipeline, tp, ep)")
+    ap.add_argument("--verbose", action="store_true", help="phase trace on stderr (disagg)")
     ap.add_argument("--prompt-mix", default="fixed", choices=["fixed", "uniform"],
                     help="prompt lengths: all --context (default), or seeded uniform in [128, --context] "
                          "per sequence (config 4's request mix)")

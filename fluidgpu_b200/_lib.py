@@ -54,6 +54,7 @@ SIGNATURES: dict[str, tuple] = {
     "fg_pack_weight_bf16": (c_int, [_P, _P, c_int, c_int, _P]),
     "fg_packed_weight_bytes": (c_size_t, [c_int, c_int]),
     "fg_gemm_grid": (c_int, [c_int, c_int, c_int, c_int]),
+    "fg_gemm_split": (c_int, [c_int, c_int, c_int, c_int]),
     "fg_gemm_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "fg_rope_kv_append": (
         c_int,

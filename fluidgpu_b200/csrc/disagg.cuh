@@ -14,6 +14,11 @@
 //
 // The data another GPU wrote is read through L2 (ld.global.cg): it is
 // coherent there, and an SM's L1 may still hold the previous message's lines.
+//
+// Programmatic dependent launch: these kernels let their dependents launch
+// only after the wait (griddepcontrol.launch_dependents follows it). A
+// dependent launched earlier would sit in its own bounded pipeline waits
+// for as long as the other GPU takes.
 #pragma once
 #include "common.cuh"
 #include "elementwise.cuh"
@@ -51,9 +56,9 @@ __global__ void __launch_bounds__(THREADS) rmsnorm_wait_kernel(const uint4* __re
                                                                uint4* __restrict__ out, int H, float eps,
                                                                int mode, const WaitSpec ws) {
   griddep_wait();
-  griddep_launch_dependents();
   __shared__ float red[THREADS / 32];
   wait_row(ws, blockIdx.x, 0x501);
+  griddep_launch_dependents();
   const int H8 = H >> 3;
   const uint4* xr = x + (int64_t)blockIdx.x * H8;
   uint4* orow = out + (int64_t)blockIdx.x * H8;
@@ -104,9 +109,9 @@ __global__ void __launch_bounds__(THREADS) sum_rmsnorm_wait_kernel(const float4*
                                                                    uint4* __restrict__ x_out, int H, float eps,
                                                                    int mode, const WaitSpec ws) {
   griddep_wait();
-  griddep_launch_dependents();
   __shared__ float red[THREADS / 32];
   wait_row(ws, blockIdx.x, 0x503);
+  griddep_launch_dependents();
   const int H8 = H >> 3;
   const long long row4 = (long long)blockIdx.x * (H >> 2);
   constexpr int kMaxVec = 4;

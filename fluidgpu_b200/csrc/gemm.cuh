@@ -981,6 +981,12 @@ int fg_gemm_grid(int T, int N, int K, int splits) {
   return fg::gemm::make_plan(T, N, K, splits).grid;
 }
 
+int fg_gemm_split(int T, int N, int K, int splits) {
+  if (T <= 0 || N <= 0 || K <= 0) return 0;
+  const fg::gemm::Plan pl = fg::gemm::make_plan(T, N, K, splits);
+  return pl.streamk ? 1 : pl.split;
+}
+
 size_t fg_gemm_workspace_bytes(int T, int N, int K, int splits) {
   if (T <= 0 || N <= 0 || K <= 0) return 0;
   return fg::gemm::workspace_bytes(fg::gemm::make_plan(T, N, K, splits));

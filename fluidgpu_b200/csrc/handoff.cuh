@@ -82,9 +82,11 @@ struct PutArgs {
   uint64_t timeout_ns;
 };
 
+// Kernels that wait on another GPU let their dependents launch (PDL) only
+// after the wait: a dependent launched earlier would sit in its own bounded
+// pipeline waits for as long as the other GPU takes.
 __global__ void __launch_bounds__(256) put_kernel(const PutArgs a) {
   griddep_wait();
-  griddep_launch_dependents();
   __shared__ uint32_t s_seq;
   __shared__ int s_last;
   if (threadIdx.x == 0) {
@@ -95,6 +97,7 @@ __global__ void __launch_bounds__(256) put_kernel(const PutArgs a) {
     s_seq = seq;
   }
   __syncthreads();
+  griddep_launch_dependents();
   const uint32_t seq = s_seq;
   const int slot = (int)(seq % (uint32_t)a.nslot);
   copy16(a.peer_slot0 + (size_t)slot * (a.slot_bytes / 16), a.src, a.n16);
@@ -125,7 +128,6 @@ struct RecvArgs {
 
 __global__ void __launch_bounds__(256) recv_kernel(const RecvArgs a) {
   griddep_wait();
-  griddep_launch_dependents();
   __shared__ uint32_t s_seq;
   __shared__ int s_last;
   if (threadIdx.x == 0) {
@@ -134,6 +136,7 @@ __global__ void __launch_bounds__(256) recv_kernel(const RecvArgs a) {
     s_seq = seq;
   }
   __syncthreads();
+  griddep_launch_dependents();
   const uint32_t seq = s_seq;
   const int slot = (int)(seq % (uint32_t)a.nslot);
   copy16(a.out, a.my_slot0 + (size_t)slot * (a.slot_bytes / 16), a.n16);
@@ -169,13 +172,14 @@ __global__ void signal_kernel(uint32_t* peer_flag, uint32_t* my_send_seq) {
 
 __global__ void wait_kernel(const uint32_t* my_flag, uint32_t* my_recv_seq, uint64_t timeout_ns) {
   griddep_wait();
-  griddep_launch_dependents();
   if (threadIdx.x == 0) {
     const uint32_t seq = *((volatile uint32_t*)my_recv_seq) + 1u;
     wait_at_least(my_flag, seq, timeout_ns, 0x403);
     *((volatile uint32_t*)my_recv_seq) = seq;
     __threadfence();
   }
+  __syncwarp();
+  griddep_launch_dependents();
 }
 
 // One CTA per 32 KiB, at most 128: small messages stay on a few SMs (only

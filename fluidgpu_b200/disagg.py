@@ -312,6 +312,10 @@ class AttentionRank(_Rank):
         kernels.Workspace.get(need, self.device, mb["slot"] + ".attn")
 
     def capture(self, m: int, standalone: bool = False) -> None:
+        """Capture micro-batch m's step for its current length bucket. Capture
+        synchronises this GPU: call it only while no replay of this rank
+        waits on the FFN GPUs for a micro-batch not yet launched (step()
+        captures all micro-batches before replaying any)."""
         mb = self.mbs[m]
         kv = mb["kv"]
         kv.prepare_step(1)
@@ -340,13 +344,21 @@ class AttentionRank(_Rank):
         for s in self.streams:
             s.wait_stream(cur)
         key = "alone" if standalone else "graph"
+        if graphs:
+            # capture every micro-batch's graph before replaying any: a capture
+            # synchronises the device, and a replayed micro-batch can only
+            # finish after the FFN GPUs have processed the others' messages
+            for m, (mb, s) in enumerate(zip(self.mbs, self.streams)):
+                kv = mb["kv"]
+                with torch.cuda.stream(s):
+                    kv.prepare_step(1)
+                    if mb.get(key) is None or kv.bucket(kv.max_attended()) != mb[key + "_bucket"]:
+                        self.capture(m, standalone)
         for m, (mb, s) in enumerate(zip(self.mbs, self.streams)):
             kv = mb["kv"]
             with torch.cuda.stream(s):
                 kv.prepare_step(1)
                 if graphs:
-                    if mb.get(key) is None or kv.bucket(kv.max_attended()) != mb[key + "_bucket"]:
-                        self.capture(m, standalone)
                     mb[key].replay()
                 else:
                     with torch.inference_mode():

@@ -129,7 +129,7 @@ def bench_gemm(T: int, N: int, K: int, epilogue: str = "store", iters: int = 20,
     peak, src = _peak_hbm()
     gbs = nbytes / (ms * 1e-3) / 1e9
     kernels.check_device("gemm microbench")
-    used = _lib.lib().fg_gemm_grid(T, N, K, splits)
+    used = _lib.lib().fg_gemm_grid(T, N, K, splits) * _lib.lib().fg_gemm_split(T, N, K, splits)
     return {"kernel": "fg_gemm_bf16", "T": T, "N": N, "K": K, "epilogue": epilogue, "grid": used, "packed": packed,
             "ms": ms, "bytes": nbytes, "GBps": gbs, "TFLOPs": flops / (ms * 1e-3) / 1e12,
             "frac_hbm": gbs / peak, "peak": f"{src} {peak} GB/s", "timing": "graph" if GRAPH else "eager"}

@@ -141,8 +141,13 @@ int fg_gemm_bf16_packed_routed(const fg_bf16* x, const void* w_packed, const fg_
  * padding is zero. `packed` holds fg_packed_weight_bytes(N, K) bytes. */
 int fg_pack_weight_bf16(const fg_bf16* w, void* packed, int N, int K, fg_stream_t stream);
 size_t fg_packed_weight_bytes(int N, int K);
-/* CTAs fg_gemm_bf16 launches for (T, N, K, splits). */
+/* Launch shape fg_gemm_bf16 plans for (T, N, K, splits): fg_gemm_grid is the
+ * number of CTAs of a persistent (many-token) plan, or of output tiles of a
+ * decode plan, each tile then run by fg_gemm_split CTAs along K (a thread-
+ * block cluster reducing through distributed shared memory); a persistent
+ * plan's split is 1. */
 int fg_gemm_grid(int T, int N, int K, int splits);
+int fg_gemm_split(int T, int N, int K, int splits);
 /* Workspace bytes fg_gemm_bf16 needs for (T, N, K, splits). 0 if none. */
 size_t fg_gemm_workspace_bytes(int T, int N, int K, int splits);
 

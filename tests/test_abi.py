@@ -81,6 +81,7 @@ def test_gemm_plan_decode_sizes(lib_path, T, N, K):
     lib = _lib.lib()
     tiles = (N + 127) // 128
     assert lib.fg_gemm_grid(T, N, K, 0) == tiles
+    assert 1 <= lib.fg_gemm_split(T, N, K, 0) <= 8
     assert lib.fg_gemm_workspace_bytes(T, N, K, 0) == 0
 
 

@@ -31,12 +31,19 @@ pytestmark = pytest.mark.gpu
 ATOL, RTOL = 2e-2, 1e-2
 
 
-def _model():
+def _model(wide=False):
+    """A small Llama; `wide` makes the O-proj and down GEMMs long enough in K
+    that their plans split each tile over a cluster of CTAs (the plans of the
+    full-size model), so the routed stores and the signal run on that path."""
     from transformers.models.llama import LlamaConfig, LlamaForCausalLM
 
     torch.manual_seed(0)
-    cfg = LlamaConfig(num_hidden_layers=3, vocab_size=2048, hidden_size=512, intermediate_size=1024,
-                      num_attention_heads=8, num_key_value_heads=2, max_position_embeddings=256)
+    if wide:
+        cfg = LlamaConfig(num_hidden_layers=2, vocab_size=2048, hidden_size=2048, intermediate_size=4096,
+                          num_attention_heads=16, num_key_value_heads=4, max_position_embeddings=256)
+    else:
+        cfg = LlamaConfig(num_hidden_layers=3, vocab_size=2048, hidden_size=512, intermediate_size=1024,
+                          num_attention_heads=8, num_key_value_heads=2, max_position_embeddings=256)
     return LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
 
 
@@ -99,14 +106,19 @@ def _colocated(model, prompts):
     return eng
 
 
-@pytest.mark.parametrize("A,S", [(1, 1), (2, 2)])
-def test_fused_disagg_one_gpu(A, S):
-    from fluidgpu_b200 import build, kernels
+@pytest.mark.parametrize("A,S,wide", [(1, 1, False), (2, 2, False), (1, 1, True), (2, 2, True)])
+def test_fused_disagg_one_gpu(A, S, wide):
+    from fluidgpu_b200 import _lib, build, kernels
     from fluidgpu_b200.disagg import AttentionRank, DisaggLayout, Fabric, FFNRank
     from fluidgpu_b200.model import ModelWeights
 
     build.build()
-    model = _model()
+    model = _model(wide)
+    if wide:  # the routed GEMMs split their tiles over clusters of CTAs
+        c = model.config
+        lib = _lib.lib()
+        assert lib.fg_gemm_split(3 * A, c.hidden_size, c.intermediate_size // S, 0) > 1  # down
+        assert lib.fg_gemm_split(3, c.hidden_size, c.hidden_size, 0) > 1  # O-proj
     M, b, steps = 2, 3, 12
     lay = DisaggLayout(tuple(range(A)), tuple(range(A, A + S)), M, b)
     dev = torch.device("cuda", 0)
@@ -200,7 +212,9 @@ def _worker(rank, port, q):
         r.release_graphs()
         imports.close()
         dist.destroy_process_group()
-        q.put((rank, True, (first, out) if rank == 0 else None, ""))
+        # plain lists: tensors would travel as shared-memory handles that die with this process
+        res = ([t.tolist() for t in first], [[t.tolist() for t in step] for step in out]) if rank == 0 else None
+        q.put((rank, True, res, ""))
     except BaseException:  # noqa: BLE001
         q.put((rank, False, None, traceback.format_exc()))
 
@@ -221,7 +235,8 @@ def test_fused_disagg_two_gpus_graphs():
         p.join(timeout=60)
     for rank, ok, _, msg in results:
         assert ok, f"rank {rank} failed:\n{msg}"
-    first, out = results[0][2]
+    first = [torch.tensor(t) for t in results[0][2][0]]
+    out = [[torch.tensor(t) for t in step] for step in results[0][2][1]]
     from fluidgpu_b200 import build
 
     build.build()

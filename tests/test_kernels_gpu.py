@@ -397,3 +397,106 @@ def test_rope_kv_append_tokens_matches_per_sequence():
         x = qkvd[rows.to(DEV)].contiguous()
         q2[rows.to(DEV)] = kernels.rope_kv_append(x, (start + j).to(DEV), inv_freq, 1.0, td, kc2, vc2, nq, nkv, hd)
     assert torch.equal(q1, q2) and torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
+
+
+# ---------------------------------------------------------------------------
+# hand-off kernels of the disaggregated step, one GPU (local destinations)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("T,N,K,epi,route", [
+    (32, 4096, 14336, "f32", "split"),        # down projection, split-K over 8 CTAs per tile
+    (32, 4096, 4096, "residual", "broadcast"),  # O-proj, split-K over 4 CTAs per tile
+    (64, 4096, 14336, "residual", "split"),
+    (4, 512, 512, "residual", "broadcast"),     # one CTA per tile
+])
+def test_routed_gemm_matches_plain_and_signals(T, N, K, epi, route):
+    from fluidgpu_b200 import _lib, kernels
+    from fluidgpu_b200._lib import call, ptr_array
+
+    g = _gen(21)
+    x = _randn((T, K), g).to(DEV)
+    w = kernels.PackedWeight(_randn((N, K), g, 0.02).to(DEV))
+    res = _randn((T, N), g).to(DEV)
+    code = _lib.FG_EPI_F32 if epi == "f32" else _lib.FG_EPI_RESIDUAL
+    dt = torch.float32 if epi == "f32" else torch.bfloat16
+    want = kernels.gemm(x, w, epilogue=code, residual=res)
+    n_dst = 2
+    if route == "split":
+        rows = (T + n_dst - 1) // n_dst
+        dst = [torch.full((rows, N), float("nan"), dtype=dt, device=DEV) for _ in range(n_dst)]
+        r_code, row0 = _lib.FG_ROUTE_SPLIT, 0
+    else:
+        rows, row0 = 3 * T, T  # a row block in the middle of each destination
+        dst = [torch.full((rows, N), float("nan"), dtype=dt, device=DEV) for _ in range(n_dst)]
+        r_code = _lib.FG_ROUTE_BROADCAST
+    flags = torch.zeros(n_dst * 32, dtype=torch.int32, device=DEV)  # 128 bytes apart
+    epoch = torch.tensor([5], dtype=torch.int32, device=DEV)
+    ticket = torch.zeros(1, dtype=torch.int32, device=DEV)
+    kernels.device_status(reset=True)
+    for rep in range(2):  # the ticket rearms for the next call
+        call("fg_gemm_bf16_packed_routed", x.data_ptr(), w.data.data_ptr(), res.data_ptr(), None, T, N, K, code,
+             r_code, ptr_array([d.data_ptr() for d in dst]), n_dst, rows if route == "split" else 0, row0,
+             ptr_array([flags[32 * i:32 * i + 1].data_ptr() for i in range(n_dst)]), n_dst, epoch.data_ptr(),
+             32, 7 + rep, ticket.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert int(ticket.item()) == 0, "ticket not rearmed"
+        assert flags[::32].tolist() == [5 * 32 + 7 + rep] * n_dst, flags[::32].tolist()
+    kernels.check_device("routed gemm")
+    if route == "split":
+        got = torch.cat(dst)[:T]
+    else:
+        for d in dst[1:]:
+            assert torch.equal(d[row0:row0 + T], dst[0][row0:row0 + T])
+        assert torch.isnan(dst[0][:row0].float()).all() and torch.isnan(dst[0][row0 + T:].float()).all()
+        got = dst[0][row0:row0 + T]
+    assert torch.equal(got, want), "routed result differs from fg_gemm_bf16_packed"
+
+
+def test_waiting_norms_match_rmsnorm():
+    """fg_rmsnorm_wait / fg_sum_rmsnorm_wait with their flags already at the
+    awaited value: the results of fg_rmsnorm (and of fg_sum_partials then
+    fg_rmsnorm) bit for bit."""
+    from fluidgpu_b200 import _lib, kernels
+    from fluidgpu_b200._lib import call, ptr_array
+
+    g = _gen(22)
+    T, H, S = 64, 4096, 3
+    x = _randn((T, H), g).to(DEV)
+    w = (1.0 + _randn((H,), g, 0.1)).to(DEV)
+    parts = torch.randn(S, T, H, generator=g).float().to(DEV)
+    epoch = torch.tensor([3], dtype=torch.int32, device=DEV)
+    flags = torch.full((4 * 32,), 3 * 10 + 4, dtype=torch.int32, device=DEV)  # epoch * 10 + 4 reached
+    fptr = ptr_array([flags[32 * i:32 * i + 1].data_ptr() for i in range(4)])
+    stream = torch.cuda.current_stream().cuda_stream
+    for mode in (_lib.FG_NORM_LLAMA, _lib.FG_NORM_FP32MUL):
+        out = torch.empty_like(x)
+        call("fg_rmsnorm_wait", x.data_ptr(), w.data_ptr(), out.data_ptr(), T, H, 1e-5, mode, fptr, 4, 16,
+             epoch.data_ptr(), 10, 4, 1000, stream)
+        assert torch.equal(out, kernels.rmsnorm(x, w, 1e-5, mode))
+        h = torch.empty(T, H, dtype=torch.bfloat16, device=DEV)
+        xo = torch.empty_like(h)
+        call("fg_sum_rmsnorm_wait", parts.data_ptr(), S, h.data_ptr(), w.data_ptr(), xo.data_ptr(), T, H, 1e-5,
+             mode, fptr, 4, epoch.data_ptr(), 10, 4, 1000, stream)
+        hs = kernels.sum_partials(parts)
+        assert torch.equal(h, hs)
+        assert torch.equal(xo, kernels.rmsnorm(hs, w, 1e-5, mode))
+    kernels.check_device("waiting norms")
+
+
+def test_waiting_norm_times_out_cleanly():
+    """A flag that never reaches its value: the wait gives up after its bound,
+    the device status records a peer flag timeout (site 0x501) and the
+    context stays usable."""
+    from fluidgpu_b200 import kernels
+    from fluidgpu_b200._lib import call, ptr_array
+
+    x = torch.zeros(4, 512, dtype=torch.bfloat16, device=DEV)
+    w = torch.ones(512, dtype=torch.bfloat16, device=DEV)
+    flags = torch.zeros(32, dtype=torch.int32, device=DEV)
+    epoch = torch.zeros(1, dtype=torch.int32, device=DEV)
+    kernels.device_status(reset=True)
+    call("fg_rmsnorm_wait", x.data_ptr(), w.data_ptr(), torch.empty_like(x).data_ptr(), 4, 512, 1e-5, 0,
+         ptr_array([flags.data_ptr()]), 1, 4, epoch.data_ptr(), 1, 1, 100, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    st = kernels.device_status(reset=True)
+    assert st & 0xFF == 2 and (st >> 8) == 0x501, f"status {st:#x}"
+    assert int(torch.arange(10, device=DEV).sum().item()) == 45

@@ -221,7 +221,8 @@ def _nccl_worker(rank, port, plan_dir, q):
         got = _drive(runner, dev)
         dist.barrier()
         dist.destroy_process_group()
-        q.put((rank, True, got if rank == 0 else None, ""))
+        # plain lists: tensors would travel as shared-memory handles that die with this process
+        q.put((rank, True, [t.tolist() for t in got] if rank == 0 else None, ""))
     except BaseException:  # noqa: BLE001
         q.put((rank, False, None, traceback.format_exc()))
 
@@ -247,6 +248,6 @@ def test_reference_process_group_comm_two_gpus():
 
     build.build()
     want = _native_logits(_model())
-    got = results[0][2]
+    got = [torch.tensor(x, dtype=torch.float32) for x in results[0][2]]
     for s in range(STEPS):
         assert torch.equal(got[s], want[s]), f"step {s}: NCCL two-rank logits differ from co-located"
