@@ -479,10 +479,55 @@ def run_fgb200(args) -> None:
         }
         if world == 1 and not args.no_cpu_baseline and spec is LLAMA3_8B:
             line["cpu_baseline"] = cpu_baseline_sample(B, ctx)
+        if world == 1 and spec is LLAMA3_8B and not args.no_extra_models:
+            # config 3's model on the same GPU, after the headline's memory is released
+            del eng, weights
+            kernels.Workspace.clear()
+            torch.cuda.empty_cache()
+            line["gpt_oss_20b"] = gptoss_step(dev, ctx, W, max(K // 2, 5))
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def gptoss_step(dev: torch.device, ctx: int, W: int, K: int) -> dict:
+    """gpt-oss-20b decode step (BASELINE configs[2]'s model on one GPU: batch
+    128, context 4096, MXFP4 experts, alternating 128-token windows, sinks),
+    CUDA-graph replays, device-timed: an extra line item of the N=1 run."""
+    from fluidgpu_b200 import kernels
+    from fluidgpu_b200.config import EngineConfig
+    from fluidgpu_b200.engine import DecodeEngine
+    from fluidgpu_b200.model import GPT_OSS_20B as spec
+    from fluidgpu_b200.model import ModelWeights
+
+    B = CONFIG_GPTOSS["batch_per_gpu"]
+    total = ctx + W + K + 8
+    eng = DecodeEngine(ModelWeights.random(spec, seed=0, device=dev),
+                       EngineConfig(model_name=spec.name, max_seq_len=total, world_size=1, device=str(dev),
+                                    max_batch=B, cuda_graph_decode=True))
+    eng.start(B, prompt_lens=[ctx] * B, reserve_tokens=total)
+    g = torch.Generator(device=dev).manual_seed(7)
+    eng.kv_cache.pool.normal_(0.0, 1.0, generator=g)
+    eng._tok_dev.copy_(torch.randint(0, spec.vocab, (B,), generator=g, device=dev))
+    for _ in range(W):
+        eng.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        eng.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    kernels.check_device("gpt-oss-20b step")
+    ms = e0.elapsed_time(e1) / K
+    out = {"workload": CONFIG_GPTOSS["workload"], "value": B / (ms * 1e-3), "unit": "tokens/s",
+           "ms_per_step": ms, "steps": K, "warmup": W, "dtype": "bf16 (experts MXFP4)"}
+    eng._graphs.clear()
+    del eng
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_disagg_fused(args) -> None:
@@ -831,6 +876,7 @@ def main() -> None:
     ap.add_argument("--model", default="llama-3-8b", choices=["llama-3-8b", "gpt-oss-20b"])
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra-models", action="store_true", help="N=1: skip the gpt-oss-20b line item")
     ap.add_argument("--eager", action="store_true", help="launch every kernel from the host (no CUDA graph)")
     ap.add_argument("--mode", default="auto", choices=["auto", "replicas", "disagg", "pipeline", "tp", "ep"],
                     help="auto: co-located at N=1, disagg at N>1. disagg: attention / merged-batch FFN GPUs with "

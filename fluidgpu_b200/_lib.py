@@ -117,6 +117,7 @@ SIGNATURES: dict[str, tuple] = {
         [_P, c_int, _P, _P, _P, c_int, c_int, c_float, c_int, _P, c_int, _P, c_uint, c_uint, c_int, _P],
     ),
     "fg_counter_add": (c_int, [_P, c_uint, _P]),
+    "fg_preload": (c_int, []),
 }
 
 

@@ -132,6 +132,15 @@ class _LocalMailbox:
         self.peers.clear()
 
 
+def _preload(device: torch.device) -> None:
+    """Load every kernel of the library on `device` before this rank's
+    kernels start waiting on other ranks (fg_preload)."""
+    from ._lib import call
+
+    with torch.cuda.device(device):
+        call("fg_preload")
+
+
 class _DeviceArray:
     """A CUDA array interface over a raw device pointer (a peer's slot), so
     torch can wrap it without copying."""
@@ -167,6 +176,7 @@ class P2PComm:
 
         assert dist.is_available() and dist.is_initialized(), "P2PComm needs torch.distributed"
         device = device or torch.device("cuda", torch.cuda.current_device())
+        _preload(device)
         slot = (int(slot_bytes) + 15) // 16 * 16
         rank, world = dist.get_rank(group), dist.get_world_size(group)
         mb = _PeerMailbox(dist, group, rank, world, nslot, slot, device)

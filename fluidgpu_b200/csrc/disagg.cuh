@@ -233,6 +233,57 @@ int fg_sum_rmsnorm_wait(const float* partials, int S, fg_bf16* h_out, const fg_b
                       reinterpret_cast<uint4*>(x_out), H, eps, weight_mode, ws);
 }
 
+int fg_preload(void) {
+  // the module holding this library's kernels (found through one of them),
+  // then every function in it loaded (driver entry points, no -lcuda)
+  using GetModule = CUresult (*)(CUmodule*, CUfunction);
+  using Count = CUresult (*)(unsigned int*, CUmodule);
+  using Enumerate = CUresult (*)(CUfunction*, unsigned int, CUmodule);
+  using Load = CUresult (*)(CUfunction);
+  void *p_mod = nullptr, *p_count = nullptr, *p_enum = nullptr, *p_load = nullptr;
+  cudaDriverEntryPointQueryResult q1, q2, q3, q4;
+  if (cudaGetDriverEntryPoint("cuFuncGetModule", &p_mod, cudaEnableDefault, &q1) != cudaSuccess ||
+      cudaGetDriverEntryPoint("cuModuleGetFunctionCount", &p_count, cudaEnableDefault, &q2) != cudaSuccess ||
+      cudaGetDriverEntryPoint("cuModuleEnumerateFunctions", &p_enum, cudaEnableDefault, &q3) != cudaSuccess ||
+      cudaGetDriverEntryPoint("cuFuncLoad", &p_load, cudaEnableDefault, &q4) != cudaSuccess ||
+      q1 != cudaDriverEntryPointSuccess || q2 != cudaDriverEntryPointSuccess || q3 != cudaDriverEntryPointSuccess ||
+      q4 != cudaDriverEntryPointSuccess) {
+    fg::set_last_error("fg_preload: driver entry points for module enumeration unavailable");
+    return FG_ERR_CUDA;
+  }
+  cudaFunction_t any = nullptr;
+  cudaError_t e = cudaGetFuncBySymbol(&any, reinterpret_cast<const void*>(fg::disagg::counter_add_kernel));
+  if (e != cudaSuccess) {
+    fg::set_last_error("fg_preload: cudaGetFuncBySymbol: %s", cudaGetErrorString(e));
+    return FG_ERR_CUDA;
+  }
+  CUmodule mod = nullptr;
+  unsigned int n = 0;
+  if (reinterpret_cast<GetModule>(p_mod)(&mod, reinterpret_cast<CUfunction>(any)) != CUDA_SUCCESS ||
+      reinterpret_cast<Count>(p_count)(&n, mod) != CUDA_SUCCESS) {
+    fg::set_last_error("fg_preload: cannot enumerate the library's kernels");
+    return FG_ERR_CUDA;
+  }
+  CUfunction* fns = static_cast<CUfunction*>(malloc(sizeof(CUfunction) * (n ? n : 1)));
+  if (!fns) {
+    fg::set_last_error("fg_preload: out of host memory");
+    return FG_ERR_CUDA;
+  }
+  int rc = FG_OK;
+  if (reinterpret_cast<Enumerate>(p_enum)(fns, n, mod) != CUDA_SUCCESS) {
+    fg::set_last_error("fg_preload: cuModuleEnumerateFunctions failed");
+    rc = FG_ERR_CUDA;
+  }
+  for (unsigned int i = 0; rc == FG_OK && i < n; ++i) {
+    if (reinterpret_cast<Load>(p_load)(fns[i]) != CUDA_SUCCESS) {
+      fg::set_last_error("fg_preload: cuFuncLoad failed for kernel %u of %u", i, n);
+      rc = FG_ERR_CUDA;
+    }
+  }
+  free(fns);
+  return rc;
+}
+
 int fg_counter_add(uint32_t* counter, uint32_t delta, fg_stream_t stream) {
   FG_REQUIRE(counter, "fg_counter_add: null pointer");
   return fg::launch_k("fg_counter_add", fg::disagg::counter_add_kernel, dim3(1), dim3(32), 0,

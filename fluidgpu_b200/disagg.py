@@ -165,6 +165,8 @@ class AttentionRank(_Rank):
         self.mailbox = _Mailbox(data, nflag, device)
         self.max_seq_len = max_seq_len
         b, H = lay.rows, s.hidden
+        qkv_w = weights.layers[0]["wqkv"].shape[0]
+        vocab = weights.lm_head.shape[0]
         self.mbs = []
         for m in range(lay.micro_batches):
             kv = PagedKVCache(num_layers=s.num_layers, owned_layer_ids=list(range(s.num_layers)),
@@ -178,9 +180,13 @@ class AttentionRank(_Rank):
                 "x": torch.empty(b, H, dtype=torch.bfloat16, device=device),
                 "epoch": torch.zeros(1, dtype=torch.int32, device=device),
                 "tickets": torch.zeros(s.num_layers, dtype=torch.int32, device=device),
+                # per-layer buffers: a step allocates nothing (see step())
+                "qkv": torch.empty(b, qkv_w, dtype=torch.bfloat16, device=device),
+                "q": torch.empty(b, s.n_q, s.head_dim, dtype=torch.bfloat16, device=device),
+                "a": torch.empty(b, s.n_q * s.head_dim, dtype=torch.bfloat16, device=device),
+                "logits": torch.empty(b, vocab, dtype=torch.bfloat16, device=device),
                 "slot": f"disagg{id(self):x}.{m}",
                 "graph": None,
-                "logits": None,
             })
         self.streams = [torch.cuda.Stream(device, priority=-(lay.micro_batches - 1 - m))
                         for m in range(lay.micro_batches)]
@@ -272,12 +278,13 @@ class AttentionRank(_Rank):
                     kernels.rmsnorm(mb["h"], L["ln1"], s.eps, s.norm_mode, out=mb["x"])
                 else:
                     self._norm_in(m, i, L["ln1"])
-            qkv = kernels.gemm(mb["x"], L["wqkv"], bias=L.get("bqkv"), slot=mb["slot"] + ".gemm")
+            qkv = kernels.gemm(mb["x"], L["wqkv"], bias=L.get("bqkv"), out=mb["qkv"], slot=mb["slot"] + ".gemm")
             kp, vp = kv.layer_pages(i)
             q = kernels.rope_kv_append(qkv, kv.positions[:b], W.inv_freq, W.rope_scaling, kv.block_table[:b],
-                                       kp, vp, s.n_q, s.n_kv, s.head_dim)
+                                       kp, vp, s.n_q, s.n_kv, s.head_dim, q_out=mb["q"])
             a = kernels.paged_decode_attn(q, kp, vp, kv.block_table[:b], kv.seq_lens[:b], kv.plan_len(),
-                                          window=s.window(i), sinks=L.get("sinks"), slot=mb["slot"] + ".attn")
+                                          window=s.window(i), sinks=L.get("sinks"), out=mb["a"],
+                                          slot=mb["slot"] + ".attn")
             if standalone:
                 kernels.gemm(a, L["wo"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h, bias=L.get("bo"), out=mb["h"],
                              slot=mb["slot"] + ".gemm")
@@ -292,8 +299,7 @@ class AttentionRank(_Rank):
             kernels.rmsnorm(mb["h"], W.final_norm, s.eps, s.norm_mode, out=mb["x"])
         else:
             self._norm_in(m, s.num_layers, W.final_norm)
-        logits = kernels.gemm(mb["x"], W.lm_head, slot=mb["slot"] + ".gemm")
-        mb["logits"] = logits
+        logits = kernels.gemm(mb["x"], W.lm_head, out=mb["logits"], slot=mb["slot"] + ".gemm")
         kernels.argmax(logits, out=mb["next"])
         mb["tok"].copy_(mb["next"])
         kernels.advance(kv.positions[:b], kv.seq_lens[:b])
@@ -302,14 +308,20 @@ class AttentionRank(_Rank):
 
     # -- graphs -----------------------------------------------------------------
     def reserve(self, m: int) -> None:
-        """Scratch at the size the current length bucket needs (before capture)."""
-        s, mb = self.spec, self.mbs[m]
+        """Scratch at the size the current length bucket needs, for the
+        attention and for every GEMM of the step (before a capture or an
+        eager step: a step must not allocate)."""
+        s, mb, W = self.spec, self.mbs[m], self.w
         kv = mb["kv"]
         lib = _lib.lib()
+        b = self.layout.rows
         plan = kv.plan_len()
-        need = max(lib.fg_attn_workspace_bytes(self.layout.rows, s.n_q, s.n_kv, s.head_dim, plan, s.window(i))
+        need = max(lib.fg_attn_workspace_bytes(b, s.n_q, s.n_kv, s.head_dim, plan, s.window(i))
                    for i in range(s.num_layers))
         kernels.Workspace.get(need, self.device, mb["slot"] + ".attn")
+        shapes = [W.layers[0]["wqkv"].shape, W.lm_head.shape, W.layers[0]["wo"].shape]
+        gneed = max(lib.fg_gemm_workspace_bytes(b, n, k, 0) for n, k in shapes)
+        kernels.Workspace.get(gneed, self.device, mb["slot"] + ".gemm")
 
     def capture(self, m: int, standalone: bool = False) -> None:
         """Capture micro-batch m's step for its current length bucket. Capture
@@ -339,11 +351,22 @@ class AttentionRank(_Rank):
 
     def step(self, graphs: bool = True, standalone: bool = False) -> list[torch.Tensor]:
         """One decode step of every micro-batch, interleaved on their
-        streams; returns the next-token buffers."""
+        streams; returns the next-token buffers.
+
+        Once a micro-batch is launched its kernels may wait on the FFN GPUs,
+        which go on only when the others are launched too. So nothing between
+        the launches may wait for this GPU to go idle: the step allocates no
+        device memory (buffers above, scratch reserved first) and launches no
+        kernel for the first time (the library's kernels are loaded when the
+        mailboxes are mapped)."""
         cur = torch.cuda.current_stream(self.device)
         for s in self.streams:
             s.wait_stream(cur)
         key = "alone" if standalone else "graph"
+        if not graphs:
+            for m, mb in enumerate(self.mbs):
+                mb["kv"].prepare_step(1)
+                self.reserve(m)
         if graphs:
             # capture every micro-batch's graph before replaying any: a capture
             # synchronises the device, and a replayed micro-batch can only
@@ -399,9 +422,13 @@ class FFNRank(_Rank):
         self.mailbox = _Mailbox(data, nflag, device)
         T = layout.A * layout.rows
         self.x = torch.empty(T, self.spec.hidden, dtype=torch.bfloat16, device=device)
+        gu = weights.layers[0]["w_gate_up"]
+        self.act = torch.empty(T, gu.shape[0] // 2, dtype=torch.bfloat16, device=device)
         self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
         self.tickets = torch.zeros(self.spec.num_layers * layout.micro_batches, dtype=torch.int32, device=device)
         self.slot = f"disagg-ffn{id(self):x}"
+        kernels.Workspace.get(_lib.lib().fg_gemm_workspace_bytes(T, gu.shape[0], gu.shape[1], 0), device,
+                              self.slot)
         self.stream = torch.cuda.Stream(device)
         self.graph = None
 
@@ -454,7 +481,7 @@ class FFNRank(_Rank):
                      float(s.eps), s.norm_mode, ptr_array(self.in_flags(m)), lay.A, lay.rows,
                      self.epoch.data_ptr(), self.L, i + 1, self.timeout_ms, stream)
                 ev = kernels.KernelTimer.start("ffn")
-                act = kernels.gemm(self.x, L["w_gate_up"], epilogue=_lib.FG_EPI_SWIGLU, slot=self.slot)
+                act = kernels.gemm(self.x, L["w_gate_up"], epilogue=_lib.FG_EPI_SWIGLU, out=self.act, slot=self.slot)
                 wd = L["w_down"]
                 res = inp if (lay.S == 1 or self.index == 0) else None
                 t = i * lay.micro_batches + m
@@ -480,12 +507,24 @@ class FFNRank(_Rank):
         self.graph = None
 
 
+def preload(device: torch.device) -> None:
+    """Load every kernel of the library on `device` before ranks start
+    waiting on each other (fg_preload: under lazy loading a kernel's first
+    launch waits for the device's work in flight, and a kernel spinning on
+    another GPU's flag can be part of it)."""
+    with torch.cuda.device(device):
+        call("fg_preload")
+
+
 class Fabric:
-    """Makes every rank's mailbox reachable from the ranks of the other role."""
+    """Makes every rank's mailbox reachable from the ranks of the other role
+    (and loads the library's kernels on each rank's device first)."""
 
     @staticmethod
     def local(ranks: list[_Rank]) -> None:
         """Ranks of one process on one device: plain device pointers."""
+        for d in {r.device for r in ranks}:
+            preload(d)
         bases = {r.rank: r.mailbox.ptr for r in ranks}
         for r in ranks:
             r.peer_base = dict(bases)
@@ -497,6 +536,7 @@ class Fabric:
         mailboxes of the other role. Returns the imports (close() them)."""
         import torch.distributed as dist
 
+        preload(rank.device)
         torch.cuda.synchronize(rank.device)
         handle = ctypes.create_string_buffer(64)
         off = ctypes.c_size_t(0)

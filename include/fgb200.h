@@ -387,6 +387,14 @@ int fg_sum_rmsnorm_wait(const float* partials, int S, fg_bf16* h_out, const fg_b
                         fg_stream_t stream);
 /* *counter += delta on the device (the per-step epoch of the hand-offs). */
 int fg_counter_add(uint32_t* counter, uint32_t delta, fg_stream_t stream);
+/* Load every kernel of this library into the current device's context now.
+ * Under CUDA's lazy loading a kernel's first launch loads its code, and the
+ * load waits for the device's work in flight; when that work is a kernel
+ * waiting for another GPU whose progress needs a launch this host has not
+ * made yet, the two GPUs stall each other. Ranks that wait on one another
+ * (the disaggregated step, P2PComm) call this once per device before their
+ * first step. */
+int fg_preload(void);
 
 /* positions[b] += 1 and seq_lens[b] += 1 after a decode step
  * (LayerKVCache.advance, kv_cache.py:140-144). Either pointer may be NULL. */

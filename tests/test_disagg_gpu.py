@@ -12,8 +12,14 @@ flag values and epochs are those of the multi-GPU runs.
     co-located engine per micro-batch bit for bit (same kernels, same
     reduction orders).
   - 2 attention ranks + 2 FFN ranks (tensor-parallel FFN, fp32 partials
-    summed by the consumer), 2 micro-batches: logits within the bf16
-    tolerance of the co-located engines, teacher-forced on their tokens.
+    summed by the consumer, so the hidden state rounds once where one GEMM
+    rounds twice), 2 micro-batches, teacher-forced on the co-located tokens:
+    against the fp32 oracle on the same tokens, every step within 2e-2 +
+    1e-2|x| or, over the run, no worse than 1.25x the co-located engine's own
+    deviation; greedy tokens equal the oracle's wherever its top-2 margin
+    clears twice that bound.
+  Both at a narrow model and at a wide one whose O-proj and down GEMMs split
+  every tile over a cluster of CTAs (the plans of the full-size model).
 Two GPUs (skipped on one): ranks as processes, every rank replaying its CUDA
 graphs concurrently, greedy tokens equal the co-located engines'."""
 import os
@@ -133,6 +139,14 @@ def test_fused_disagg_one_gpu(A, S, wide):
     g = torch.Generator().manual_seed(4)
     toks = {(a, m): torch.randint(0, 2048, (b,), generator=g) for a in range(A) for m in range(M)}
     refs = {k: _colocated(model, v[:, None]) for k, v in toks.items()}
+    if S > 1:
+        from oracle import decode_ref as ref
+
+        spec = ref.spec_from_hf(model.config)
+        w32 = {k: v.float() for k, v in ref.weights_from_hf(model).items()}
+        truth = {k: ref.OracleModel(spec, w32, torch.float32) for k in toks}
+        worst = {"tp": 0.0, "colo": 0.0}
+        loose = []
     for r in attn:
         r.start([[0] * b for _ in range(M)], reserve_tokens=60)
     kernels.device_status(reset=True)
@@ -160,9 +174,20 @@ def test_fused_disagg_one_gpu(A, S, wide):
             if S == 1:
                 assert torch.equal(got, want), f"step {step} rank {a} micro-batch {m}: logits differ"
             else:
-                err = (got - want).abs()
-                assert (err <= ATOL + RTOL * want.abs()).all(), f"step {step} rank {a} mb {m}: {err.max()}"
+                lt = truth[(a, m)].step(t).float()
+                err = (got - lt).abs()
+                worst["tp"] = max(worst["tp"], err.max().item())
+                worst["colo"] = max(worst["colo"], (want - lt).abs().max().item())
+                if not (err <= ATOL + RTOL * lt.abs()).all():
+                    loose.append((step, a, m))
+                top2 = lt.topk(2, dim=-1).values
+                clear = (top2[:, 0] - top2[:, 1]) > 2 * (ATOL + RTOL * top2[:, 0].abs())
+                assert torch.equal(got.argmax(-1)[clear], lt.argmax(-1)[clear]), f"step {step}: greedy tokens"
             toks[(a, m)] = want.argmax(-1)  # teacher forcing on the co-located choice
+    if S > 1:
+        print(f"A={A} S={S} wide={wide}: {len(loose)} (step, rank, micro-batch) outside 2e-2 + 1e-2|x| of the "
+              f"fp32 oracle; worst |delta| {worst['tp']:.4f} vs the co-located engine's {worst['colo']:.4f}")
+        assert not loose or worst["tp"] <= 1.25 * worst["colo"] + 1e-3, (loose, worst)
     kernels.check_device("fused disaggregated decode")
 
 
