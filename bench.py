@@ -559,7 +559,7 @@ def run_disagg_fused(args) -> None:
     weights = ModelWeights.random(spec, seed=0, device=dev,
                                   ffn_shard=(idx, lay.S) if role == "ffn" and lay.S > 1 else None)
     if role == "attn":
-        r = AttentionRank(lay, rank, weights, total, device=dev)
+        r = AttentionRank(lay, rank, weights, total, device=dev, schedule=args.schedule)
         lens = [prompt_lengths(b, ctx, args.prompt_mix, seed=rank * M + m) for m in range(M)]
         r.start(lens, reserve_tokens=total)
         g = torch.Generator(device=dev).manual_seed(1 + rank)
@@ -711,7 +711,7 @@ def run_disagg_fused(args) -> None:
             "warmup": W, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {**CONFIG, "batch_per_gpu": B, "attention_gpus": lay.A, "ffn_gpus": lay.S,
-                       "micro_batches": M, "sequences_per_micro_batch": b,
+                       "micro_batches": M, "sequences_per_micro_batch": b, "schedule": args.schedule,
                        "parallelism": (f"disaggregated: attention dp{lay.A} / FFN tp{lay.S}, {M} ping-pong micro-"
                                        f"batches of {b} per attention GPU, FFN batches merged over the attention "
                                        f"GPUs ({lay.A * b} tokens), hand-offs stored by the producing GEMM over NVLink"),
@@ -877,6 +877,9 @@ def main() -> None:
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra-models", action="store_true", help="N=1: skip the gpt-oss-20b line item")
+    ap.add_argument("--schedule", default="interleaved", choices=["interleaved", "streams"],
+                    help="disagg attention GPUs: micro-batches alternating layer by layer on one stream, or each "
+                         "on a stream of its own")
     ap.add_argument("--eager", action="store_true", help="launch every kernel from the host (no CUDA graph)")
     ap.add_argument("--mode", default="auto", choices=["auto", "replicas", "disagg", "pipeline", "tp", "ep"],
                     help="auto: co-located at N=1, disagg at N>1. disagg: attention / merged-batch FFN GPUs with "

@@ -157,9 +157,12 @@ class AttentionRank(_Rank):
     paged KV cache, buffers, stream and graph."""
 
     def __init__(self, layout: DisaggLayout, rank: int, weights: ModelWeights, max_seq_len: int, *,
-                 device: torch.device, timeout_ms: int = 10000) -> None:
+                 device: torch.device, timeout_ms: int = 10000, schedule: str = "interleaved") -> None:
         super().__init__(layout, rank, weights, device, timeout_ms)
         assert self.role == "attn"
+        assert schedule in ("interleaved", "streams"), f"unknown schedule {schedule!r}"
+        self.schedule = schedule
+        self._graphs: dict[str, tuple[torch.cuda.CUDAGraph, tuple[int, ...]]] = {}
         s, lay = self.spec, layout
         data, nflag = self.attn_geometry()
         self.mailbox = _Mailbox(data, nflag, device)
@@ -226,7 +229,7 @@ class AttentionRank(_Rank):
         for mb, lens in zip(self.mbs, prompt_lens):
             assert len(lens) == self.layout.rows
             mb["kv"].start_batch(lens, reserve_tokens)
-            mb["graph"] = None
+        self.release_graphs()
 
     def set_tokens(self, m: int, tokens: torch.Tensor) -> None:
         self.mbs[m]["tok"].copy_(tokens.reshape(-1))
@@ -262,6 +265,23 @@ class AttentionRank(_Rank):
         left out (no hand-offs, the O-proj result is the next layer's input):
         a timing reference for how much of the step the hand-offs and the
         remote FFN add, not a model computation."""
+        for _ in self._enqueue(m, standalone):
+            pass
+
+    def step_interleaved(self, standalone: bool = False) -> None:
+        """Enqueue one decode step of every micro-batch on the current stream,
+        layer by layer: micro-batch 0's layer l, micro-batch 1's layer l, ...,
+        then layer l + 1. While one micro-batch's attention runs here, the FFN
+        GPUs work on the one before it, and its answer is back by the time
+        this stream reaches that micro-batch's next layer."""
+        gens = [self._enqueue(m, standalone) for m in range(len(self.mbs))]
+        while gens:
+            gens = [g for g in gens if next(g, StopIteration) is not StopIteration]
+
+    def _enqueue(self, m: int, standalone: bool):
+        """Generator enqueuing micro-batch m's step; it yields after each
+        layer's hand-off to the FFN ranks (the points where another
+        micro-batch's layer may be enqueued)."""
         s, lay, mb, W = self.spec, self.layout, self.mbs[m], self.w
         kv = mb["kv"]
         b = lay.rows
@@ -269,8 +289,8 @@ class AttentionRank(_Rank):
         kernels.rmsnorm(mb["h"], W.layers[0]["ln1"], s.eps, s.norm_mode, out=mb["x"])
         dsts = ptr_array(self.ffn_in_rows(m)) if not standalone else None
         sigs = ptr_array(self.ffn_in_flags(m)) if not standalone else None
-        stream = kernels._stream(self.device)
         for i in range(s.num_layers):
+            stream = kernels._stream(self.device)
             L = W.layers[i]
             h = mb["h"] if (i == 0 or standalone) else self._residual(m)
             if i > 0:
@@ -288,13 +308,15 @@ class AttentionRank(_Rank):
             if standalone:
                 kernels.gemm(a, L["wo"], epilogue=_lib.FG_EPI_RESIDUAL, residual=h, bias=L.get("bo"), out=mb["h"],
                              slot=mb["slot"] + ".gemm")
-                continue
-            wo = L["wo"]
-            call("fg_gemm_bf16_packed_routed", a.data_ptr(), wo.data.data_ptr(), h.data_ptr(),
-                 None if L.get("bo") is None else L["bo"].data_ptr(), b, s.hidden, s.n_q * s.head_dim,
-                 _lib.FG_EPI_RESIDUAL, _lib.FG_ROUTE_BROADCAST, dsts, lay.S, b, self.index * b, sigs, lay.S,
-                 mb["epoch"].data_ptr(), self.L, i + 1, mb["tickets"][i:i + 1].data_ptr(), stream)
-            self._hook("after_send", "in", m, i)
+            else:
+                wo = L["wo"]
+                call("fg_gemm_bf16_packed_routed", a.data_ptr(), wo.data.data_ptr(), h.data_ptr(),
+                     None if L.get("bo") is None else L["bo"].data_ptr(), b, s.hidden, s.n_q * s.head_dim,
+                     _lib.FG_EPI_RESIDUAL, _lib.FG_ROUTE_BROADCAST, dsts, lay.S, b, self.index * b, sigs, lay.S,
+                     mb["epoch"].data_ptr(), self.L, i + 1, mb["tickets"][i:i + 1].data_ptr(), stream)
+                self._hook("after_send", "in", m, i)
+            yield
+        stream = kernels._stream(self.device)
         if standalone:
             kernels.rmsnorm(mb["h"], W.final_norm, s.eps, s.norm_mode, out=mb["x"])
         else:
@@ -323,35 +345,57 @@ class AttentionRank(_Rank):
         gneed = max(lib.fg_gemm_workspace_bytes(b, n, k, 0) for n, k in shapes)
         kernels.Workspace.get(gneed, self.device, mb["slot"] + ".gemm")
 
+    def _bucket_for_step(self, m: int) -> int:
+        kv = self.mbs[m]["kv"]
+        return kv.bucket(kv.max_attended())
+
+    def _capture(self, ms: list[int], standalone: bool) -> tuple[torch.cuda.CUDAGraph, tuple[int, ...]]:
+        """Capture the step of micro-batches `ms` (one of them: that
+        micro-batch's step; all of them: the interleaved step) for their
+        current length buckets, on the first one's stream."""
+        buckets = []
+        snaps = []
+        for m in ms:
+            kv = self.mbs[m]["kv"]
+            kv.prepare_step(1)
+            self.reserve(m)
+            buckets.append(self._bucket_for_step(m))
+            snaps.append(kv.snapshot_host())
+            kv.plan_len_override = buckets[-1]
+        g = torch.cuda.CUDAGraph()
+        s = self.streams[ms[0]]
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        try:
+            with torch.cuda.stream(s), torch.inference_mode():
+                with torch.cuda.graph(g, stream=s):
+                    if len(ms) == 1:
+                        self.step_mb(ms[0], standalone)
+                    else:
+                        self.step_interleaved(standalone)
+        finally:
+            for m, snap in zip(ms, snaps):
+                kv = self.mbs[m]["kv"]
+                kv.plan_len_override = None
+                kv.restore_host(snap)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        return g, tuple(buckets)
+
     def capture(self, m: int, standalone: bool = False) -> None:
         """Capture micro-batch m's step for its current length bucket. Capture
         synchronises this GPU: call it only while no replay of this rank
         waits on the FFN GPUs for a micro-batch not yet launched (step()
         captures all micro-batches before replaying any)."""
-        mb = self.mbs[m]
-        kv = mb["kv"]
-        kv.prepare_step(1)
-        bucket = kv.bucket(kv.max_attended())
-        self.reserve(m)
-        snap = kv.snapshot_host()
-        kv.plan_len_override = bucket
-        g = torch.cuda.CUDAGraph()
-        s = self.streams[m]
-        s.wait_stream(torch.cuda.current_stream(self.device))
-        try:
-            with torch.cuda.stream(s), torch.inference_mode():
-                with torch.cuda.graph(g, stream=s):
-                    self.step_mb(m, standalone)
-        finally:
-            kv.plan_len_override = None
-            kv.restore_host(snap)
-        torch.cuda.current_stream(self.device).wait_stream(s)
         key = "alone" if standalone else "graph"
-        mb[key], mb[key + "_bucket"] = g, bucket
+        mb = self.mbs[m]
+        mb[key], (mb[key + "_bucket"],) = self._capture([m], standalone)
 
     def step(self, graphs: bool = True, standalone: bool = False) -> list[torch.Tensor]:
-        """One decode step of every micro-batch, interleaved on their
-        streams; returns the next-token buffers.
+        """One decode step of every micro-batch; returns the next-token buffers.
+
+        schedule "interleaved" (the default): one stream, micro-batches
+        alternating layer by layer (step_interleaved), one graph for all.
+        schedule "streams": each micro-batch on a stream and graph of its own,
+        the GPU interleaving them as their waits allow.
 
         Once a micro-batch is launched its kernels may wait on the FFN GPUs,
         which go on only when the others are launched too. So nothing between
@@ -367,26 +411,41 @@ class AttentionRank(_Rank):
             for m, mb in enumerate(self.mbs):
                 mb["kv"].prepare_step(1)
                 self.reserve(m)
-        if graphs:
-            # capture every micro-batch's graph before replaying any: a capture
-            # synchronises the device, and a replayed micro-batch can only
-            # finish after the FFN GPUs have processed the others' messages
+        if self.schedule == "interleaved":
+            s = self.streams[0]
+            with torch.cuda.stream(s):
+                for mb in self.mbs:
+                    mb["kv"].prepare_step(1)
+                if graphs:
+                    want = tuple(self._bucket_for_step(m) for m in range(len(self.mbs)))
+                    if self._graphs.get(key, (None, None))[1] != want:
+                        self._graphs[key] = self._capture(list(range(len(self.mbs))), standalone)
+                    self._graphs[key][0].replay()
+                else:
+                    with torch.inference_mode():
+                        self.step_interleaved(standalone)
+                for mb in self.mbs:
+                    mb["kv"].host_advance(1)
+        else:
+            if graphs:
+                # capture every micro-batch's graph before replaying any: a capture
+                # synchronises the device, and a replayed micro-batch can only
+                # finish after the FFN GPUs have processed the others' messages
+                for m, (mb, s) in enumerate(zip(self.mbs, self.streams)):
+                    with torch.cuda.stream(s):
+                        mb["kv"].prepare_step(1)
+                        if mb.get(key) is None or self._bucket_for_step(m) != mb[key + "_bucket"]:
+                            self.capture(m, standalone)
             for m, (mb, s) in enumerate(zip(self.mbs, self.streams)):
                 kv = mb["kv"]
                 with torch.cuda.stream(s):
                     kv.prepare_step(1)
-                    if mb.get(key) is None or kv.bucket(kv.max_attended()) != mb[key + "_bucket"]:
-                        self.capture(m, standalone)
-        for m, (mb, s) in enumerate(zip(self.mbs, self.streams)):
-            kv = mb["kv"]
-            with torch.cuda.stream(s):
-                kv.prepare_step(1)
-                if graphs:
-                    mb[key].replay()
-                else:
-                    with torch.inference_mode():
-                        self.step_mb(m, standalone)
-                kv.host_advance(1)
+                    if graphs:
+                        mb[key].replay()
+                    else:
+                        with torch.inference_mode():
+                            self.step_mb(m, standalone)
+                    kv.host_advance(1)
         for s in self.streams:
             cur.wait_stream(s)
         return [mb["next"] for mb in self.mbs]
@@ -401,6 +460,7 @@ class AttentionRank(_Rank):
                 mb["kv"].host_advance(1)
 
     def release_graphs(self) -> None:
+        self._graphs.clear()
         for mb in self.mbs:
             mb["graph"] = None
             mb["alone"] = None

@@ -19,9 +19,12 @@ flag values and epochs are those of the multi-GPU runs.
     deviation; greedy tokens equal the oracle's wherever its top-2 margin
     clears twice that bound.
   Both at a narrow model and at a wide one whose O-proj and down GEMMs split
-  every tile over a cluster of CTAs (the plans of the full-size model).
+  every tile over a cluster of CTAs (the plans of the full-size model), and
+  under both attention-side schedules: micro-batches on streams of their own,
+  and micro-batches alternating layer by layer on one stream.
 Two GPUs (skipped on one): ranks as processes, every rank replaying its CUDA
-graphs concurrently, greedy tokens equal the co-located engines'."""
+graphs concurrently (both schedules), greedy tokens equal the co-located
+engines'."""
 import os
 import queue
 import socket
@@ -112,8 +115,10 @@ def _colocated(model, prompts):
     return eng
 
 
-@pytest.mark.parametrize("A,S,wide", [(1, 1, False), (2, 2, False), (1, 1, True), (2, 2, True)])
-def test_fused_disagg_one_gpu(A, S, wide):
+@pytest.mark.parametrize("A,S,wide,schedule", [(1, 1, False, "streams"), (2, 2, False, "streams"),
+                                                (1, 1, True, "streams"), (2, 2, True, "streams"),
+                                                (1, 1, False, "interleaved"), (2, 2, True, "interleaved")])
+def test_fused_disagg_one_gpu(A, S, wide, schedule):
     from fluidgpu_b200 import _lib, build, kernels
     from fluidgpu_b200.disagg import AttentionRank, DisaggLayout, Fabric, FFNRank
     from fluidgpu_b200.model import ModelWeights
@@ -128,8 +133,8 @@ def test_fused_disagg_one_gpu(A, S, wide):
     M, b, steps = 2, 3, 12
     lay = DisaggLayout(tuple(range(A)), tuple(range(A, A + S)), M, b)
     dev = torch.device("cuda", 0)
-    attn = [AttentionRank(lay, a, ModelWeights.from_hf(model, dev), 64, device=dev, timeout_ms=5000)
-            for a in range(A)]
+    attn = [AttentionRank(lay, a, ModelWeights.from_hf(model, dev), 64, device=dev, timeout_ms=5000,
+                          schedule=schedule) for a in range(A)]
     ffn = [FFNRank(lay, A + j, ModelWeights.from_hf(model, dev, ffn_shard=(j, S) if S > 1 else None),
                    device=dev, timeout_ms=5000) for j in range(S)]
     Fabric.local(attn + ffn)
@@ -164,8 +169,21 @@ def test_fused_disagg_one_gpu(A, S, wide):
                 kv.host_advance(1)
             return go
 
-        fns = [attn_mb(a, m) for a in range(A) for m in range(M)] + [lambda j=j: ffn[j].step(graphs=False)
-                                                                        for j in range(S)]
+        def attn_rank(a):  # one thread per attention rank, its micro-batches layer by layer
+            def go():
+                for mb in attn[a].mbs:
+                    mb["kv"].prepare_step(1)
+                with torch.inference_mode():
+                    attn[a].step_interleaved()
+                for mb in attn[a].mbs:
+                    mb["kv"].host_advance(1)
+            return go
+
+        if schedule == "interleaved":
+            fns = [attn_rank(a) for a in range(A)]
+        else:
+            fns = [attn_mb(a, m) for a in range(A) for m in range(M)]
+        fns += [lambda j=j: ffn[j].step(graphs=False) for j in range(S)]
         _run_parallel(fns)
         torch.cuda.synchronize()
         for (a, m), t in toks.items():
@@ -198,7 +216,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, port, q):
+def _worker(rank, port, q, schedule):
     try:
         import torch.distributed as dist
 
@@ -216,7 +234,8 @@ def _worker(rank, port, q):
         M, b, steps = 2, 4, 10
         lay = DisaggLayout((0,), (1,), M, b)
         w = ModelWeights.from_hf(model, dev)
-        r = AttentionRank(lay, 0, w, 64, device=dev) if rank == 0 else FFNRank(lay, 1, w, device=dev)
+        r = (AttentionRank(lay, 0, w, 64, device=dev, schedule=schedule) if rank == 0
+             else FFNRank(lay, 1, w, device=dev))
         imports = Fabric.ipc(r)
         g = torch.Generator().manual_seed(5)
         first = [torch.randint(0, 2048, (b,), generator=g) for _ in range(M)]
@@ -244,7 +263,8 @@ def _worker(rank, port, q):
         q.put((rank, False, None, traceback.format_exc()))
 
 
-def test_fused_disagg_two_gpus_graphs():
+@pytest.mark.parametrize("schedule", ["interleaved", "streams"])
+def test_fused_disagg_two_gpus_graphs(schedule):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -252,7 +272,7 @@ def test_fused_disagg_two_gpus_graphs():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, port, q, schedule)) for r in range(2)]
     for p in procs:
         p.start()
     results = sorted((q.get(timeout=300) for _ in procs), key=lambda x: x[0])
