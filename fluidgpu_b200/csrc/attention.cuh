@@ -452,12 +452,35 @@ inline int occupancy(int hd) {
 }
 
 // Split plan: slices per (sequence, kv head) for a batch whose longest
-// sequence has max_seq_len tokens (window bounds the span). The kernel is
-// HBM-bound and its CTAs do equal work, so the slice count is chosen for
-// whole waves: among S with >= kMinSlice pages per slice, the one whose
-// B*nkv*S CTAs fill the last wave of (resident CTAs per SM x SMs) best, with
-// a small charge per slice for the extra partials. The kernel then splits
-// each sequence's actual pages evenly over its slices.
+// sequence has max_seq_len tokens (window bounds the span). Each candidate
+// slice count S is priced with a model of this kernel on B200, fitted to a
+// sweep of batch 16-128 x context 2048-8192 (32 q / 8 kv heads, hd 128;
+// within 8% of every measured time):
+//   - the B*nkv*S CTAs run in waves of (resident CTAs per SM x SMs);
+//   - a CTA streams its K/V pages at most kCtaRate (its own copy and math
+//     pipeline), all resident CTAs together at most kReadRate (HBM, reads);
+//   - each wave adds kWaveCost (a CTA's prologue, pipeline fill, partials);
+//   - S > 1 adds the merge kernel: kMergeCost plus its partials' traffic.
+// Few slices leave SMs idle or the last wave long; many slices pay the
+// per-CTA cost and the merge. The cheapest S wins (the fewer on a tie).
+// The kernel then splits each sequence's actual pages evenly over its slices.
+constexpr double kCtaRate = 24.2e3;   // bytes per microsecond, one CTA
+constexpr double kReadRate = 7.44e6;  // bytes per microsecond, all CTAs
+constexpr double kWaveCost = 3.4;     // microseconds per wave
+constexpr double kMergeCost = 5.8;    // microseconds, the merge kernel
+
+inline double plan_cost_us(double pairs, double bytes_per_pair, int s, double slots, int hd) {
+  const double n = pairs * s;
+  const double w = bytes_per_pair / s;  // bytes per CTA
+  const double full = floor(n / slots), rem = n - full * slots;
+  double t = full * (w / fmin(kCtaRate, kReadRate / slots) + kWaveCost);
+  if (rem > 0) t += w / fmin(kCtaRate, kReadRate / rem) + kWaveCost;
+  // partial O and (m, l) per (query head, slice), written then read; four
+  // query heads per kv head assumed for the partials' size
+  if (s > 1) t += kMergeCost + pairs * 4.0 * s * (hd * 4.0 + 8.0) * 2.0 / kReadRate;
+  return t;
+}
+
 inline int plan_splits(int B, int nkv, int hd, int max_seq_len, int window) {
   int span = max_seq_len;
   if (window > 0 && window + kBlock < span) span = window + kBlock;
@@ -466,17 +489,16 @@ inline int plan_splits(int B, int nkv, int hd, int max_seq_len, int window) {
   const int occ = occupancy(hd);
   const double slots = (double)(occ > 0 ? occ : 2) * num_sms();
   const double pairs = (double)B * nkv;
+  const double bytes_per_pair = (double)pages * kBlock * hd * 2.0 /* K and V */ * 2.0 /* bf16 */;
   int max_s = pages / kMinSlice;
   if (max_s > kMaxSplits) max_s = kMaxSplits;
   if (max_s < 1) max_s = 1;
   int best_s = 1;
-  double best = -1.0;
-  for (int s = 1; s <= max_s; ++s) {
-    const double waves = pairs * s / slots;
-    const double eff = waves / ceil(waves);
-    const double score = eff - 0.002 * s;
-    if (score > best + 1e-9) {
-      best = score;
+  double best = plan_cost_us(pairs, bytes_per_pair, 1, slots, hd);
+  for (int s = 2; s <= max_s; ++s) {
+    const double t = plan_cost_us(pairs, bytes_per_pair, s, slots, hd);
+    if (t < best * (1.0 - 1e-9)) {
+      best = t;
       best_s = s;
     }
   }

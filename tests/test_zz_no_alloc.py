@@ -90,13 +90,17 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
 
     build.build()
     lib = _lib.lib()
-    # 32 sequences x 128 query heads at 32K tokens: 4 splits of fp32 partials > 8 MiB
-    need = lib.fg_attn_workspace_bytes(32, 128, 8, 128, 32768, 0)
-    assert need > (8 << 20)
+    # a shape whose split plan on this GPU needs more than the 8 MiB built in
+    # (the plan depends on the SM count and the kernel's occupancy)
+    shapes = [(B, nq, nkv, ctx) for nq, nkv in ((128, 8), (256, 16), (512, 32))
+              for B in (8, 16, 32, 64, 128) for ctx in (32768, 131072)]
+    big = [sh for sh in shapes if lib.fg_attn_workspace_bytes(sh[0], sh[1], sh[2], 128, sh[3], 0) > (8 << 20)]
+    assert big, "no candidate shape needs more than the built-in scratch"
+    B, nq, nkv, ctx = big[0]
     dummy = torch.zeros(16, dtype=torch.bfloat16, device=DEV)
     rc = lib.fg_paged_decode_attn_noalloc(
         dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(),
-        None, dummy.data_ptr(), 32, 128, 8, 128, 16, 1, 2048, 32768, 0, 0.1,
+        None, dummy.data_ptr(), B, nq, nkv, 128, 16, 1, ctx // 16, ctx, 0, 0.1,
         torch.cuda.current_stream().cuda_stream)
     assert rc == _lib.FG_ERR_ARG
     assert b"built-in" in lib.fg_last_error()
