@@ -34,8 +34,8 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
+import threading
 import time
 from pathlib import Path
 
@@ -73,63 +73,75 @@ def measured_peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi SM clock / throttle reasons sampled every 200 ms."""
+    """SM clock, power and clock-event (throttle) reasons of this process's
+    GPU, sampled through NVML every 10 ms from a thread while the timed region
+    runs, plus one sample at its start and one at its end (a region of a few
+    hundred milliseconds still gets a record). The GPU is found by UUID, so the
+    sample is of the device this rank runs on whatever CUDA_VISIBLE_DEVICES
+    says."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index: int) -> None:
-        self.gpu = gpu_index
-        self.proc = None
-        self.out = None
-        self.path = Path(f"/tmp/fgb200_clocks_{os.getpid()}.csv")
+    def __init__(self, cuda_index: int, period_s: float = 0.01) -> None:
+        self.period = period_s
+        self.rows: list[tuple[float, float, int]] = []
+        self.handle = None
+        self.max_mhz = None
+        self.err = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            self.nv = pynvml
+            pynvml.nvmlInit()
+            try:
+                uuid = str(torch.cuda.get_device_properties(cuda_index).uuid)
+                uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            except Exception:  # noqa: BLE001
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            get = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None)
+            self._reasons = get or pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception as e:  # noqa: BLE001
+            self.handle = None
+            self.err = f"NVML unavailable: {type(e).__name__}"
+
+    def _sample(self) -> None:
+        nv, h = self.nv, self.handle
+        try:
+            self.rows.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                              nv.nvmlDeviceGetPowerUsage(h) / 1000.0, int(self._reasons(h))))
+        except Exception as e:  # noqa: BLE001
+            self.err = f"NVML query failed: {type(e).__name__}"
+
+    def _run(self) -> None:
+        while not self._stop.wait(self.period):
+            self._sample()
 
     def start(self) -> None:
-        try:
-            self.out = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu), "-lms", "200"],
-                stdout=self.out, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
-            self._close()
-            self.path.unlink(missing_ok=True)
-
-    def _close(self) -> None:
-        if self.out is not None:
-            self.out.close()
-            self.out = None
+        if self.handle is None:
+            return
+        self.rows = []
+        self._stop.clear()
+        self._sample()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
 
     def stop(self) -> dict:
-        if self.proc is None:
-            self._close()
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-            self.proc.wait(timeout=5)
-        self._close()
-        rows = []
-        for line in self.path.read_text().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        try:
-            self.path.unlink()
-        except Exception:
-            pass
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        if self.handle is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "NVML unavailable"]}
+        self._stop.set()
+        self._thread.join(timeout=5)
+        self._sample()
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [self.err or "no samples"]}
+        reasons = sorted({name for _, _, bits in self.rows for bit, name in self.REASONS.items() if bits & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": self.max_mhz,
+                "power_w": statistics.median(r[1] for r in self.rows), "reasons": reasons,
+                "samples": len(self.rows), "source": "NVML, 10 ms"}
 
 
 def attn_bytes(meta: dict, lens_sum: int) -> float:
@@ -552,7 +564,7 @@ def run_disagg_fused(args) -> None:
     B = args.batch or 64
     assert B % M == 0, f"--batch {B} must split into {M} micro-batches"
     b = B // M
-    lay = DisaggLayout.split(world, M, b)
+    lay = DisaggLayout.split(world, M, b, args.handoff)
     role, idx = lay.role(rank)
     ctx, W, K, R = args.context, args.warmup, args.steps, 3
     total = ctx + W + 2 * K + 3 * R + 8
@@ -638,15 +650,11 @@ def run_disagg_fused(args) -> None:
     e2e_ms = f0.elapsed_time(f1)
 
     # ---- per-role kernel times from event pairs on the launching stream ----
-    # FFN GPUs: R eager steps of every rank (the FFN GEMM pair after each wait)
-    if role == "ffn":
-        kernels.KernelTimer.enable("ffn")
+    # R eager steps of every rank (the launches the graphs replay, from the host)
     for _ in range(R):
         step(graphs=False)
     torch.cuda.synchronize()
-    timed = kernels.KernelTimer.durations_ms("ffn") if role == "ffn" else []
-    kernels.KernelTimer.disable()
-    kernels.check_device("disagg roofline region")
+    kernels.check_device("disagg eager steps")
     dist.barrier()
     role_stats = {}
     if role == "attn":
@@ -679,11 +687,12 @@ def run_disagg_fused(args) -> None:
         torch.cuda.synchronize()
         role_stats["alone_ms_per_step"] = a0.elapsed_time(a1) / R
     else:
-        tot_ms = sum(d for d, _ in timed)
-        tot_b = sum(3.0 * meta["H"] * meta["I"] * 2 + meta["T"] * meta["H"] * 2 * 2 for _, meta in timed)
-        tot_f = sum(2.0 * meta["T"] * 3 * meta["H"] * meta["I"] for _, meta in timed)
-        role_stats = {"ffn_bytes": tot_b, "ffn_flops": tot_f, "ffn_ms": tot_ms, "ffn_pairs": len(timed),
-                      "T": timed[0][1]["T"] if timed else 0}
+        # FFN GPUs: their own kernels for one (layer, micro-batch) with no
+        # waits, graph-replayed: RMSNorm + gate/up (SwiGLU) + down
+        pair_ms = r.time_standalone(R)
+        T, H, I = lay.A * b, spec.hidden, r.w.layers[0]["w_down"].K
+        role_stats = {"ffn_bytes": 3.0 * H * I * 2 + T * H * 2 * 2, "ffn_flops": 2.0 * T * 3 * H * I,
+                      "ffn_ms": pair_ms, "T": T, "I": I}
     kernels.check_device("disagg stand-alone region")
     t = torch.tensor([ms, e2e_ms, float(launches)], device=dev)
     dist.all_reduce(t[:2], op=dist.ReduceOp.MAX)
@@ -699,9 +708,9 @@ def run_disagg_fused(args) -> None:
         a_stats = [s for ro, s in stats if ro == "attn"]
         f_stats = [s for ro, s in stats if ro == "ffn"]
         attn_gbs = sum(s["attn_bytes"] for s in a_stats) / (sum(s["attn_ms"] for s in a_stats) * 1e-3) / 1e9
-        ffn_ms = sum(s["ffn_ms"] for s in f_stats)
-        ffn_gbs = sum(s["ffn_bytes"] for s in f_stats) / (ffn_ms * 1e-3) / 1e9
-        ffn_tf = sum(s["ffn_flops"] for s in f_stats) / (ffn_ms * 1e-3) / 1e12
+        ffn_ms = max(s["ffn_ms"] for s in f_stats)  # per (layer, micro-batch), slowest FFN GPU
+        ffn_gbs = f_stats[0]["ffn_bytes"] / (ffn_ms * 1e-3) / 1e9
+        ffn_tf = f_stats[0]["ffn_flops"] / (ffn_ms * 1e-3) / 1e12
         step_ms = ms / K
         alone = max(s["alone_ms_per_step"] for s in a_stats)
         nv = nvlink_bytes_per_step(lay, spec.hidden, spec.num_layers)
@@ -712,6 +721,7 @@ def run_disagg_fused(args) -> None:
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {**CONFIG, "batch_per_gpu": B, "attention_gpus": lay.A, "ffn_gpus": lay.S,
                        "micro_batches": M, "sequences_per_micro_batch": b, "schedule": args.schedule,
+                       "handoff": args.handoff,
                        "parallelism": (f"disaggregated: attention dp{lay.A} / FFN tp{lay.S}, {M} ping-pong micro-"
                                        f"batches of {b} per attention GPU, FFN batches merged over the attention "
                                        f"GPUs ({lay.A * b} tokens), hand-offs stored by the producing GEMM over NVLink"),
@@ -722,9 +732,14 @@ def run_disagg_fused(args) -> None:
             "roofline": {"bound": "hbm", "kernel": "fg_paged_decode_attn (attention GPUs)", "achieved": attn_gbs,
                          "peak": hbm, "unit": "GB/s", "frac": attn_gbs / hbm, "peak_source": f"{peak_src} (hbm_gbs)",
                          "traffic": None},
-            "ffn_roofline": {"kernel": "gate_up + down GEMMs (FFN GPUs)", "tokens_per_gemm": f_stats[0]["T"],
+            "ffn_roofline": {"kernel": "RMSNorm + gate_up (SwiGLU) + down GEMMs per FFN GPU, one (layer, "
+                                       "micro-batch), graph-replayed without waits",
+                             "tokens_per_gemm": f_stats[0]["T"], "intermediate_per_gpu": f_stats[0]["I"],
+                             "us_per_layer_micro_batch": ffn_ms * 1e3,
                              "achieved_gbs": ffn_gbs, "hbm_frac": ffn_gbs / hbm, "achieved_tflops": ffn_tf,
-                             "tensor_frac": ffn_tf / tflops, "tensor_peak_source": "measured (bf16_tflops_sustained)"},
+                             "tensor_frac": ffn_tf / tflops, "tensor_peak_source": "measured (bf16_tflops_sustained)",
+                             "note": "decode-size GEMMs are weight-streaming: hbm_frac is their roofline, "
+                                     "tensor_frac what the tokens make of the tensor pipe"},
             "handoff": {"nvlink_bytes_per_step": nv, "nvlink_us_per_step_at_770GBs": nv / 770e9 * 1e6,
                         "attention_alone_ms_per_step": alone,
                         "exposed_frac": max(0.0, 1.0 - alone / step_ms),
@@ -877,6 +892,9 @@ def main() -> None:
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra-models", action="store_true", help="N=1: skip the gpt-oss-20b line item")
+    ap.add_argument("--handoff", default="pull", choices=["pull", "push"],
+                    help="disagg: FFN GPUs read the O-proj rows from the attention GPUs (pull), or the O-proj "
+                         "epilogue stores them into every FFN GPU (push)")
     ap.add_argument("--schedule", default="interleaved", choices=["interleaved", "streams"],
                     help="disagg attention GPUs: micro-batches alternating layer by layer on one stream, or each "
                          "on a stream of its own")

@@ -112,6 +112,11 @@ SIGNATURES: dict[str, tuple] = {
     "fg_rmsnorm_wait": (
         c_int, [_P, _P, _P, c_int, c_int, c_float, c_int, _P, c_int, c_int, _P, c_uint, c_uint, c_int, _P],
     ),
+    "fg_rmsnorm_gather_wait": (
+        c_int,
+        [_P, c_int, c_int, _P, _P, _P, c_int, c_int, c_float, c_int, _P, c_int, c_int, _P, c_uint, c_uint, c_int,
+         _P],
+    ),
     "fg_sum_rmsnorm_wait": (
         c_int,
         [_P, c_int, _P, _P, _P, c_int, c_int, c_float, c_int, _P, c_int, _P, c_uint, c_uint, c_int, _P],

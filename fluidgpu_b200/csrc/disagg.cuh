@@ -49,18 +49,29 @@ __device__ __forceinline__ void wait_row(const WaitSpec& w, int row, unsigned in
   __syncthreads();
 }
 
-// out[r] = RMSNorm(x[r]) once row r's flag has arrived (fg_rmsnorm semantics)
-template <int THREADS>
+// Rows gathered from other GPUs' buffers: row r is row r % rows_per_src of
+// src[r / rows_per_src] (a peer's memory, read over NVLink), copied to
+// copy[r] on this GPU as it is read.
+struct GatherSpec {
+  const uint4* src[kMaxFlags];
+  int rows_per_src;
+  uint4* copy;
+};
+
+// out[r] = RMSNorm(x[r]) once row r's flag has arrived (fg_rmsnorm semantics);
+// GATHER: x[r] is read from gs.src (and kept in gs.copy) instead of x
+template <int THREADS, bool GATHER>
 __global__ void __launch_bounds__(THREADS) rmsnorm_wait_kernel(const uint4* __restrict__ x,
                                                                const uint4* __restrict__ w,
                                                                uint4* __restrict__ out, int H, float eps,
-                                                               int mode, const WaitSpec ws) {
+                                                               int mode, const WaitSpec ws, const GatherSpec gs) {
   griddep_wait();
   __shared__ float red[THREADS / 32];
   wait_row(ws, blockIdx.x, 0x501);
   griddep_launch_dependents();
   const int H8 = H >> 3;
-  const uint4* xr = x + (int64_t)blockIdx.x * H8;
+  const uint4* xr = GATHER ? gs.src[blockIdx.x / gs.rows_per_src] + (int64_t)(blockIdx.x % gs.rows_per_src) * H8
+                           : x + (int64_t)blockIdx.x * H8;
   uint4* orow = out + (int64_t)blockIdx.x * H8;
   constexpr int kMaxVec = 4;
   uint4 xv[kMaxVec];
@@ -68,8 +79,13 @@ __global__ void __launch_bounds__(THREADS) rmsnorm_wait_kernel(const uint4* __re
 #pragma unroll
   for (int j = 0; j < kMaxVec; ++j) {
     const int i = threadIdx.x + j * THREADS;
+    if (i < H8) xv[j] = __ldcg(xr + i);  // all of the row's loads in flight at once
+  }
+#pragma unroll
+  for (int j = 0; j < kMaxVec; ++j) {
+    const int i = threadIdx.x + j * THREADS;
     if (i < H8) {
-      xv[j] = __ldcg(xr + i);
+      if (GATHER) gs.copy[(int64_t)blockIdx.x * H8 + i] = xv[j];
       const uint32_t* p = reinterpret_cast<const uint32_t*>(&xv[j]);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -206,10 +222,49 @@ int fg_rmsnorm_wait(const fg_bf16* x, const fg_bf16* weight, fg_bf16* out, int T
                                        "fg_rmsnorm_wait");
   if (rc) return rc;
   if (T == 0) return FG_OK;
-  return fg::launch_k("fg_rmsnorm_wait", fg::disagg::rmsnorm_wait_kernel<256>, dim3(T), dim3(256), 0,
+  fg::disagg::GatherSpec gs;
+  memset(&gs, 0, sizeof(gs));
+  return fg::launch_k("fg_rmsnorm_wait", fg::disagg::rmsnorm_wait_kernel<256, false>, dim3(T), dim3(256), 0,
                       (cudaStream_t)stream, reinterpret_cast<const uint4*>(x),
                       reinterpret_cast<const uint4*>(weight), reinterpret_cast<uint4*>(out), H, eps,
-                      weight_mode, ws);
+                      weight_mode, ws, gs);
+}
+
+int fg_rmsnorm_gather_wait(const fg_bf16* const* srcs, int n_src, int rows_per_src, fg_bf16* gathered,
+                           const fg_bf16* weight, fg_bf16* out, int T, int H, float eps, int weight_mode,
+                           uint32_t* const* flags, int n_flags, int rows_per_flag, const uint32_t* epoch,
+                           uint32_t seq_mul, uint32_t seq_add, int timeout_ms, fg_stream_t stream) {
+  FG_REQUIRE(srcs && gathered && weight && out, "fg_rmsnorm_gather_wait: null pointer");
+  FG_REQUIRE(n_src >= 1 && n_src <= fg::disagg::kMaxFlags && rows_per_src > 0 &&
+                 (long long)n_src * rows_per_src >= T,
+             "fg_rmsnorm_gather_wait: %d sources of %d rows (1..%d sources) do not cover %d rows", n_src,
+             rows_per_src, fg::disagg::kMaxFlags, T);
+  FG_REQUIRE(T >= 0 && H > 0 && H % 8 == 0 && H <= 8192, "fg_rmsnorm_gather_wait: H=%d (multiple of 8, <= 8192)",
+             H);
+  FG_REQUIRE(weight_mode == FG_NORM_LLAMA || weight_mode == FG_NORM_FP32MUL,
+             "fg_rmsnorm_gather_wait: bad weight_mode");
+  FG_REQUIRE((((uintptr_t)gathered | (uintptr_t)weight | (uintptr_t)out) & 15) == 0,
+             "fg_rmsnorm_gather_wait: pointers must be 16-byte aligned");
+  FG_REQUIRE(n_flags == 0 || (rows_per_flag > 0 && (long long)rows_per_flag * n_flags >= T),
+             "fg_rmsnorm_gather_wait: %d flags of %d rows do not cover %d rows", n_flags, rows_per_flag, T);
+  fg::disagg::GatherSpec gs;
+  memset(&gs, 0, sizeof(gs));
+  for (int i = 0; i < n_src; ++i) {
+    FG_REQUIRE(srcs[i] != nullptr && ((uintptr_t)srcs[i] & 15) == 0,
+               "fg_rmsnorm_gather_wait: srcs[%d] is null or not 16-byte aligned", i);
+    gs.src[i] = reinterpret_cast<const uint4*>(srcs[i]);
+  }
+  gs.rows_per_src = rows_per_src;
+  gs.copy = reinterpret_cast<uint4*>(gathered);
+  fg::disagg::WaitSpec ws;
+  const int rc = fg::disagg::make_wait(ws, flags, n_flags, rows_per_flag, epoch, seq_mul, seq_add, timeout_ms,
+                                       "fg_rmsnorm_gather_wait");
+  if (rc) return rc;
+  if (T == 0) return FG_OK;
+  return fg::launch_k("fg_rmsnorm_gather_wait", fg::disagg::rmsnorm_wait_kernel<256, true>, dim3(T), dim3(256),
+                      0, (cudaStream_t)stream, static_cast<const uint4*>(nullptr),
+                      reinterpret_cast<const uint4*>(weight), reinterpret_cast<uint4*>(out), H, eps,
+                      weight_mode, ws, gs);
 }
 
 int fg_sum_rmsnorm_wait(const float* partials, int S, fg_bf16* h_out, const fg_bf16* weight, fg_bf16* x_out,

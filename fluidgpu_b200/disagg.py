@@ -59,15 +59,20 @@ FLAG_STRIDE = 128  # bytes between flags (one per cache line)
 
 @dataclass(frozen=True)
 class DisaggLayout:
-    """Global ranks of the two roles, micro-batches per attention rank and
-    sequences per micro-batch."""
+    """Global ranks of the two roles, micro-batches per attention rank,
+    sequences per micro-batch, and how the hidden state reaches the FFN ranks:
+    "pull" (the O-proj GEMM stores it in the attention GPU's own memory and
+    the FFN ranks' waiting RMSNorm reads it over NVLink) or "push" (the O-proj
+    GEMM's epilogue stores it into every FFN rank's memory)."""
 
     attn_ranks: tuple[int, ...]
     ffn_ranks: tuple[int, ...]
     micro_batches: int
     rows: int
+    handoff: str = "pull"
 
     def __post_init__(self) -> None:
+        assert self.handoff in ("pull", "push"), f"unknown hand-off {self.handoff!r}"
         assert self.attn_ranks and self.ffn_ranks, "need at least one attention and one FFN rank"
         assert not set(self.attn_ranks) & set(self.ffn_ranks), "a rank has one role"
         assert len(self.attn_ranks) <= 8 and len(self.ffn_ranks) <= 8, "at most 8 ranks per role"
@@ -92,11 +97,11 @@ class DisaggLayout:
         return "ffn", self.ffn_ranks.index(rank)
 
     @classmethod
-    def split(cls, world: int, micro_batches: int, rows: int) -> "DisaggLayout":
+    def split(cls, world: int, micro_batches: int, rows: int, handoff: str = "pull") -> "DisaggLayout":
         """First half of the ranks attention, second half FFN (one of each for 2)."""
         assert world >= 2 and world % 2 == 0, f"a split layout needs an even world, got {world}"
         h = world // 2
-        return cls(tuple(range(h)), tuple(range(h, world)), micro_batches, rows)
+        return cls(tuple(range(h)), tuple(range(h, world)), micro_batches, rows, handoff)
 
 
 class _Mailbox:
@@ -142,10 +147,20 @@ class _Rank:
         return (data + 255) // 256 * 256, lay.micro_batches * lay.A
 
     def attn_geometry(self) -> tuple[int, int]:
+        """Return buffers ret[m] (then, pulling, send buffers send[m]) and
+        one flag per (micro-batch, FFN rank)."""
+        lay, H = self.layout, self.spec.hidden
+        data = self.attn_send_offset()
+        if lay.handoff == "pull":
+            data += lay.micro_batches * lay.rows * H * 2
+        return (data + 255) // 256 * 256, lay.micro_batches * lay.S
+
+    def attn_send_offset(self) -> int:
+        """Byte offset of send[0] in an attention rank's mailbox (pull)."""
         lay, H = self.layout, self.spec.hidden
         elem = 4 if lay.S > 1 else 2
         data = lay.micro_batches * lay.S * lay.rows * H * elem
-        return (data + 255) // 256 * 256, lay.micro_batches * lay.S
+        return (data + 255) // 256 * 256
 
     def _hook(self, what: str, *args) -> None:
         if self.hooks is not None:
@@ -209,6 +224,13 @@ class AttentionRank(_Rank):
     def ret_flags(self, m: int) -> list[int]:
         return [_flag(self.mailbox.ptr, self.mailbox.data_bytes, m * self.layout.S + j)
                 for j in range(self.layout.S)]
+
+    def send_view(self, m: int) -> torch.Tensor:
+        """send[m], [b, H] bf16: micro-batch m's hidden state after the O-proj,
+        which the FFN ranks read (pull)."""
+        lay, H = self.layout, self.spec.hidden
+        off = self.attn_send_offset() + m * lay.rows * H * 2
+        return self.mailbox.buf[off:off + lay.rows * H * 2].view(torch.bfloat16).view(lay.rows, H)
 
     def ffn_in_rows(self, m: int) -> list[int]:
         """Address of this rank's row block of in[m] on every FFN rank."""
@@ -287,8 +309,13 @@ class AttentionRank(_Rank):
         b = lay.rows
         kernels.embed(mb["tok"], W.embed, out=mb["h"])
         kernels.rmsnorm(mb["h"], W.layers[0]["ln1"], s.eps, s.norm_mode, out=mb["x"])
-        dsts = ptr_array(self.ffn_in_rows(m)) if not standalone else None
-        sigs = ptr_array(self.ffn_in_flags(m)) if not standalone else None
+        pull = lay.handoff == "pull"
+        if standalone:
+            dsts = sigs = None
+        else:
+            dsts = ptr_array([self.send_view(m).data_ptr()] if pull else self.ffn_in_rows(m))
+            sigs = ptr_array(self.ffn_in_flags(m))
+        n_dst, row0 = (1, 0) if pull else (lay.S, self.index * b)
         for i in range(s.num_layers):
             stream = kernels._stream(self.device)
             L = W.layers[i]
@@ -312,7 +339,7 @@ class AttentionRank(_Rank):
                 wo = L["wo"]
                 call("fg_gemm_bf16_packed_routed", a.data_ptr(), wo.data.data_ptr(), h.data_ptr(),
                      None if L.get("bo") is None else L["bo"].data_ptr(), b, s.hidden, s.n_q * s.head_dim,
-                     _lib.FG_EPI_RESIDUAL, _lib.FG_ROUTE_BROADCAST, dsts, lay.S, b, self.index * b, sigs, lay.S,
+                     _lib.FG_EPI_RESIDUAL, _lib.FG_ROUTE_BROADCAST, dsts, n_dst, b, row0, sigs, lay.S,
                      mb["epoch"].data_ptr(), self.L, i + 1, mb["tickets"][i:i + 1].data_ptr(), stream)
                 self._hook("after_send", "in", m, i)
             yield
@@ -502,6 +529,12 @@ class FFNRank(_Rank):
         return [_flag(self.mailbox.ptr, self.mailbox.data_bytes, m * self.layout.A + a)
                 for a in range(self.layout.A)]
 
+    def attn_send_rows(self, m: int) -> list[int]:
+        """Address of send[m] on every attention rank (pull)."""
+        lay, H = self.layout, self.spec.hidden
+        off = self.attn_send_offset() + m * lay.rows * H * 2
+        return [self.peer_base[r] + off for r in lay.attn_ranks]
+
     def ret_rows(self, m: int) -> list[int]:
         """Address of this shard's plane of ret[m] on every attention rank."""
         lay, H = self.layout, self.spec.hidden
@@ -537,10 +570,15 @@ class FFNRank(_Rank):
             for m in range(lay.micro_batches):
                 self._hook("before_wait", "in", m, i)
                 inp = self.in_view(m)
-                call("fg_rmsnorm_wait", inp.data_ptr(), L["ln2"].data_ptr(), self.x.data_ptr(), T, s.hidden,
-                     float(s.eps), s.norm_mode, ptr_array(self.in_flags(m)), lay.A, lay.rows,
-                     self.epoch.data_ptr(), self.L, i + 1, self.timeout_ms, stream)
-                ev = kernels.KernelTimer.start("ffn")
+                if lay.handoff == "pull":  # read the attention ranks' send[m] over NVLink into in[m]
+                    call("fg_rmsnorm_gather_wait", ptr_array(self.attn_send_rows(m)), lay.A, lay.rows,
+                         inp.data_ptr(), L["ln2"].data_ptr(), self.x.data_ptr(), T, s.hidden, float(s.eps),
+                         s.norm_mode, ptr_array(self.in_flags(m)), lay.A, lay.rows, self.epoch.data_ptr(), self.L,
+                         i + 1, self.timeout_ms, stream)
+                else:
+                    call("fg_rmsnorm_wait", inp.data_ptr(), L["ln2"].data_ptr(), self.x.data_ptr(), T, s.hidden,
+                         float(s.eps), s.norm_mode, ptr_array(self.in_flags(m)), lay.A, lay.rows,
+                         self.epoch.data_ptr(), self.L, i + 1, self.timeout_ms, stream)
                 act = kernels.gemm(self.x, L["w_gate_up"], epilogue=_lib.FG_EPI_SWIGLU, out=self.act, slot=self.slot)
                 wd = L["w_down"]
                 res = inp if (lay.S == 1 or self.index == 0) else None
@@ -549,9 +587,52 @@ class FFNRank(_Rank):
                      None if res is None else res.data_ptr(), None, T, s.hidden, wd.K, epi, _lib.FG_ROUTE_SPLIT,
                      ptr_array(self.ret_rows(m)), lay.A, lay.rows, 0, ptr_array(self.ret_flags(m)), lay.A,
                      self.epoch.data_ptr(), self.L, i + 1, self.tickets[t:t + 1].data_ptr(), stream)
-                kernels.KernelTimer.stop("ffn", ev, T=T, H=s.hidden, I=wd.K)
                 self._hook("after_send", "ret", m, i)
         call("fg_counter_add", self.epoch.data_ptr(), 1, stream)
+
+    def time_standalone(self, reps: int = 3) -> float:
+        """Device milliseconds of this rank's own FFN work for one (layer,
+        micro-batch): RMSNorm, gate/up GEMM with SwiGLU, down GEMM, over every
+        layer and micro-batch with no waits and no hand-offs (the down GEMM
+        writes a local buffer), replayed from a CUDA graph. A timing reference
+        for the FFN GPUs' roofline, not a model computation; call it only
+        while no other rank waits on this one."""
+        s, lay, W = self.spec, self.layout, self.w
+        T = lay.A * lay.rows
+        epi = _lib.FG_EPI_RESIDUAL if lay.S == 1 else _lib.FG_EPI_F32
+        out = torch.empty(T, s.hidden, dtype=torch.bfloat16 if lay.S == 1 else torch.float32, device=self.device)
+        wd0 = W.layers[0]["w_down"]
+        kernels.Workspace.get(_lib.lib().fg_gemm_workspace_bytes(T, s.hidden, wd0.K, 0), self.device,
+                              self.slot + ".alone")
+
+        def body():
+            for i in range(s.num_layers):
+                L = W.layers[i]
+                for m in range(lay.micro_batches):
+                    inp = self.in_view(m)
+                    kernels.rmsnorm(inp, L["ln2"], s.eps, s.norm_mode, out=self.x)
+                    act = kernels.gemm(self.x, L["w_gate_up"], epilogue=_lib.FG_EPI_SWIGLU, out=self.act,
+                                       slot=self.slot)
+                    kernels.gemm(act, L["w_down"], epilogue=epi, residual=inp if epi == _lib.FG_EPI_RESIDUAL else None,
+                                 out=out, slot=self.slot + ".alone")
+
+        g = torch.cuda.CUDAGraph()
+        st = self.stream
+        st.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(st), torch.inference_mode():
+            with torch.cuda.graph(g, stream=st):
+                body()
+            g.replay()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                g.replay()
+            e1.record()
+        e1.synchronize()
+        torch.cuda.current_stream(self.device).wait_stream(st)
+        del g
+        return e0.elapsed_time(e1) / (reps * s.num_layers * lay.micro_batches)
 
     def capture(self) -> None:
         g = torch.cuda.CUDAGraph()

@@ -377,6 +377,17 @@ int fg_rmsnorm_wait(const fg_bf16* x, const fg_bf16* weight, fg_bf16* out, int T
                     int weight_mode, uint32_t* const* flags, int n_flags, int rows_per_flag,
                     const uint32_t* epoch, uint32_t seq_mul, uint32_t seq_add, int timeout_ms,
                     fg_stream_t stream);
+/* fg_rmsnorm_wait over rows that live on other GPUs: row r is row
+ * r % rows_per_src of srcs[r / rows_per_src] (peer buffers, read over NVLink
+ * once the row's flag has arrived), written to gathered[r] on this GPU as it
+ * is read, and out[r] = RMSNorm(row r). The FFN side of the disaggregated
+ * step in its pull form: the attention GPUs' O-proj stores stay in their own
+ * memory, and the FFN GPU moves the rows (replaces the reference's recv of
+ * the hidden state at the attention -> FFN boundary, executor.py:104-123). */
+int fg_rmsnorm_gather_wait(const fg_bf16* const* srcs, int n_src, int rows_per_src, fg_bf16* gathered,
+                           const fg_bf16* weight, fg_bf16* out, int T, int H, float eps, int weight_mode,
+                           uint32_t* const* flags, int n_flags, int rows_per_flag, const uint32_t* epoch,
+                           uint32_t seq_mul, uint32_t seq_add, int timeout_ms, fg_stream_t stream);
 /* After all n_flags flags: h_out[r] = bf16(partials[0][r] + ... +
  * partials[S-1][r]) (fp32 sums in shard order, as fg_sum_partials; partials
  * [S][T][H] fp32) and x_out[r] = fg_rmsnorm(h_out[r]): the reduce-by-consumer

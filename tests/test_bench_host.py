@@ -1,52 +1,80 @@
-"""bench.py host logic without a GPU: the nvidia-smi clock sampler that runs
-during the timed region (median SM clock, max clock, throttle reasons seen)."""
-import os
+"""bench.py host logic without a GPU: the NVML clock sampler that runs
+during the timed region (median SM clock, max clock, clock-event reasons
+seen), driven by a fake NVML module."""
+import sys
 import time
+import types
 
 import bench
 
-ROW = "0, {sm}, 1965, 700.5, 0x4, Not Active, Not Active, {thermal}, Active"
+SW_POWER_CAP, SW_THERMAL = 0x4, 0x20
 
 
-def _fake_smi(tmp_path, rows):
-    fake = tmp_path / "nvidia-smi"
-    lines = "".join(f"echo '{r}'; " for r in rows)
-    fake.write_text(f"#!/bin/sh\nwhile true; do {lines}sleep 0.05; done\n")
-    fake.chmod(0o755)
-    return fake
+def _fake_nvml(monkeypatch, samples, fail=False):
+    """A stand-in pynvml whose SM clock and reasons cycle through `samples`."""
+    nv = types.ModuleType("pynvml")
+    nv.NVML_CLOCK_SM = 1
+    state = {"i": 0}
+
+    def init():
+        if fail:
+            raise RuntimeError("no NVML here")
+
+    def clock(h, which):
+        sm, _ = samples[state["i"] % len(samples)]
+        return sm
+
+    def reasons(h):
+        _, bits = samples[state["i"] % len(samples)]
+        state["i"] += 1
+        return bits
+
+    nv.nvmlInit = init
+    nv.nvmlDeviceGetHandleByUUID = lambda u: "h"
+    nv.nvmlDeviceGetHandleByIndex = lambda i: "h"
+    nv.nvmlDeviceGetMaxClockInfo = lambda h, which: 1965
+    nv.nvmlDeviceGetClockInfo = clock
+    nv.nvmlDeviceGetPowerUsage = lambda h: 700500
+    nv.nvmlDeviceGetCurrentClocksEventReasons = reasons
+    monkeypatch.setitem(sys.modules, "pynvml", nv)
 
 
-def test_clock_sampler_reports_median_and_reasons(tmp_path, monkeypatch):
-    _fake_smi(tmp_path, [ROW.format(sm=1965, thermal="Not Active"), ROW.format(sm=1800, thermal="Not Active")])
-    monkeypatch.setenv("PATH", f"{tmp_path}{os.pathsep}{os.environ['PATH']}")
+def test_clock_sampler_reports_median_and_reasons(monkeypatch):
+    _fake_nvml(monkeypatch, [(1965, SW_POWER_CAP), (1800, SW_POWER_CAP)])
     s = bench.ClockSampler(0)
     s.start()
-    time.sleep(0.5)
+    time.sleep(0.2)
     r = s.stop()
-    assert r["samples"] >= 2
+    assert r["samples"] >= 2  # one at each end at least, however short the region
     assert r["sm_max_mhz"] == 1965.0
     assert 1800.0 <= r["sm_mhz"] <= 1965.0
+    assert r["power_w"] == 700.5
     assert r["reasons"] == ["sw_power_cap"]  # power cap is kept and noted
-    assert s.out is None and not s.path.exists()
 
 
-def test_clock_sampler_flags_thermal_slowdown(tmp_path, monkeypatch):
-    _fake_smi(tmp_path, [ROW.format(sm=1500, thermal="Active")])
-    monkeypatch.setenv("PATH", f"{tmp_path}{os.pathsep}{os.environ['PATH']}")
+def test_clock_sampler_short_region_still_samples(monkeypatch):
+    _fake_nvml(monkeypatch, [(1965, 0)])
     s = bench.ClockSampler(0)
     s.start()
-    time.sleep(0.3)
+    r = s.stop()
+    assert r["samples"] >= 2 and r["sm_mhz"] == 1965.0 and r["reasons"] == []
+
+
+def test_clock_sampler_flags_thermal_slowdown(monkeypatch):
+    _fake_nvml(monkeypatch, [(1500, SW_POWER_CAP | SW_THERMAL)])
+    s = bench.ClockSampler(0)
+    s.start()
+    time.sleep(0.05)
     r = s.stop()
     assert r["reasons"] == ["sw_power_cap", "sw_thermal_slowdown"]
 
 
-def test_clock_sampler_without_nvidia_smi(tmp_path, monkeypatch):
-    monkeypatch.setenv("PATH", str(tmp_path))  # an empty directory: no nvidia-smi
+def test_clock_sampler_without_nvml(monkeypatch):
+    _fake_nvml(monkeypatch, [(1965, 0)], fail=True)
     s = bench.ClockSampler(0)
     s.start()
     r = s.stop()
-    assert r["reasons"] == ["nvidia-smi unavailable"] and r["sm_mhz"] is None
-    assert s.out is None and not s.path.exists()
+    assert r["reasons"] == ["NVML unavailable: RuntimeError"] and r["sm_mhz"] is None
 
 
 def test_prompt_lengths_fixed_and_uniform():

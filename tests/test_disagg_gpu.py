@@ -20,8 +20,10 @@ flag values and epochs are those of the multi-GPU runs.
     clears twice that bound.
   Both at a narrow model and at a wide one whose O-proj and down GEMMs split
   every tile over a cluster of CTAs (the plans of the full-size model), and
-  under both attention-side schedules: micro-batches on streams of their own,
-  and micro-batches alternating layer by layer on one stream.
+  under both attention-side schedules (micro-batches on streams of their own,
+  and micro-batches alternating layer by layer on one stream) and both
+  hand-off forms (the FFN ranks pulling the O-proj rows from the attention
+  ranks' memory, or the O-proj pushing them into the FFN ranks' memory).
 Two GPUs (skipped on one): ranks as processes, every rank replaying its CUDA
 graphs concurrently (both schedules), greedy tokens equal the co-located
 engines'."""
@@ -115,10 +117,12 @@ def _colocated(model, prompts):
     return eng
 
 
-@pytest.mark.parametrize("A,S,wide,schedule", [(1, 1, False, "streams"), (2, 2, False, "streams"),
-                                                (1, 1, True, "streams"), (2, 2, True, "streams"),
-                                                (1, 1, False, "interleaved"), (2, 2, True, "interleaved")])
-def test_fused_disagg_one_gpu(A, S, wide, schedule):
+@pytest.mark.parametrize("A,S,wide,schedule,handoff", [
+    (1, 1, False, "streams", "pull"), (2, 2, False, "streams", "pull"),
+    (1, 1, True, "streams", "pull"), (2, 2, True, "streams", "pull"),
+    (1, 1, False, "interleaved", "pull"), (2, 2, True, "interleaved", "pull"),
+    (1, 1, False, "interleaved", "push"), (2, 2, True, "interleaved", "push")])
+def test_fused_disagg_one_gpu(A, S, wide, schedule, handoff):
     from fluidgpu_b200 import _lib, build, kernels
     from fluidgpu_b200.disagg import AttentionRank, DisaggLayout, Fabric, FFNRank
     from fluidgpu_b200.model import ModelWeights
@@ -131,7 +135,7 @@ def test_fused_disagg_one_gpu(A, S, wide, schedule):
         assert lib.fg_gemm_split(3 * A, c.hidden_size, c.intermediate_size // S, 0) > 1  # down
         assert lib.fg_gemm_split(3, c.hidden_size, c.hidden_size, 0) > 1  # O-proj
     M, b, steps = 2, 3, 12
-    lay = DisaggLayout(tuple(range(A)), tuple(range(A, A + S)), M, b)
+    lay = DisaggLayout(tuple(range(A)), tuple(range(A, A + S)), M, b, handoff)
     dev = torch.device("cuda", 0)
     attn = [AttentionRank(lay, a, ModelWeights.from_hf(model, dev), 64, device=dev, timeout_ms=5000,
                           schedule=schedule) for a in range(A)]
@@ -216,7 +220,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, port, q, schedule):
+def _worker(rank, port, q, schedule, handoff):
     try:
         import torch.distributed as dist
 
@@ -232,7 +236,7 @@ def _worker(rank, port, q, schedule):
         build.build()
         model = _model()
         M, b, steps = 2, 4, 10
-        lay = DisaggLayout((0,), (1,), M, b)
+        lay = DisaggLayout((0,), (1,), M, b, handoff)
         w = ModelWeights.from_hf(model, dev)
         r = (AttentionRank(lay, 0, w, 64, device=dev, schedule=schedule) if rank == 0
              else FFNRank(lay, 1, w, device=dev))
@@ -263,8 +267,8 @@ def _worker(rank, port, q, schedule):
         q.put((rank, False, None, traceback.format_exc()))
 
 
-@pytest.mark.parametrize("schedule", ["interleaved", "streams"])
-def test_fused_disagg_two_gpus_graphs(schedule):
+@pytest.mark.parametrize("schedule,handoff", [("interleaved", "pull"), ("streams", "pull"), ("interleaved", "push")])
+def test_fused_disagg_two_gpus_graphs(schedule, handoff):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -272,7 +276,7 @@ def test_fused_disagg_two_gpus_graphs(schedule):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, q, schedule)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, port, q, schedule, handoff)) for r in range(2)]
     for p in procs:
         p.start()
     results = sorted((q.get(timeout=300) for _ in procs), key=lambda x: x[0])

@@ -18,6 +18,9 @@ def test_split_layout_roles():
         DisaggLayout((0, 1), (1, 2), 2, 8)  # a rank with two roles
     with pytest.raises(AssertionError):
         lay.role(9)
+    assert lay.handoff == "pull" and DisaggLayout.split(2, 1, 8, "push").handoff == "push"
+    with pytest.raises(AssertionError):
+        DisaggLayout.split(2, 1, 8, "mail")
 
 
 def test_nvlink_bytes_per_step():

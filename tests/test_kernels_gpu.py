@@ -452,9 +452,10 @@ def test_routed_gemm_matches_plain_and_signals(T, N, K, epi, route):
 
 
 def test_waiting_norms_match_rmsnorm():
-    """fg_rmsnorm_wait / fg_sum_rmsnorm_wait with their flags already at the
-    awaited value: the results of fg_rmsnorm (and of fg_sum_partials then
-    fg_rmsnorm) bit for bit."""
+    """fg_rmsnorm_wait / fg_sum_rmsnorm_wait / fg_rmsnorm_gather_wait with
+    their flags already at the awaited value: the results of fg_rmsnorm (and
+    of fg_sum_partials then fg_rmsnorm) bit for bit, and the gathered rows
+    equal to their sources."""
     from fluidgpu_b200 import _lib, kernels
     from fluidgpu_b200._lib import call, ptr_array
 
@@ -479,6 +480,15 @@ def test_waiting_norms_match_rmsnorm():
         hs = kernels.sum_partials(parts)
         assert torch.equal(h, hs)
         assert torch.equal(xo, kernels.rmsnorm(hs, w, 1e-5, mode))
+        # gathering form: the rows of x live in four separate buffers of 16
+        # rows (stand-ins for four attention GPUs' send buffers)
+        srcs = [x[16 * i:16 * (i + 1)].clone() for i in range(4)]
+        gathered = torch.full_like(x, float("nan"))
+        out2 = torch.empty_like(x)
+        call("fg_rmsnorm_gather_wait", ptr_array([t.data_ptr() for t in srcs]), 4, 16, gathered.data_ptr(),
+             w.data_ptr(), out2.data_ptr(), T, H, 1e-5, mode, fptr, 4, 16, epoch.data_ptr(), 10, 4, 1000, stream)
+        assert torch.equal(gathered, x)
+        assert torch.equal(out2, out)
     kernels.check_device("waiting norms")
 
 
