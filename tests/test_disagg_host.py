@@ -32,3 +32,25 @@ def test_nvlink_bytes_per_step():
     four = DisaggLayout.split(8, 2, 32)
     per_layer_mb = 4 * 4 * 32 * H * 2 + 4 * 4 * 32 * H * 4
     assert nvlink_bytes_per_step(four, H, L) == per_layer_mb * 2 * L
+
+
+def test_mailbox_geometry_pull_and_push():
+    """Attention mailboxes: return buffers (bf16 with one FFN rank, fp32
+    partials otherwise), then, pulling, one send buffer per micro-batch; FFN
+    mailboxes: the merged rows of every micro-batch. Flags follow the data."""
+    from types import SimpleNamespace
+
+    from fluidgpu_b200.disagg import _Rank
+
+    H = 4096
+    for world, handoff in ((2, "pull"), (8, "pull"), (8, "push")):
+        lay = DisaggLayout.split(world, 2, 32, handoff)
+        r = _Rank.__new__(_Rank)
+        r.layout, r.spec = lay, SimpleNamespace(hidden=H)
+        ret = 2 * lay.S * 32 * H * (4 if lay.S > 1 else 2)
+        assert r.attn_send_offset() == ret
+        data, nflag = r.attn_geometry()
+        assert data == ret + (2 * 32 * H * 2 if handoff == "pull" else 0) and nflag == 2 * lay.S
+        assert data % 256 == 0
+        fdata, fflag = r.ffn_geometry()
+        assert fdata == 2 * lay.A * 32 * H * 2 and fflag == 2 * lay.A
