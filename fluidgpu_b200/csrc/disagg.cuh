@@ -336,6 +336,11 @@ int fg_preload(void) {
     }
   }
   free(fns);
+  int (*active)[9] = nullptr;  // the GEMM plans' resident-cluster counts too
+  if (rc == FG_OK && !fg::gemm::active_clusters_table(active)) {
+    fg::set_last_error("fg_preload: cannot query resident clusters for the GEMM plans");
+    rc = FG_ERR_CUDA;
+  }
   return rc;
 }
 

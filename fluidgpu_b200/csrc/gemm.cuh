@@ -17,7 +17,9 @@
 //  - tiles >= half the resident CTA slots (gate_up, lm_head): one CTA per
 //    tile; with packed weights this streams at 90-99% of the HBM peak.
 //  - fewer tiles (qkv, o_proj, down): a thread-block cluster of S <= 8 CTAs
-//    per tile, CTA r owning K slice r. The fp32 partial tiles are reduced
+//    per tile, CTA r owning K slice r; S is the largest that keeps all the
+//    tiles' clusters resident in one wave (for one CTA per SM the device's
+//    own count of resident clusters per size, cudaOccupancyMaxActiveClusters). The fp32 partial tiles are reduced
 //    through distributed shared memory: every CTA parks its accumulator in
 //    its own shared memory, and after a cluster barrier CTA r sums rows
 //    [r*128/S, (r+1)*128/S) across the S CTAs and runs the epilogue for them.
@@ -40,6 +42,7 @@
 //   warps 2-5     : epilogue. tcgen05.ld (32x32b) of their TMEM lane quarter;
 //                   bias / residual / SwiGLU; bf16 stores, token-major.
 #pragma once
+#include <mutex>
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -790,6 +793,8 @@ inline int pick_bn(int T) {
   return 256;
 }
 
+constexpr int kMinSliceSteps = 4;  // fewest K steps (64 columns each) a split slice gets
+
 struct Plan {
   int bn, n_tiles, t_tiles, nkb, grid, max_contrib, split;
   bool streamk;
@@ -797,6 +802,68 @@ struct Plan {
 };
 
 inline int ctas_per_sm(int bn) { return bn >= 256 ? 1 : 2; }
+
+// Clusters of s CTAs (1 x s x 1) of the cluster kernel for BN tokens that the
+// current device keeps resident at once (cudaOccupancyMaxActiveClusters: it
+// counts shared memory, TMEM-free occupancy and how clusters pack into the
+// GPCs, which a CTA count alone does not); -1 if it cannot be asked.
+template <int BN, int STAGES>
+int query_active_clusters(int s) {
+  using L = Layout<BN, STAGES>;
+  auto kern = gemm_cluster_kernel<BN, STAGES, true>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN_SMEM) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, s, 1);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::DYN_SMEM;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 1;
+  attr.val.clusterDim.y = s;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -1;
+  }
+  return n;
+}
+
+// Resident clusters for every (BN, split) of the decode plans on the current
+// device, asked once per device; false without a device (the plan then falls
+// back to counting CTAs).
+inline bool active_clusters_table(int (*&table)[9]) {
+  static std::mutex mu;
+  static int cache[64][5][9];
+  static bool done[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done[dev & 63]) {
+    for (int sp = 1; sp <= 8; ++sp) {
+      cache[dev & 63][0][sp] = query_active_clusters<16, 6>(sp);
+      cache[dev & 63][1][sp] = query_active_clusters<32, 5>(sp);
+      cache[dev & 63][2][sp] = query_active_clusters<64, 4>(sp);
+      cache[dev & 63][3][sp] = query_active_clusters<128, 3>(sp);
+      cache[dev & 63][4][sp] = query_active_clusters<256, 4>(sp);
+      for (int b = 0; b < 5; ++b)
+        if (cache[dev & 63][b][sp] < 1) return false;  // not known: ask again next time
+    }
+    done[dev & 63] = true;
+  }
+  table = cache[dev & 63];
+  return true;
+}
+
+inline int bn_index(int bn) { return bn <= 16 ? 0 : bn <= 32 ? 1 : bn <= 64 ? 2 : bn <= 128 ? 3 : 4; }
 
 // splits == 0: automatic (cluster kernel); > 0: cluster kernel with that many
 // K slices per tile (capped at 8 and at K/64); < 0: persistent stream-K over
@@ -832,13 +899,25 @@ inline Plan make_plan(int T, int N, int K, int splits) {
     pl.grid = (int)(-splits < pl.units ? -splits : pl.units);
   } else if (splits > 0) {
     pl.split = splits;
-  } else if (2 * tiles > slots) {
-    pl.split = 1;  // enough tiles to fill the resident slots: one CTA per tile
   } else {
-    // fill the slots, but keep >= 16 K steps (256 KB of weights) per CTA so
-    // the stream, not the pipeline ramp, sets the time
-    pl.split = (int)(slots / tiles);
-    if (pl.split > pl.nkb / 16) pl.split = pl.nkb / 16;
+    // as many K slices per tile (at least kMinSliceSteps K steps each) as
+    // keep every tile's cluster resident in one wave: more CTAs stream the
+    // weights at once, and a second wave of clusters costs more than the
+    // slices save (measured on B200 over every split of the decode shapes of
+    // Llama-3-8B and gpt-oss-20b, T = 32-256). One CTA per SM (BN >= 128):
+    // the device's own count of resident clusters per size. Two per SM: about
+    // 82% of the CTA slots, where clusters still packed into the GPCs in one
+    // wave (5 x 48 = 240 CTAs did, 6 x 48 = 288 did not).
+    const int max_split = pl.nkb / kMinSliceSteps < 8 ? pl.nkb / kMinSliceSteps : 8;
+    int (*table)[9] = nullptr;
+    if (pl.bn >= 128 && active_clusters_table(table)) {
+      const int* active = table[bn_index(pl.bn)];
+      for (int sp = 1; sp <= max_split; ++sp)
+        if (tiles <= active[sp]) pl.split = sp;
+    } else {
+      const long long fit = (slots * 41) / (50 * tiles);
+      pl.split = (int)(fit < max_split ? fit : max_split);
+    }
   }
   if (!pl.streamk) {
     if (pl.split > 8) pl.split = 8;
@@ -1005,6 +1084,8 @@ int fg_pack_weight_bf16(const fg_bf16* w, void* packed, int N, int K, fg_stream_
              "fg_pack_weight_bf16: pointers must be 16-byte aligned");
   const int nkb = (K + fg::gemm::BK - 1) / fg::gemm::BK;
   const long long chunks = (long long)fg_packed_weight_bytes(N, K) / 16;
+  int (*active)[9] = nullptr;  // ask the device for the GEMM plans now, before any stream capture
+  (void)fg::gemm::active_clusters_table(active);
   const int threads = 256;
   return fg::launch_k("fg_pack_weight_bf16", fg::gemm::pack_weight_kernel,
                       dim3((unsigned)((chunks + threads - 1) / threads)), dim3(threads), 0,

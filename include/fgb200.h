@@ -404,7 +404,8 @@ int fg_counter_add(uint32_t* counter, uint32_t delta, fg_stream_t stream);
  * waiting for another GPU whose progress needs a launch this host has not
  * made yet, the two GPUs stall each other. Ranks that wait on one another
  * (the disaggregated step, P2PComm) call this once per device before their
- * first step. */
+ * first step. It also asks the device how many GEMM clusters of each size it
+ * keeps resident (the decode GEMM plans use it; fg_pack_weight_bf16 asks too). */
 int fg_preload(void);
 
 /* positions[b] += 1 and seq_lens[b] += 1 after a decode step
