@@ -542,6 +542,15 @@ def gptoss_step(dev: torch.device, ctx: int, W: int, K: int) -> dict:
     return out
 
 
+def disagg_workload(A: int, S: int, batch: int, ctx: int, mix: str) -> str:
+    """The workload a disaggregated bench line measures, with the BASELINE
+    config it is quoted on (configs[1]: 1 + 1 GPUs; configs[3]: 4 + 4)."""
+    prompts = f"prompts uniform in [128, {ctx}]" if mix == "uniform" else f"prompt {ctx}"
+    which = {(1, 1): " (BASELINE configs[1])", (4, 4): " (BASELINE configs[3])"}.get((A, S), "")
+    return (f"llama-3-8b disaggregated decode step, {A} attention + {S} FFN GPUs, batch {A * batch} "
+            f"({batch} per attention GPU), {prompts}, paged KV block 16{which}")
+
+
 def run_disagg_fused(args) -> None:
     """The disaggregated decode step of fluidgpu_b200.disagg on N GPUs: N/2
     attention GPUs with `batch` sequences each in M micro-batches, N/2 FFN
@@ -719,7 +728,8 @@ def run_disagg_fused(args) -> None:
             "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {**CONFIG, "batch_per_gpu": B, "attention_gpus": lay.A, "ffn_gpus": lay.S,
+            "config": {**CONFIG, "workload": disagg_workload(lay.A, lay.S, B, ctx, args.prompt_mix),
+                       "batch_per_gpu": B, "attention_gpus": lay.A, "ffn_gpus": lay.S,
                        "micro_batches": M, "sequences_per_micro_batch": b, "schedule": args.schedule,
                        "handoff": args.handoff,
                        "parallelism": (f"disaggregated: attention dp{lay.A} / FFN tp{lay.S}, {M} ping-pong micro-"
@@ -743,8 +753,12 @@ def run_disagg_fused(args) -> None:
             "handoff": {"nvlink_bytes_per_step": nv, "nvlink_us_per_step_at_770GBs": nv / 770e9 * 1e6,
                         "attention_alone_ms_per_step": alone,
                         "exposed_frac": max(0.0, 1.0 - alone / step_ms),
+                        "handoff_frac": max(0.0, 1.0 - alone / step_ms),
+                        "handoff_kernels": 0,
                         "note": "exposed_frac = 1 - (attention GPU's own kernels, FFN left out) / step: what the "
-                                "hand-offs and the remote FFN add to the attention GPUs' step"},
+                                "hand-offs and the remote FFN add to the attention GPUs' step; there are no "
+                                "hand-off kernels (the producing GEMM stores and signals, the consuming "
+                                "RMSNorm waits), so handoff_frac is that same exposed share"},
             "gpu_launches": launches_all * K,
             "cuda_graph": True,
             "clocks": clocks,
@@ -907,14 +921,17 @@ def main() -> None:
     ap.add_argument("--micro-batches", type=int, default=2,
                     help="ping-pong micro-batches per attention GPU (disagg, pipeline, tp, ep)")
     ap.add_argument("--verbose", action="store_true", help="phase trace on stderr (disagg)")
-    ap.add_argument("--prompt-mix", default="fixed", choices=["fixed", "uniform"],
-                    help="prompt lengths: all --context (default), or seeded uniform in [128, --context] "
-                         "per sequence (config 4's request mix)")
+    ap.add_argument("--prompt-mix", default=None, choices=["fixed", "uniform"],
+                    help="prompt lengths: all --context, or seeded uniform in [128, --context] per sequence "
+                         "(config 4's request mix; the default for the disaggregated step on 8 GPUs, fixed "
+                         "otherwise)")
     args = ap.parse_args()
     assert args.warmup >= 0 and args.steps > 0
     world = dist_env()[0]
     mode = args.mode if args.mode != "auto" else ("disagg" if world > 1 else "replicas")
     args.mode = mode
+    if args.prompt_mix is None:
+        args.prompt_mix = "uniform" if (mode == "disagg" and world == 8 and args.impl != "reference") else "fixed"
     if args.impl == "reference":
         run_reference(args)
     elif mode == "disagg":

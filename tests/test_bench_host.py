@@ -85,3 +85,11 @@ def test_prompt_lengths_fixed_and_uniform():
     assert a != bench.prompt_lengths(256, 4096, "uniform", seed=1)  # per rank
     assert 1500 < sum(a) / len(a) < 2700  # mean of U[128, 4096] is 2112
     assert bench.prompt_lengths(3, 100, "uniform") == [100] * 3  # contexts below 128
+
+
+def test_disagg_workload_names_the_baseline_config():
+    w2 = bench.disagg_workload(1, 1, 64, 4096, "fixed")
+    assert "1 attention + 1 FFN" in w2 and "batch 64" in w2 and w2.endswith("(BASELINE configs[1])")
+    w8 = bench.disagg_workload(4, 4, 64, 4096, "uniform")
+    assert "batch 256" in w8 and "uniform in [128, 4096]" in w8 and w8.endswith("(BASELINE configs[3])")
+    assert "BASELINE" not in bench.disagg_workload(2, 2, 64, 4096, "fixed")  # no config has 2 + 2
