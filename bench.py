@@ -24,9 +24,13 @@ Under torchrun (N > 1) the default is the disaggregated step
 each (2 ping-pong micro-batches of 32), the other N/2 hold the FFN
 tensor-parallel over the intermediate dimension (one GPU at N = 2), every
 FFN GPU merging all attention GPUs' rows of a micro-batch into one GEMM per
-layer; hidden states cross NVLink as stores from the producing GEMM's
-epilogue (weak scaling in the attention GPUs). --mode replicas runs N
-independent co-located engines instead.
+layer. Attention -> FFN: the O-proj GEMM keeps its rows in the attention
+GPU's memory and signals, the FFN GPUs' RMSNorm reads them over NVLink;
+FFN -> attention: the down GEMM's epilogue stores into the attention GPUs'
+memory and signals (weak scaling in the attention GPUs). On 8 GPUs the
+prompts follow config 4's mix (uniform in [128, 4096]) unless --prompt-mix
+says otherwise. --mode replicas runs N independent co-located engines
+instead.
 """
 from __future__ import annotations
 
