@@ -88,7 +88,11 @@ def _time(fn, iters: int, warmup: int) -> float:
 
 
 def bench_attn(B: int, ctx: int, nq: int = 32, nkv: int = 8, hd: int = 128, window: int = 0,
-               iters: int = 20, warmup: int = 5, seed: int = 1) -> dict:
+               iters: int = 20, warmup: int = 5, seed: int = 1, plan_len: int = 0) -> dict:
+    """plan_len > 0: the length the split plan is made for (at most ctx; the
+    plan's slice count is capped by plan_len / 128 pages, so a sweep over
+    plan_len visits the smaller slice counts), else ctx."""
+    plan = plan_len if 0 < plan_len <= ctx else ctx
     g = torch.Generator(device="cuda").manual_seed(seed)
     pages = (ctx + 15) // 16
     num_blocks = B * pages
@@ -99,7 +103,7 @@ def bench_attn(B: int, ctx: int, nq: int = 32, nkv: int = 8, hd: int = 128, wind
     q = torch.empty((B, nq, hd), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
     lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
     out = torch.empty((B, nq * hd), dtype=torch.bfloat16, device="cuda")
-    fn = lambda: kernels.paged_decode_attn(q, kc, vc, table, lens, ctx, window=window, out=out)  # noqa: E731
+    fn = lambda: kernels.paged_decode_attn(q, kc, vc, table, lens, plan, window=window, out=out)  # noqa: E731
     ms = _time(fn, iters, warmup)
     eff = min(ctx, window) if window else ctx
     nbytes = 2.0 * B * nkv * hd * 2 * eff + 2.0 * B * nq * hd * 2
@@ -107,7 +111,8 @@ def bench_attn(B: int, ctx: int, nq: int = 32, nkv: int = 8, hd: int = 128, wind
     gbs = nbytes / (ms * 1e-3) / 1e9
     kernels.check_device("attn microbench")
     return {"kernel": "fg_paged_decode_attn", "B": B, "context": ctx, "nq": nq, "nkv": nkv, "hd": hd,
-            "window": window, "ms": ms, "bytes": nbytes, "GBps": gbs, "frac_hbm": gbs / peak,
+            "window": window, "splits": _lib.lib().fg_attn_splits(B, nkv, hd, plan, window),
+            "ms": ms, "bytes": nbytes, "GBps": gbs, "frac_hbm": gbs / peak,
             "peak": f"{src} {peak} GB/s", "timing": "graph" if GRAPH else "eager"}
 
 
@@ -373,6 +378,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--window", type=int, default=0)
+    ap.add_argument("--plan-len", type=int, default=0,
+                    help="attn: length the split plan is made for (caps the slice count; default --context)")
     ap.add_argument("--nq", type=int, default=32)
     ap.add_argument("--nkv", type=int, default=8)
     ap.add_argument("--hd", type=int, default=128)
@@ -394,7 +401,8 @@ def main() -> None:
         return
     torch.cuda.set_device(0)
     if a.what == "attn":
-        print(json.dumps(bench_attn(a.batch, a.context, a.nq, a.nkv, a.hd, a.window, a.iters, a.warmup)))
+        print(json.dumps(bench_attn(a.batch, a.context, a.nq, a.nkv, a.hd, a.window, a.iters, a.warmup,
+                                    plan_len=a.plan_len)))
     elif a.what == "gemm":
         print(json.dumps(bench_gemm(a.T, a.N, a.K, a.epilogue, a.iters, a.warmup, splits=a.splits,
                                     packed=not a.rowmajor)))
