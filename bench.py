@@ -296,9 +296,19 @@ def run_reference(args) -> None:
     threads = host_threads()
     torch.set_num_threads(threads)
     ctx = args.context
+    config = CONFIG
+    if world > 1 and args.mode == "disagg":
+        # the workload the other arm measures at this N; with config 4's prompt
+        # mix the sample runs at its mean prompt length
+        config = {**CONFIG, "workload": disagg_workload(world // 2, world // 2, args.batch or 64, ctx,
+                                                        args.prompt_mix)}
+        if args.prompt_mix == "uniform":
+            lens = prompt_lengths(256, ctx, "uniform", seed=0)
+            ctx = int(round(sum(lens) / len(lens)))
+            config["reference_sample_context"] = ctx
     common = {"impl": "reference", "metric": METRIC, "unit": "tokens/s", "n_gpus": args.gpus,
               "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-              "vs_baseline": None, "data": "synthetic", "config": CONFIG}
+              "vs_baseline": None, "data": "synthetic", "config": config}
     if (REF_DIR / "fluidgpu_torch").is_dir():
         t0 = time.perf_counter()
         ref = ReferenceRunner(ctx)
@@ -935,7 +945,7 @@ def main() -> None:
     mode = args.mode if args.mode != "auto" else ("disagg" if world > 1 else "replicas")
     args.mode = mode
     if args.prompt_mix is None:
-        args.prompt_mix = "uniform" if (mode == "disagg" and world == 8 and args.impl != "reference") else "fixed"
+        args.prompt_mix = "uniform" if (mode == "disagg" and world == 8) else "fixed"
     if args.impl == "reference":
         run_reference(args)
     elif mode == "disagg":
