@@ -278,6 +278,58 @@ __device__ __forceinline__ uint16_t dbl_to_bf16(double v) {
   return (uint16_t)(sign | ((uint32_t)biased << 7) | (kept & 0x7f));
 }
 
+// The same logit through an fp64 sum with a rigorous error bound, when that
+// settles it. A product of two bf16 values is exact in fp64 (8-bit
+// significands; every bf16 value, subnormals included, is an fp64 normal),
+// and any summation order of n exact terms in fp64 lands within
+// gamma_(n-1) * sum|p_i| of the exact sum (u = 2^-53, gamma_k = k u/(1 - k u);
+// all terms are multiples of 2^-266, far above fp64's subnormals, so the
+// standard model holds). E = (n 2^-52) * (fp64 sum of |p_i|) is at least that
+// bound with margin for the rounding of |p_i|'s own sum, and lo / hi = s -/+ 2E
+// computed in fp64 still enclose the exact sum. Rounding to nearest even is
+// monotone, so if lo and hi round to the same finite nonzero bf16, every real
+// between them does too and that is the exact logit. Otherwise (a rounding
+// midpoint within the bound, a result that rounds to zero or overflows, a
+// non-finite input) returns false and warp_exact_dot decides. Every lane
+// returns the same answer (lane 0's sums are broadcast).
+__device__ bool warp_filtered_dot(const uint4* __restrict__ xr, const uint4* __restrict__ wr, int n8,
+                                  const __nv_bfloat16* bias, int lane, uint16_t& out) {
+  double s = 0.0, a = 0.0;
+  for (int i = lane; i < n8; i += 32) {
+    const uint4 xa = xr[i], wb = wr[i];
+    const uint32_t* pa = reinterpret_cast<const uint32_t*>(&xa);
+    const uint32_t* pb = reinterpret_cast<const uint32_t*>(&wb);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 fa = unpack_bf16x2(pa[q]), fb = unpack_bf16x2(pb[q]);
+      const double p0 = __dmul_rn((double)fa.x, (double)fb.x);
+      const double p1 = __dmul_rn((double)fa.y, (double)fb.y);
+      s = __dadd_rn(__dadd_rn(s, p0), p1);
+      a = __dadd_rn(__dadd_rn(a, fabs(p0)), fabs(p1));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    a = __dadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+  }
+  s = __shfl_sync(0xffffffffu, s, 0);
+  a = __shfl_sync(0xffffffffu, a, 0);
+  if (bias) {
+    const double b = (double)__bfloat162float(*bias);
+    s = __dadd_rn(s, b);
+    a = __dadd_rn(a, fabs(b));
+  }
+  if (!isfinite(s) || !isfinite(a)) return false;
+  const double n = 8.0 * n8 + 1.0;  // terms, the bias included
+  const double e2 = 2.0 * __dmul_rn(a, n * 0x1p-52);
+  const uint16_t r_lo = dbl_to_bf16(__dsub_rn(s, e2));
+  const uint16_t r_hi = dbl_to_bf16(__dadd_rn(s, e2));
+  if (r_lo != r_hi || (r_lo & 0x7fffu) == 0 || (r_lo & 0x7f80u) == 0x7f80u) return false;
+  out = r_lo;
+  return true;
+}
+
 }  // namespace exact
 
 // Top-k of the E <= 64 logits a warp holds (lane e has experts e and e+32),
@@ -325,8 +377,9 @@ __device__ __forceinline__ void warp_topk_softmax(float v0, float v1, int lane, 
 }
 
 // One CTA of 32 warps per token: the x row's exponent statistics first (all
-// warps), then warp w computes the exactly rounded logits of experts w, w+32,
-// and warp 0 selects the top-k.
+// warps), then warp w computes the exactly rounded logits of experts w, w+32
+// (an fp64 sum with an error bound where that settles the rounding, the
+// exact accumulation otherwise), and warp 0 selects the top-k.
 __global__ void __launch_bounds__(1024) router_topk_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
     const __nv_bfloat16* __restrict__ bias, int H, int E, int k, __nv_bfloat16* __restrict__ out_w,
@@ -358,8 +411,9 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(
   }
   for (int e = warp; e < E; e += 32) {
     const uint4* wr = reinterpret_cast<const uint4*>(w + (int64_t)e * H);
-    const uint16_t b = exact::warp_exact_dot(xr, wr, H8, bias ? bias + e : nullptr, xhi, xlo,
-                                             digits[warp], lane);
+    uint16_t b;
+    if (!exact::warp_filtered_dot(xr, wr, H8, bias ? bias + e : nullptr, lane, b))
+      b = exact::warp_exact_dot(xr, wr, H8, bias ? bias + e : nullptr, xhi, xlo, digits[warp], lane);
     if (lane == 0) {
       logit[e] = bf2f(__ushort_as_bfloat16(b));
       if (out_logits) out_logits[(int64_t)t * E + e] = __ushort_as_bfloat16(b);
